@@ -1,0 +1,436 @@
+"""Benchmark: batched TT-KV decode step on Llama-3.2-3B-shaped layers.
+
+One STEP = for each of the 28 layers: encode the step's new token of every request into its slot
+(frozen projection + residual/V select-pack, `ttkv_write_paged`) and read every request's whole
+store (`ttkv_decode_paged`: reconstruct, patch, rotate, score, online softmax, V readout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). `value` = decoded tokens/s of the whole job (requests x ranks /
+step time, device-timed, max over ranks). Inputs are synthetic (seeded; shapes of config 1) and
+the stores are encoded by this repository's own encoder (device TT-SVD fit per request and
+layer, then the CUDA writer). The per-step working set (~0.9 GB of slots) exceeds L2, so no flush
+is needed between steps.
+
+Multi-GPU (torchrun): KV heads are sharded across ranks for the read (rank g reads heads
+[g*H/N, (g+1)*H/N) of every request from its replica of the cache) and the per-layer head outputs
+are all-gathered over NCCL; the write is replicated (each rank encodes the step's tokens into its
+own replica). Total work is fixed as N grows ("strong").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "ttkv-vllm_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs peak"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in pathlib.Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------- workload
+def synth_kv_device(gen, H, n, d=128, rank=96, dtype=None):
+    """Device version of vllm_ttkv.synthetic.synth_kv's distribution (seeded torch generator)."""
+    import torch
+    dev = gen.device
+    Z = torch.randn(H, n, rank, generator=gen, device=dev)
+    B = torch.randn(H, rank, d, generator=gen, device=dev) / rank ** 0.5
+    idx = torch.stack([torch.randperm(d, generator=gen, device=dev)[:4] for _ in range(H)])
+    scale = torch.ones(H, 1, d, device=dev)
+    scale.scatter_(2, idx.unsqueeze(1), 8.0)
+    K = torch.bmm(Z, B * scale) + 0.02 * torch.randn(H, n, d, generator=gen, device=dev)
+    V = torch.randn(H, n, d, generator=gen, device=dev)
+    if dtype is not None:
+        K, V = K.to(dtype), V.to(dtype)
+    return K, V
+
+
+class Workload:
+    """Config-1 stores on one device: per layer a paged cache, a decoder pool and pinv pool."""
+
+    def __init__(self, B, n, r1s, cfg, device, dtype, seed=0, block_size=16, HQ=24, H=8):
+        import numpy as np
+        import torch
+
+        from vllm_ttkv import encode, synthetic
+        from vllm_ttkv.layout import layout_for_config
+        self.B, self.n, self.HQ, self.H, self.bs = B, n, HQ, H, block_size
+        self.r1s = list(r1s)
+        self.L = len(self.r1s)
+        self.device, self.dtype = device, dtype
+        seq = n + 1                                            # the stored rows incl. this step's
+        bt_np, n_blocks = synthetic.block_table(seed, [seq] * B, block_size)
+        self.block_table = torch.from_numpy(bt_np).to(device)
+        self.seq_lens = torch.full((B,), seq, dtype=torch.int32, device=device)
+        self.max_seq = seq
+        self.n_slots = n_blocks * block_size
+        slots_all = torch.from_numpy(
+            (bt_np[:, :, None].astype(np.int64) * block_size + np.arange(block_size)
+             ).reshape(B, -1)[:, :seq]).to(device)
+        self.new_slots = slots_all[:, n].contiguous()             # [B] slot of the step's token
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.layouts, self.caches, self.decoders, self.pinvT = [], [], [], []
+        self.k_new, self.v_new, self.q, self.out = [], [], [], []
+        self.fit_s = 0.0
+        self.dec_index = torch.arange(B, dtype=torch.int32, device=device)
+        for l, r1 in enumerate(self.r1s):
+            lay = layout_for_config(cfg, r1, H=H)
+            cache = torch.zeros(self.n_slots, lay.compressed_bytes_per_token(), dtype=torch.uint8,
+                                device=device)
+            dec = torch.zeros(B, r1, H * 128, device=device)
+            pinvT = torch.zeros(B, r1, H * 128, device=device)
+            kn = torch.empty(B, H, 128, dtype=dtype, device=device)
+            vn = torch.empty(B, H, 128, dtype=dtype, device=device)
+            for r in range(B):
+                K, V = synth_kv_device(gen, H, seq, dtype=dtype)
+                t0 = time.perf_counter()
+                fk = encode.fit_into_budget(K[:, :n], lay, cfg)
+                encode.write_fitted(cache, slots_all[r, :n].contiguous(), fk,
+                                    K[:, :n].permute(1, 0, 2).contiguous(),
+                                    V[:, :n].permute(1, 0, 2).contiguous(), lay)
+                dec[r] = fk.decoder.decoder_f
+                pinvT[r] = fk.decoder.pinvT
+                torch.cuda.synchronize(device)
+                self.fit_s += time.perf_counter() - t0
+                kn[r] = K[:, n].to(dtype)
+                vn[r] = V[:, n].to(dtype)
+            self.layouts.append(lay)
+            self.caches.append(cache)
+            self.decoders.append(dec)
+            self.pinvT.append(pinvT)
+            self.k_new.append(kn)
+            self.v_new.append(vn)
+            self.q.append(torch.randn(B, HQ, 128, generator=gen, device=device).to(dtype))
+            self.out.append(torch.empty(B, HQ, 128, dtype=dtype, device=device))
+        self.table = torch.from_numpy(synthetic.cos_sin_cache(seq + 16, dtype="float32")).to(device).to(dtype)
+        self.scale = 128 ** -0.5
+
+    def slot_bytes(self, l):
+        return self.B * self.max_seq * self.layouts[l].compressed_bytes_per_token()
+
+    def read_bytes(self, l, n_heads=8):
+        """Algorithmic bytes of one decode launch: the slots' coefficient blocks and the read
+        heads' K/V rows, the decoders (fp32, the heads read), the queries and outputs."""
+        lay = self.layouts[l]
+        per_tok = lay.coeff_bytes + 2 + n_heads * (lay.k_row_bytes + lay.v_row_bytes)
+        if n_heads == self.H:
+            per_tok = lay.compressed_bytes_per_token()
+        dec = self.B * lay.r1 * n_heads * 128 * 4
+        io = 2 * self.B * (self.HQ * n_heads // self.H) * 128 * 2
+        return self.B * self.max_seq * per_tok + dec + io
+
+    def step(self, head_lo=0, head_hi=8, gather=None):
+        from vllm_ttkv import encode, ops
+        for l in range(self.L):
+            lay = self.layouts[l]
+            encode.write_frozen(self.caches[l], self.new_slots, self.k_new[l], self.v_new[l],
+                                self.dec_index, self.decoders[l], self.pinvT[l], lay)
+            ops.decode_paged(lay, self.caches[l], self.bs, self.block_table, self.seq_lens,
+                             self.decoders[l], self.dec_index, self.table, self.q[l], self.scale,
+                             self.out[l], self.max_seq, head_lo, head_hi)
+            if gather is not None:
+                gather(l)
+
+
+# ---------------------------------------------------------------------------- CPU baseline
+def cpu_sample(wl_params, sample_layers=(0, 9, 18, 27), reps=1, seed=0):
+    """Time the oracle (the reference's torch CPU path restated in numpy) on a bounded sample of
+    (request, layer) pairs of the same workload, built on the CPU by the oracle's own fit:
+    a decode read over n+1 rows plus the write of one token. Returns seconds per (request, layer)
+    averaged over the sample."""
+    import numpy as np
+
+    from oracle import ttkv_oracle as O
+    from vllm_ttkv import synthetic as S
+    B, n, r1s, cfg = wl_params
+    per = []
+    for i, l in enumerate(sample_layers):
+        g = O.geometry_for_config(cfg, r1s[l])
+        K, V = S.synth_kv(seed + i, n + 1)
+        f = O.fit_into_budget(K[:, :n], g, cfg)
+        blobs = O.build_slots(g, f["coeff_q"], f["coeff_scale"], f["R"], V[:, :n])
+        pinv = np.linalg.pinv(f["decoder_f"]).astype(np.float32)
+        table = S.cos_sin_cache(n + 16, dtype="bfloat16")
+        q = S.synth_queries(seed + i, (24, 128), "bfloat16")
+        cos, sin = O.cos_sin_from_table(table, np.arange(n + 1), 128)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            cq, cs, R = O.encode_frozen(K[:, n:n + 1], f["decoder_f"], pinv)
+            blob = O.build_slots(g, cq, cs, R, V[:, n:n + 1])
+            allb = np.concatenate([blobs, blob])
+            O.attend(g, allb[:, :g.k_slot_bytes], allb[:, g.k_slot_bytes:], f["decoder_f"], q, cos, sin)
+        per.append((time.perf_counter() - t0) / reps)
+    return sum(per) / len(per)
+
+
+def run_reference(args):
+    """The reference arm: the reference's CPU path (the oracle port) on a bounded sample."""
+    from vllm_ttkv import synthetic as S
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count()
+    B, n = args.batch, args.ctx
+    r1s = S.LLAMA32_3B_R1
+    times = []
+    for _ in range(args.warmup):
+        cpu_sample((B, n, r1s, "safe"), sample_layers=(9,))
+    for k in range(args.steps):
+        per = cpu_sample((B, n, r1s, "safe"), sample_layers=(9,), seed=k)
+        times.append(per * B * len(r1s))
+    step_s = statistics.median(times)
+    v = B / step_s
+    line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"cfg1 decode step: B={B} x {n} ctx, 28 layers, safe", "batch": B,
+                       "ctx": n, "layers": len(r1s)},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"1 (request, layer) pair per step at n={n}, r1={r1s[9]}, "
+                                       f"scaled x{B * len(r1s)} to a full step"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--ctx", type=int, default=4322)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--cfg", default="safe")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from vllm_ttkv import synthetic as S
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    H = 8
+    if H % world:
+        raise SystemExit(f"{world} ranks do not divide the {H} KV heads")
+    head_lo, head_hi = rank * H // world, (rank + 1) * H // world
+
+    r1s = (S.LLAMA32_3B_R1 * ((args.layers + 27) // 28))[:args.layers]
+    t0 = time.perf_counter()
+    wl = Workload(args.batch, args.ctx, r1s, args.cfg, device, torch.bfloat16, seed=0)
+    setup_s = time.perf_counter() - t0
+
+    gather = None
+    if world > 1:
+        G = wl.HQ // H
+        nh = head_hi - head_lo
+        shard = [torch.empty(wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
+        full = [torch.empty(world, wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
+
+        def gather(l):
+            shard[l].copy_(wl.out[l][:, head_lo * G:head_hi * G])
+            dist.all_gather_into_tensor(full[l], shard[l])
+
+    def run_steps(k):
+        for _ in range(k):
+            wl.step(head_lo, head_hi, gather)
+
+    run_steps(args.warmup)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index if world == 1 else local) as clk:
+        ev0.record()
+        run_steps(args.steps)
+        ev1.record()
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    clocks = clk.summary()
+
+    # ---- the decode launch alone, per layer, CUDA events on the launching stream
+    from vllm_ttkv import ops
+    n_heads = head_hi - head_lo
+    reps = 3
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(wl.L * reps)]
+    torch.cuda.synchronize(device)
+    for rep in range(reps):
+        for l in range(wl.L):
+            a, b = evs[rep * wl.L + l]
+            a.record()
+            ops.decode_paged(wl.layouts[l], wl.caches[l], wl.bs, wl.block_table, wl.seq_lens,
+                             wl.decoders[l], wl.dec_index, wl.table, wl.q[l], wl.scale, wl.out[l],
+                             wl.max_seq, head_lo, head_hi)
+            b.record()
+    torch.cuda.synchronize(device)
+    dec_ms = [a.elapsed_time(b) for a, b in evs]
+    dec_total_ms = sum(dec_ms) / reps                          # all layers' decode launches, per step
+    alg_bytes = sum(wl.read_bytes(l, n_heads) for l in range(wl.L))
+    achieved = alg_bytes / (dec_total_ms * 1e-3) / 1e9
+    hbm, tc, peak_kind = _peaks()
+
+    # ---- e2e: the same step through the C-ABI with host buffers copied in and out every step
+    pin_q = [x.cpu().pin_memory() for x in wl.q]
+    pin_k = [x.cpu().pin_memory() for x in wl.k_new]
+    pin_v = [x.cpu().pin_memory() for x in wl.v_new]
+    pin_o = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in wl.out]
+    h2d = sum(x.numel() * x.element_size() for x in pin_q + pin_k + pin_v)
+    d2h = sum(x.numel() * x.element_size() for x in pin_o)
+
+    def e2e_step():
+        for l in range(wl.L):
+            wl.q[l].copy_(pin_q[l], non_blocking=True)
+            wl.k_new[l].copy_(pin_k[l], non_blocking=True)
+            wl.v_new[l].copy_(pin_v[l], non_blocking=True)
+        wl.step(head_lo, head_hi, gather)
+        for l in range(wl.L):
+            pin_o[l].copy_(wl.out[l], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        per = cpu_sample((args.batch, args.ctx, r1s, args.cfg), sample_layers=(9,))
+        cpu_step = per * args.batch * len(r1s)
+        cpu = {"value": args.batch / cpu_step, "unit": "tok/s", "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": f"1 (request, layer) pair (layer 9, r1={r1s[9]}, n={args.ctx}): oracle "
+                         f"frozen write of one token + decode read, scaled x{args.batch * len(r1s)}"}
+
+    launches = wl.L * 2 + wl.L * 2                                # write (project+pack) + read (split+merge)
+    if rank == 0:
+        line = {"metric": METRIC, "value": args.batch / (ms * 1e-3), "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16 model tensors, fp32 math, u8 slots", "data": "synthetic",
+                "config": {"workload": f"cfg1 decode step: B={args.batch} x {args.ctx} ctx, "
+                                       f"{len(r1s)} Llama-3.2-3B layers (calibrated r1), {args.cfg}, "
+                                       f"block 16",
+                           "batch": args.batch, "ctx": args.ctx, "layers": len(r1s),
+                           "kv_heads_per_rank": n_heads,
+                           "l2": "inputs larger than L2 (slots %.0f MB/step)" % (
+                               sum(wl.slot_bytes(l) for l in range(wl.L)) / 1e6),
+                           "parallelism": f"kv-head shard x{world}" if world > 1 else "single"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                             "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
+                             "kernel": "attn_split_kernel + merge_kernel (ttkv_decode_paged)",
+                             "decode_ms_per_step": dec_total_ms},
+                "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "gpu_launches": launches * args.steps, "clocks": clocks,
+                "setup_s": round(setup_s, 1), "fit_s": round(wl.fit_s, 1)}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,190 @@
+"""Parity of the CUDA read path (decode + continuation) with the oracle, through the C ABI.
+
+Stores are encoded on the CPU by the oracle (`oracle/stores.py`), so these tests check the read
+kernels independently of the write kernels. Tolerance: 2e-3 max-abs on attention outputs (the
+fp16-store bound of the reference's `north_star`), 1e-2 for the 4-bit ("campaign4x") store.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import stores
+from oracle import ttkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL_FP16_STORE = 2e-3
+ATOL_4BIT_STORE = 1e-2
+
+
+def _dev(st, q=None):
+    dev = "cuda"
+    from vllm_ttkv import layout as L
+    g = st["g"]
+    lay = L.TTKLayout(H=g.H, d=g.d, r1=g.r1, qbits=g.qbits, res_k=g.res_k, res_bits=g.res_bits,
+                      v_lanes=g.v_lanes, v_bits=g.v_bits)
+    tdt = {"float16": torch.float16, "bfloat16": torch.bfloat16}[st["dtype"]]
+    return dict(
+        lay=lay,
+        cache=torch.from_numpy(st["cache"]).to(dev),
+        bt=torch.from_numpy(st["block_table"]).to(dev),
+        seq=torch.from_numpy(st["seq_lens"]).to(dev),
+        dec=torch.from_numpy(st["decoders"]).to(dev),
+        idx=torch.arange(len(st["seq_lens"]), dtype=torch.int32, device=dev),
+        table=torch.from_numpy(st["table"]).to(dev).to(tdt),
+        q=torch.from_numpy(st["q"] if q is None else q).to(dev).to(tdt),
+        tdt=tdt)
+
+
+def _decode(st, out_dtype=torch.float32, head_lo=0, head_hi=None, q=None, scale=None):
+    from vllm_ttkv import ops
+    d = _dev(st, q)
+    B, HQ, _ = d["q"].shape
+    out = torch.zeros(B, HQ, 128, dtype=out_dtype, device="cuda")
+    ops.reset_status()
+    ops.decode_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"], d["idx"],
+                     d["table"], d["q"], 128 ** -0.5 if scale is None else scale, out,
+                     int(st["seq_lens"].max()), head_lo, head_hi)
+    ops.check_status()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("cfg,atol", [("safe", ATOL_FP16_STORE), ("tight", ATOL_FP16_STORE),
+                                      ("campaign4x", ATOL_4BIT_STORE)])
+def test_decode_matches_oracle_ragged_batch(cfg, atol):
+    st = stores.make_store(1, [70, 33, 129, 1, 16], cfg=cfg, r1=32)
+    got = _decode(st)
+    want = stores.expected_decode(st)
+    err = np.abs(got - want).max()
+    assert err < atol, err
+    assert err < 1e-4, f"fp32 reconstruction drifted: {err}"
+
+
+@pytest.mark.parametrize("HQ", [8, 32, 56])
+def test_decode_gqa_groups(HQ):
+    st = stores.make_store(2, [45, 100], cfg="safe", r1=24, HQ=HQ)
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_decode_fp16_and_bf16_outputs_and_tables():
+    st = stores.make_store(3, [80, 17], cfg="safe", r1=40, dtype="bfloat16")
+    want = stores.expected_decode(st)
+    for odt in (torch.float16, torch.bfloat16):
+        got = _decode(st, out_dtype=odt)
+        assert np.abs(got - want).max() < ATOL_FP16_STORE
+
+
+def test_decode_rank_sweep_including_multiples_of_16():
+    """The reference's Triton kernel crashed on r1 multiples of 16 (krt_triton.py:35-43)."""
+    for r1 in (16, 33, 61, 64, 110, 143):
+        st = stores.make_store(4, [150, 31], cfg="safe", r1=r1)
+        assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4, r1
+
+
+def test_decode_head_shard_writes_only_its_heads():
+    st = stores.make_store(5, [64, 40], cfg="safe", r1=32)
+    want = stores.expected_decode(st)
+    got = _decode(st, head_lo=2, head_hi=5)
+    G = 3
+    np.testing.assert_allclose(got[:, 2 * G:5 * G], want[:, 2 * G:5 * G], atol=1e-4)
+    assert np.all(got[:, :2 * G] == 0) and np.all(got[:, 5 * G:] == 0)
+
+
+def test_decode_long_context_split_merge():
+    st = stores.make_store(6, [2100], cfg="safe", r1=48)
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_rotation_is_per_row_negative_control():
+    """Reading with the angle table shifted by one position must change the scores a lot --
+    the failure this path is shaped around is a silent mis-rotation (reference.py:1-30)."""
+    st = stores.make_store(7, [90], cfg="safe", r1=32)
+    good = _decode(st)
+    shifted = dict(st)
+    shifted["table"] = np.concatenate([st["table"][1:], st["table"][-1:]])
+    bad = _decode(shifted)
+    assert np.abs(good - bad).max() > 1e-2
+
+
+def test_decode_over_reference_golden_store():
+    """The reference's own encoded store and its own attend_raw_store output."""
+    from conftest import GOLDEN
+    s = dict(np.load(GOLDEN / "store_safe_recip.npz"))
+    g = O.geometry_for_config("safe", int(s["fit_coeff_q"].shape[1]))
+    blobs = np.concatenate([np.concatenate([s["k_slots"], s["v_slots"]], 1),
+                            np.concatenate([s["fz_k_slots"], s["fz_v_slots"]], 1)])
+    n = blobs.shape[0]
+    bs = 16
+    bt = np.arange((n + bs - 1) // bs, dtype=np.int32)[::-1].copy()[None]
+    cache = np.zeros((bt.size * bs, g.blob_bytes), np.uint8)
+    cache[O.block_slots(bt[0], n, bs)] = blobs
+    dec = np.zeros((1, g.r1, 1024), np.float32)
+    d0 = s["fit_dec_q"].astype(np.float32) * s["fit_dec_scale"].view(np.float16).astype(np.float32)[:, None]
+    dec[0, :d0.shape[0]] = d0
+    st = dict(g=g, cache=cache, block_table=bt, seq_lens=np.array([n], np.int32), decoders=dec,
+              table=s["table"].astype(np.float32), q=s["q"].astype(np.float32)[None],
+              block_size=bs, dtype="float16")
+    got = _decode(st)[0]
+    assert np.abs(got - s["attend"]).max() < 1e-4
+
+
+def test_continuation_matches_oracle_causal():
+    from vllm_ttkv import ops
+    st = stores.make_store(8, [70, 40, 129], cfg="safe", r1=32)
+    q_lens = [6, 1, 37]
+    rng = np.random.default_rng(0)
+    qs = [rng.standard_normal((24, ql, 128)).astype(np.float16).astype(np.float32) for ql in q_lens]
+    d = _dev(st)
+    flat = np.concatenate([q.transpose(1, 0, 2) for q in qs])            # [N, HQ, d]
+    qt = torch.from_numpy(flat).cuda().to(torch.float16)
+    start = np.concatenate([[0], np.cumsum(q_lens)[:-1]]).astype(np.int32)
+    out = torch.zeros(qt.shape, dtype=torch.float32, device="cuda")
+    ops.reset_status()
+    ops.prefill_cont_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"],
+                           d["idx"], d["table"], torch.from_numpy(start).cuda(),
+                           torch.tensor(q_lens, dtype=torch.int32, device="cuda"), qt,
+                           128 ** -0.5, out, max(q_lens), int(st["seq_lens"].max()))
+    ops.check_status()
+    got = out.cpu().numpy()
+    for r, ql in enumerate(q_lens):
+        want = stores.expected_continuation(st, r, qs[r])                # [HQ, Q, d]
+        err = np.abs(got[start[r]:start[r] + ql].transpose(1, 0, 2) - want).max()
+        assert err < 1e-4, (r, err)
+
+
+def test_continuation_with_one_query_equals_decode():
+    from vllm_ttkv import ops
+    st = stores.make_store(9, [77, 12], cfg="safe", r1=32)
+    d = _dev(st)
+    dec = _decode(st)
+    out = torch.zeros(2, 24, 128, device="cuda")
+    ops.prefill_cont_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"],
+                           d["idx"], d["table"], torch.tensor([0, 1], dtype=torch.int32, device="cuda"),
+                           torch.ones(2, dtype=torch.int32, device="cuda"), d["q"], 128 ** -0.5, out,
+                           1, 77)
+    np.testing.assert_allclose(out.cpu().numpy(), dec, atol=1e-6)
+
+
+def test_block_outside_the_cache_is_refused_on_device():
+    from vllm_ttkv import ops
+    st = stores.make_store(10, [40], cfg="safe", r1=32)
+    bad = dict(st)
+    bad["block_table"] = st["block_table"].copy()
+    bad["block_table"][0, 1] = 10_000                                     # past the cache
+    with pytest.raises(IndexError):
+        _decode(bad)
+    ops.reset_status()
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4   # context still usable
+
+
+def test_decoder_index_outside_pool_is_refused_on_device():
+    from vllm_ttkv import ops
+    st = stores.make_store(11, [20], cfg="safe", r1=32)
+    d = _dev(st)
+    out = torch.zeros(1, 24, 128, device="cuda")
+    ops.reset_status()
+    ops.decode_paged(d["lay"], d["cache"], 16, d["bt"], d["seq"], d["dec"],
+                     torch.tensor([5], dtype=torch.int32, device="cuda"), d["table"], d["q"],
+                     0.1, out, 20)
+    with pytest.raises(RuntimeError, match="decoder"):
+        ops.check_status()

@@ -1,0 +1,606 @@
+// The TT-KV read: decode and chunked-prefill continuation over a paged, packed cache.
+//
+// One launch covers every request of a layer. A CTA owns (request, KV head, query block, token
+// split); it stages its head's slice of the request's decoder in shared memory once and then
+// walks 32-token tiles of the request's rows through the block table:
+//
+//   gather     the tile's slot ids from the block table, the coefficient block, this head's K
+//              residual row and V row, and the RoPE rows of the tokens' positions
+//   rebuild    K_pre = (cq * cs) @ decoder[:, head]        fp32 FMA (the reference's ieee dot)
+//   patch      K_pre += residual lanes (bitmap + MSB-first codes + fp16 ruler)
+//   rotate     y = RoPE(K_pre, the row's own position), (j, j + d/2) pairing
+//   score      s = scale * q . y for the G query heads (x query block), causal mask
+//   softmax    online (running max and sum per query row)
+//   readout    o += p * V lanes decoded from the slot
+//
+// and writes (o, max, sum) per split; a merge kernel combines the splits into the output.
+// This is vllm_ttkv/impl.py:511-540 (_decode_one) + krt_triton.py:66-151 (_krt_kernel) +
+// softmax + v_out_triton.py:51-118 (_v_out_kernel) for the decode, and impl.py:725-778 with
+// krt_triton.py:155-266 / v_out_triton.py:159-246 for the continuation, fused and batched.
+#include <cfloat>
+#include <cmath>
+
+#include "ttkv_common.cuh"
+
+namespace ttkv {
+namespace {
+
+constexpr int TT = 32;    // tokens per tile
+constexpr int NT = 128;   // threads per CTA
+constexpr int RS = 132;   // row stride (floats) of the rotated-key tile
+
+struct ReadParams {
+    int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset, k_pb, v_pb;
+    const uint8_t* cache;
+    int64_t n_slots, row_bytes;
+    int block_size;
+    const int32_t* block_table;
+    int64_t bt_stride;
+    int bt_cols;
+    const int32_t* seq_lens;
+    const float* decoders;
+    int64_t dec_stride;
+    const int32_t* dec_index;
+    int n_decoders;
+    const void* table;
+    int table_dtype;
+    int64_t table_rows;
+    const void* q;
+    int q_dtype;
+    int64_t q_stride;
+    int HQ, G;
+    const int32_t* q_start;   // null for decode
+    const int32_t* q_len;
+    float scale;
+    int head_lo, n_heads;     // KV heads [head_lo, head_lo + n_heads)
+    int qmax, n_qblk, n_splits, chunk;
+    float* part_o;            // [req][head][qmax*G][split][128]
+    float* part_ml;           // [req][head][qmax*G][split][2]
+    void* out;
+    int out_dtype;
+    int64_t out_stride;
+    int32_t* status;
+};
+
+struct Smem {
+    float* dec;       // [r1][128]
+    float* q;         // [QR][128]
+    float* coef;      // [r1][TT]
+    float* y;         // [TT][RS]
+    float* p;         // [QR][TT]
+    float* cosv;      // [TT][64]
+    float* sinv;      // [TT][64]
+    float* cs;        // [TT]
+    float* krs;       // [TT]
+    float* vrs;       // [TT]
+    float* m;         // [QR]
+    float* l;         // [QR]
+    float* corr;      // [QR]
+    uint32_t* kw;     // [TT][4]
+    uint32_t* kpre;   // [TT][4]
+    uint32_t* vw;     // [TT][4]
+    uint32_t* vpre;   // [TT][4]
+    int64_t* slot;    // [TT]
+    uint8_t* krow;    // [TT][kpad]
+    uint8_t* vrow;    // [TT][vpad]
+    int kpad, vpad;
+};
+
+__host__ __device__ inline int pad4(int n) { return (n + 3) & ~3; }
+
+__host__ __device__ inline size_t smem_bytes(int r1, int QR, int k_row, int v_row) {
+    size_t f = size_t(r1) * 128 + size_t(QR) * 128 + size_t(r1) * TT + size_t(TT) * RS +
+               size_t(QR) * TT + 2 * TT * 64 + 3 * TT + 3 * QR;
+    size_t b = f * 4 + 4 * TT * 4 * 4 + 8 + TT * 8 + size_t(TT) * (pad4(k_row + 1) + pad4(v_row + 1));
+    return (b + 15) & ~size_t(15);
+}
+
+__device__ inline Smem carve(unsigned char* base, int r1, int QR, int k_row, int v_row) {
+    Smem s;
+    float* f = reinterpret_cast<float*>(base);
+    s.dec = f;  f += r1 * 128;
+    s.q = f;    f += QR * 128;
+    s.coef = f; f += r1 * TT;
+    s.y = f;    f += TT * RS;
+    s.p = f;    f += QR * TT;
+    s.cosv = f; f += TT * 64;
+    s.sinv = f; f += TT * 64;
+    s.cs = f;   f += TT;
+    s.krs = f;  f += TT;
+    s.vrs = f;  f += TT;
+    s.m = f;    f += QR;
+    s.l = f;    f += QR;
+    s.corr = f; f += QR;
+    uint32_t* u = reinterpret_cast<uint32_t*>(f);
+    s.kw = u;   u += TT * 4;
+    s.kpre = u; u += TT * 4;
+    s.vw = u;   u += TT * 4;
+    s.vpre = u; u += TT * 4;
+    // int64 slots need 8-byte alignment: every block above is a multiple of 4 floats except
+    // the QR-sized ones, so round up here
+    uintptr_t a = (reinterpret_cast<uintptr_t>(u) + 7) & ~uintptr_t(7);
+    s.slot = reinterpret_cast<int64_t*>(a);
+    unsigned char* b = reinterpret_cast<unsigned char*>(s.slot + TT);
+    s.kpad = pad4(k_row + 1);
+    s.vpad = pad4(v_row + 1);
+    s.krow = b; b += TT * s.kpad;
+    s.vrow = b;
+    return s;
+}
+
+// Value of lane j in a staged packed row whose 4 bitmap words and their exclusive prefix
+// popcounts are precomputed. A well-formed row has exactly `kmax` bits set; a malformed one
+// (more bits) reads lanes past the kmax-th as zero instead of reading past the staged row.
+__device__ __forceinline__ float staged_lane(const uint32_t* w, const uint32_t* pre,
+                                             const uint8_t* stream, float ruler, int bits, int kmax,
+                                             int j) {
+    const int wi = j >> 5, l = j & 31;
+    const uint32_t word = w[wi];
+    if (!((word >> (31 - l)) & 1u)) return 0.f;
+    const int rank = int(pre[wi]) + __popc(word & ~(0xffffffffu >> l));
+    if (rank >= kmax) return 0.f;
+    return float(code_at(stream, rank, bits) - (1 << (bits - 1))) * ruler;
+}
+
+template <int QR>
+__device__ __forceinline__ void write_partial(const ReadParams& P, int r, int hl, int qrow0,
+                                              int split, const float (&o)[QR], const Smem& S,
+                                              int nrows) {
+    const int tid = threadIdx.x;
+    const int QG = P.qmax * P.G;
+    #pragma unroll
+    for (int i = 0; i < QR; ++i) {
+        if (i < nrows) {
+            const int64_t row = (int64_t(r) * P.n_heads + hl) * QG + qrow0 + i;
+            P.part_o[(row * P.n_splits + split) * 128 + tid] = o[i];
+            if (tid == 0) {
+                P.part_ml[(row * P.n_splits + split) * 2 + 0] = S.m[i];
+                P.part_ml[(row * P.n_splits + split) * 2 + 1] = S.l[i];
+            }
+        }
+    }
+}
+
+// QB query tokens x G heads = QR query rows per CTA. MULTI: continuation (causal, q_start/q_len).
+template <int G, int QB, bool MULTI>
+__global__ void __launch_bounds__(NT) attn_split_kernel(const ReadParams P) {
+    constexpr int QR = G * QB;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int tid = threadIdx.x;
+    const int split = blockIdx.x;
+    const int hl = blockIdx.y / P.n_qblk, qb = blockIdx.y % P.n_qblk;
+    const int h = P.head_lo + hl;
+    const int r = blockIdx.z;
+    Smem S = carve(smem_raw, P.r1, QR, P.k_row, P.v_row);
+
+    const int seq = P.seq_lens[r];
+    const int qlen = MULTI ? P.q_len[r] : 1;
+    const int qrow_first = MULTI ? P.q_start[r] : r;
+    const int j0 = qb * QB;                               // first query of this block
+    const int nq = min(QB, qlen - j0);                    // queries in this block
+    const int nrows = max(nq, 0) * G;
+    const int p0 = seq - qlen;                            // position of query 0
+
+    float o[QR];
+    #pragma unroll
+    for (int i = 0; i < QR; ++i) o[i] = 0.f;
+    if (tid < QR) { S.m[tid] = -INFINITY; S.l[tid] = 0.f; }
+
+    // ---- validation: a refusal is recorded and the CTA contributes nothing
+    const int di = P.dec_index[r];
+    bool bad = false;
+    if (nq <= 0) bad = true;                              // an empty query block: nothing to do
+    if (!bad && (MULTI && (qlen > seq || qlen < 0))) { report(P.status, TTKV_STATUS_QUERY); bad = true; }
+    if (!bad && (di < 0 || di >= P.n_decoders)) { report(P.status, TTKV_STATUS_DECODER); bad = true; }
+    const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
+    if (!bad && blocks_needed > P.bt_cols) { report(P.status, TTKV_STATUS_ROW_SHORT); bad = true; }
+    int t_begin = split * P.chunk;
+    int t_end = min(seq, t_begin + P.chunk);
+    if (MULTI) t_end = min(t_end, p0 + j0 + nq);          // rows past the block's last query
+    if (!bad && t_begin < t_end) {
+        const int64_t n_blocks = P.n_slots / P.block_size;
+        const int32_t* row = P.block_table + int64_t(r) * P.bt_stride;
+        int local_bad = 0;
+        for (int b = t_begin / P.block_size + tid; b <= (t_end - 1) / P.block_size; b += NT) {
+            const int32_t blk = row[b];
+            if (blk < 0 || blk >= n_blocks) local_bad = 1;
+        }
+        if (__syncthreads_or(local_bad)) {
+            if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
+            bad = true;
+        }
+    }
+    __syncthreads();
+    if (bad || t_begin >= t_end) {
+        write_partial<QR>(P, r, hl, j0 * G, split, o, S, nrows);
+        return;
+    }
+
+    // ---- stage this head's decoder slice and the query rows
+    const float* dec = P.decoders + int64_t(di) * P.dec_stride;
+    for (int i = tid; i < P.r1 * 32; i += NT) {
+        const int rr = i >> 5, c4 = i & 31;
+        reinterpret_cast<float4*>(S.dec)[i] =
+            reinterpret_cast<const float4*>(dec + int64_t(rr) * P.H * 128 + h * 128)[c4];
+    }
+    for (int i = tid; i < QR * 128; i += NT) {
+        const int qr = i >> 7, lane = i & 127;
+        const int jq = j0 + qr / G, g = qr % G;
+        float v = 0.f;
+        if (jq < qlen) {
+            const int64_t e = int64_t(qrow_first + jq) * P.q_stride + int64_t(h * G + g) * 128 + lane;
+            v = load_elt(P.q, P.q_dtype, e);
+        }
+        S.q[i] = v;
+    }
+
+    const int lg = tid & 15, tg = tid >> 4;               // lane group, token group
+    const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
+    const int kfield = P.coeff_bytes + 2 + h * P.k_row;
+    const int vfield = P.v_offset + h * P.v_row;
+
+    for (int t0 = t_begin; t0 < t_end; t0 += TT) {
+        __syncthreads();                                   // previous tile fully consumed
+        // ---- gather: slots, rulers, residual / V rows, RoPE rows
+        if (tid < TT) {
+            const int t = t0 + tid;
+            int64_t slot = -1;
+            if (t < t_end) slot = int64_t(brow[t / P.block_size]) * P.block_size + t % P.block_size;
+            S.slot[tid] = slot;
+        }
+        __syncthreads();
+        if (tid < TT) {
+            const int64_t slot = S.slot[tid];
+            S.cs[tid] = slot >= 0 ? f16_at(P.cache + slot * P.row_bytes + P.coeff_bytes) : 0.f;
+        }
+        for (int i = tid; i < TT * P.k_row; i += NT) {
+            const int t = i / P.k_row, b = i % P.k_row;
+            const int64_t slot = S.slot[t];
+            S.krow[t * S.kpad + b] = slot >= 0 ? P.cache[slot * P.row_bytes + kfield + b] : 0;
+        }
+        for (int i = tid; i < TT * P.v_row; i += NT) {
+            const int t = i / P.v_row, b = i % P.v_row;
+            const int64_t slot = S.slot[t];
+            S.vrow[t * S.vpad + b] = slot >= 0 ? P.cache[slot * P.row_bytes + vfield + b] : 0;
+        }
+        for (int i = tid; i < TT * 64; i += NT) {
+            const int t = i >> 6, c = i & 63;
+            const int pos = min(t0 + t, int(P.table_rows - 1));
+            S.cosv[i] = load_elt(P.table, P.table_dtype, int64_t(pos) * 128 + c);
+            S.sinv[i] = load_elt(P.table, P.table_dtype, int64_t(pos) * 128 + 64 + c);
+        }
+        __syncthreads();
+        for (int i = tid; i < P.r1 * TT; i += NT) {
+            const int rr = i / TT, t = i % TT;
+            const int64_t slot = S.slot[t];
+            const float cq = slot >= 0 ? float(int8_t(P.cache[slot * P.row_bytes + rr])) : 0.f;
+            S.coef[rr * TT + t] = cq * S.cs[t];           // g = cq * cs, exact in fp32
+        }
+        if (tid < TT) {
+            const uint8_t* kr = S.krow + tid * S.kpad;
+            const uint8_t* vr = S.vrow + tid * S.vpad;
+            uint32_t kp = 0, vp = 0;
+            #pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const uint32_t kw = bitmap_word(kr, w), vw = bitmap_word(vr, w);
+                S.kw[tid * 4 + w] = kw; S.kpre[tid * 4 + w] = kp; kp += __popc(kw);
+                S.vw[tid * 4 + w] = vw; S.vpre[tid * 4 + w] = vp; vp += __popc(vw);
+            }
+            S.krs[tid] = f16_at(kr + 16 + P.k_pb);
+            S.vrs[tid] = f16_at(vr + 16 + P.v_pb);
+        }
+        __syncthreads();
+
+        // ---- rebuild + patch + rotate: thread owns tokens 4tg..4tg+3, lanes 4lg.. and 64+4lg..
+        {
+            float acc[4][8];
+            #pragma unroll
+            for (int t = 0; t < 4; ++t)
+                #pragma unroll
+                for (int c = 0; c < 8; ++c) acc[t][c] = 0.f;
+            for (int rr = 0; rr < P.r1; ++rr) {
+                const float4 dl = *reinterpret_cast<const float4*>(S.dec + rr * 128 + 4 * lg);
+                const float4 dh = *reinterpret_cast<const float4*>(S.dec + rr * 128 + 64 + 4 * lg);
+                const float4 cv = *reinterpret_cast<const float4*>(S.coef + rr * TT + 4 * tg);
+                const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+                const float dd[8] = {dl.x, dl.y, dl.z, dl.w, dh.x, dh.y, dh.z, dh.w};
+                #pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    #pragma unroll
+                    for (int c = 0; c < 8; ++c) acc[t][c] = fmaf(cc[t], dd[c], acc[t][c]);
+            }
+            #pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int tt = 4 * tg + t;
+                const uint8_t* stream = S.krow + tt * S.kpad + 16;
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int jl = 4 * lg + c, jh = 64 + 4 * lg + c;
+                    const float klo = acc[t][c] + staged_lane(S.kw + tt * 4, S.kpre + tt * 4, stream,
+                                                              S.krs[tt], P.res_bits, P.res_k, jl);
+                    const float khi = acc[t][4 + c] + staged_lane(S.kw + tt * 4, S.kpre + tt * 4, stream,
+                                                                  S.krs[tt], P.res_bits, P.res_k, jh);
+                    const float cz = S.cosv[tt * 64 + jl], sz = S.sinv[tt * 64 + jl];
+                    S.y[tt * RS + jl] = klo * cz - khi * sz;
+                    S.y[tt * RS + jh] = khi * cz + klo * sz;
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- scores: one (query row, token) pair per thread-iteration
+        for (int i = tid; i < QR * TT; i += NT) {
+            const int qr = i / TT, t = i % TT;
+            const int jq = j0 + qr / G;
+            const int tabs = t0 + t;
+            float s = -INFINITY;
+            const bool live = tabs < t_end && qr < nrows && (!MULTI || tabs <= p0 + jq);
+            if (live) {
+                const float4* yr = reinterpret_cast<const float4*>(S.y + t * RS);
+                const float4* qv = reinterpret_cast<const float4*>(S.q + qr * 128);
+                float a = 0.f;
+                #pragma unroll 8
+                for (int c = 0; c < 32; ++c) {
+                    const float4 x = yr[c], w = qv[c];
+                    a = fmaf(x.x, w.x, a); a = fmaf(x.y, w.y, a);
+                    a = fmaf(x.z, w.z, a); a = fmaf(x.w, w.w, a);
+                }
+                s = a * P.scale;
+            }
+            S.p[qr * TT + t] = s;
+        }
+        __syncthreads();
+
+        // ---- online softmax: one warp per query row
+        for (int qr = tid >> 5; qr < QR; qr += NT / 32) {
+            const int lane = tid & 31;
+            const float s = S.p[qr * TT + lane];
+            float mx = s;
+            #pragma unroll
+            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_old = S.m[qr];
+            const float m_new = fmaxf(m_old, mx);
+            float pe = 0.f, corr = 1.f;
+            if (m_new != -INFINITY) {
+                pe = (s == -INFINITY) ? 0.f : expf(s - m_new);
+                corr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+            }
+            float sum = pe;
+            #pragma unroll
+            for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            S.p[qr * TT + lane] = pe;
+            __syncwarp();
+            if (lane == 0) {
+                S.l[qr] = S.l[qr] * corr + sum;
+                S.m[qr] = m_new;
+                S.corr[qr] = corr;
+            }
+        }
+        __syncthreads();
+
+        // ---- readout: thread = lane
+        {
+            #pragma unroll
+            for (int i = 0; i < QR; ++i) o[i] *= S.corr[i];
+            const int ntok = min(TT, t_end - t0);
+            for (int t = 0; t < ntok; ++t) {
+                const float v = staged_lane(S.vw + t * 4, S.vpre + t * 4, S.vrow + t * S.vpad + 16,
+                                            S.vrs[t], P.v_bits, P.v_lanes, tid);
+                #pragma unroll
+                for (int i = 0; i < QR; ++i) o[i] = fmaf(S.p[i * TT + t], v, o[i]);
+            }
+        }
+    }
+    __syncthreads();
+    write_partial<QR>(P, r, hl, j0 * G, split, o, S, nrows);
+}
+
+// Combine the splits of one (request, KV head, query row): thread = lane.
+__global__ void __launch_bounds__(128) merge_kernel(const ReadParams P) {
+    const int qr = blockIdx.x, hl = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
+    const int jq = qr / P.G, g = qr % P.G;
+    const int qlen = P.q_len ? P.q_len[r] : 1;
+    if (jq >= qlen) return;
+    const int QG = P.qmax * P.G;
+    const int64_t row = (int64_t(r) * P.n_heads + hl) * QG + qr;
+    float M = -INFINITY;
+    for (int s = 0; s < P.n_splits; ++s) M = fmaxf(M, P.part_ml[(row * P.n_splits + s) * 2]);
+    float acc = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < P.n_splits; ++s) {
+            const float ms = P.part_ml[(row * P.n_splits + s) * 2];
+            if (ms == -INFINITY) continue;
+            const float w = expf(ms - M);
+            acc = fmaf(w, P.part_o[(row * P.n_splits + s) * 128 + lane], acc);
+            den = fmaf(w, P.part_ml[(row * P.n_splits + s) * 2 + 1], den);
+        }
+    }
+    const float v = den > 0.f ? acc / den : 0.f;
+    const int qrow = (P.q_start ? P.q_start[r] : r) + jq;
+    const int head_q = (P.head_lo + hl) * P.G + g;
+    store_elt(P.out, P.out_dtype, int64_t(qrow) * P.out_stride + int64_t(head_q) * 128 + lane, v);
+}
+
+// ------------------------------------------------------------------ host side
+int qblock_for(int G, bool multi) {
+    if (!multi) return 1;
+    return G <= 3 ? 16 : (G <= 6 ? 8 : 4);               // G*QB <= 48 query rows per CTA
+}
+
+struct Plan {
+    int qb, n_qblk, n_splits, chunk;
+    size_t part_o_bytes, part_ml_bytes, smem;
+};
+
+Plan make_plan(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_q, int max_seq,
+               int n_heads, bool multi) {
+    Plan pl{};
+    const int G = HQ / lay->H;
+    pl.qb = qblock_for(G, multi);
+    const int qmax = multi ? max(max_q, 1) : 1;
+    pl.n_qblk = (qmax + pl.qb - 1) / pl.qb;
+    const int base = max(1, n_reqs * n_heads * pl.n_qblk);
+    const int max_tiles = max(1, (max_seq + TT - 1) / TT);
+    int want = (2 * 148 + base - 1) / base;                // about two CTAs per SM
+    want = max(1, min(want, max_tiles));
+    const int tiles_per_split = (max_tiles + want - 1) / want;
+    pl.chunk = tiles_per_split * TT;
+    pl.n_splits = max(1, (max_seq + pl.chunk - 1) / pl.chunk);
+    const size_t rows = size_t(n_reqs) * n_heads * qmax * G;
+    pl.part_o_bytes = rows * pl.n_splits * 128 * sizeof(float);
+    pl.part_ml_bytes = rows * pl.n_splits * 2 * sizeof(float);
+    pl.smem = smem_bytes(lay->r1, G * pl.qb, lay->k_row_bytes, lay->v_row_bytes);
+    return pl;
+}
+
+int check_common(const ttkv_layout_t* lay, const ttkv_cache_t* cache, const ttkv_batch_t* batch,
+                 const ttkv_rope_t* rope, int HQ, int head_lo, int head_hi) {
+    if (!lay || !cache || !batch || !rope) return fail(TTKV_ERR_ARG, "null layout/cache/batch/rope");
+    if (lay->d != kHeadDim) return fail(TTKV_ERR_UNSUPPORTED, "head dim %d: the kernels serve d=128", lay->d);
+    if (lay->qbits != 8) return fail(TTKV_ERR_UNSUPPORTED, "qbits=%d: coefficients are int8", lay->qbits);
+    if (lay->r1 < 1 || lay->r1 > kMaxRank)
+        return fail(TTKV_ERR_UNSUPPORTED, "r1=%d outside 1..%d", lay->r1, kMaxRank);
+    if (lay->res_k < 1) return fail(TTKV_ERR_UNSUPPORTED, "res_k=0 (no residual) is not served");
+    if (HQ < lay->H || HQ % lay->H)
+        return fail(TTKV_ERR_ARG, "HQ=%d is not a multiple of H=%d", HQ, lay->H);
+    if (HQ / lay->H > kMaxG) return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d > %d", HQ / lay->H, kMaxG);
+    if (head_lo < 0 || head_hi > lay->H || head_lo >= head_hi)
+        return fail(TTKV_ERR_ARG, "head range [%d, %d) outside [0, %d)", head_lo, head_hi, lay->H);
+    if (!cache->base || cache->block_size < 1 || cache->n_slots < 0 || cache->row_bytes < lay->blob_bytes)
+        return fail(TTKV_ERR_ARG, "cache rows are %lld bytes, the layout needs %d",
+                    (long long)cache->row_bytes, lay->blob_bytes);
+    if (!batch->block_table || !batch->seq_lens || !batch->decoders || !batch->dec_index || batch->n_reqs < 0)
+        return fail(TTKV_ERR_ARG, "batch has a null pointer");
+    if (batch->dec_stride < int64_t(lay->r1) * lay->H * 128)
+        return fail(TTKV_ERR_ARG, "decoder stride %lld < r1*H*d", (long long)batch->dec_stride);
+    if ((reinterpret_cast<uintptr_t>(batch->decoders) & 15) || (batch->dec_stride & 3))
+        return fail(TTKV_ERR_ALIGN, "decoders must be 16-byte aligned with a stride of 4 floats");
+    if (!rope->table || rope->rows < 1) return fail(TTKV_ERR_ARG, "RoPE table missing");
+    if (rope->dtype < TTKV_F32 || rope->dtype > TTKV_BF16) return fail(TTKV_ERR_ARG, "RoPE dtype");
+    return TTKV_OK;
+}
+
+ReadParams base_params(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                       const ttkv_batch_t* batch, const ttkv_rope_t* rope) {
+    ReadParams P{};
+    P.H = lay->H; P.r1 = lay->r1; P.res_k = lay->res_k; P.res_bits = lay->res_bits;
+    P.v_lanes = lay->v_lanes; P.v_bits = lay->v_bits;
+    P.coeff_bytes = lay->coeff_bytes; P.k_row = lay->k_row_bytes; P.v_row = lay->v_row_bytes;
+    P.v_offset = lay->v_offset;
+    P.k_pb = packed_row_bytes(lay->res_k, lay->res_bits);
+    P.v_pb = packed_row_bytes(lay->v_lanes, lay->v_bits);
+    P.cache = cache->base; P.n_slots = cache->n_slots; P.row_bytes = cache->row_bytes;
+    P.block_size = cache->block_size;
+    P.block_table = batch->block_table; P.bt_stride = batch->bt_stride; P.bt_cols = batch->bt_cols;
+    P.seq_lens = batch->seq_lens; P.decoders = batch->decoders; P.dec_stride = batch->dec_stride;
+    P.dec_index = batch->dec_index; P.n_decoders = batch->n_decoders;
+    P.table = rope->table; P.table_dtype = rope->dtype; P.table_rows = rope->rows;
+    return P;
+}
+
+template <int G, int QB, bool MULTI>
+int launch_g(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
+    auto k = attn_split_kernel<G, QB, MULTI>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) != cudaSuccess)
+        return fail(TTKV_ERR_CUDA, "shared memory %zu bytes refused", pl.smem);
+    dim3 grid(pl.n_splits, P.n_heads * pl.n_qblk, n_reqs);
+    k<<<grid, NT, pl.smem, st>>>(P);
+    if (int e = check_launch("attn_split_kernel")) return e;
+    dim3 mg(P.qmax * P.G, P.n_heads, n_reqs);
+    merge_kernel<<<mg, 128, 0, st>>>(P);
+    return check_launch("merge_kernel");
+}
+
+template <bool MULTI>
+int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
+    switch (P.G) {
+        case 1: return launch_g<1, (MULTI ? 16 : 1), MULTI>(P, pl, n_reqs, st);
+        case 2: return launch_g<2, (MULTI ? 16 : 1), MULTI>(P, pl, n_reqs, st);
+        case 3: return launch_g<3, (MULTI ? 16 : 1), MULTI>(P, pl, n_reqs, st);
+        case 4: return launch_g<4, (MULTI ? 8 : 1), MULTI>(P, pl, n_reqs, st);
+        case 5: return launch_g<5, (MULTI ? 8 : 1), MULTI>(P, pl, n_reqs, st);
+        case 6: return launch_g<6, (MULTI ? 8 : 1), MULTI>(P, pl, n_reqs, st);
+        case 7: return launch_g<7, (MULTI ? 4 : 1), MULTI>(P, pl, n_reqs, st);
+        case 8: return launch_g<8, (MULTI ? 4 : 1), MULTI>(P, pl, n_reqs, st);
+    }
+    return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
+}
+
+}  // namespace
+}  // namespace ttkv
+
+using namespace ttkv;
+
+extern "C" size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
+                                              int32_t max_seq_len, int32_t head_lo, int32_t head_hi) {
+    if (!lay || lay->H < 1 || HQ < lay->H || head_hi <= head_lo) return 0;
+    const Plan pl = make_plan(lay, n_reqs, HQ, 1, max_seq_len, head_hi - head_lo, false);
+    return pl.part_o_bytes + pl.part_ml_bytes;
+}
+
+extern "C" size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
+                                               int32_t max_q_len, int32_t max_seq_len,
+                                               int32_t head_lo, int32_t head_hi) {
+    if (!lay || lay->H < 1 || HQ < lay->H || head_hi <= head_lo) return 0;
+    const Plan pl = make_plan(lay, n_reqs, HQ, max_q_len, max_seq_len, head_hi - head_lo, true);
+    return pl.part_o_bytes + pl.part_ml_bytes;
+}
+
+static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                      const ttkv_batch_t* batch, const ttkv_rope_t* rope, const int32_t* q_start,
+                      const int32_t* q_len, const void* q, int32_t q_dtype, int64_t q_stride,
+                      int32_t HQ, float scale, int32_t head_lo, int32_t head_hi, void* out,
+                      int32_t out_dtype, int64_t out_stride, int32_t max_q_len, int32_t max_seq_len,
+                      void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+    if (int e = check_common(lay, cache, batch, rope, HQ, head_lo, head_hi)) return e;
+    if (!q || !out) return fail(TTKV_ERR_ARG, "q/out null");
+    if (q_dtype < TTKV_F32 || q_dtype > TTKV_BF16 || out_dtype < TTKV_F32 || out_dtype > TTKV_BF16)
+        return fail(TTKV_ERR_ARG, "q/out dtype");
+    if (q_stride < int64_t(HQ) * 128 || out_stride < int64_t(HQ) * 128)
+        return fail(TTKV_ERR_ARG, "q/out stride below HQ*d");
+    if (multi && (!q_start || !q_len)) return fail(TTKV_ERR_ARG, "q_start/q_len null");
+    if (max_seq_len < 0 || (multi && max_q_len < 1)) return fail(TTKV_ERR_ARG, "max lengths");
+    if (max_seq_len > rope->rows)
+        return fail(TTKV_ERR_ARG, "position %d is past the model's cos_sin_cache, which holds %lld rows",
+                    max_seq_len - 1, (long long)rope->rows);
+    if (batch->n_reqs == 0 || max_seq_len == 0) return TTKV_OK;
+    const int n_heads = head_hi - head_lo;
+    const Plan pl = make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
+    if (pl.smem > 227 * 1024) return fail(TTKV_ERR_UNSUPPORTED, "r1=%d needs %zu B of shared memory", lay->r1, pl.smem);
+    if (!workspace || ws_bytes < pl.part_o_bytes + pl.part_ml_bytes)
+        return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, pl.part_o_bytes + pl.part_ml_bytes);
+    ReadParams P = base_params(lay, cache, batch, rope);
+    P.q = q; P.q_dtype = q_dtype; P.q_stride = q_stride; P.HQ = HQ; P.G = HQ / lay->H;
+    P.q_start = multi ? q_start : nullptr; P.q_len = multi ? q_len : nullptr;
+    P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
+    P.qmax = multi ? max_q_len : 1; P.n_qblk = pl.n_qblk; P.n_splits = pl.n_splits; P.chunk = pl.chunk;
+    P.part_o = reinterpret_cast<float*>(workspace);
+    P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
+    P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return multi ? launch<true>(P, pl, batch->n_reqs, st) : launch<false>(P, pl, batch->n_reqs, st);
+}
+
+extern "C" int ttkv_decode_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                 const ttkv_batch_t* batch, const ttkv_rope_t* rope, const void* q,
+                                 int32_t q_dtype, int64_t q_stride, int32_t HQ, float scale,
+                                 int32_t head_lo, int32_t head_hi, void* out, int32_t out_dtype,
+                                 int64_t out_stride, int32_t max_seq_len, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, void* stream) {
+    return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ, scale,
+                      head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, workspace,
+                      workspace_bytes, status, stream);
+}
+
+extern "C" int ttkv_prefill_cont_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                       const ttkv_batch_t* batch, const ttkv_rope_t* rope,
+                                       const int32_t* q_start, const int32_t* q_len, const void* q,
+                                       int32_t q_dtype, int64_t q_stride, int32_t HQ, float scale,
+                                       int32_t head_lo, int32_t head_hi, void* out,
+                                       int32_t out_dtype, int64_t out_stride, int32_t max_q_len,
+                                       int32_t max_seq_len, void* workspace,
+                                       size_t workspace_bytes, int32_t* status, void* stream) {
+    return read_entry(true, lay, cache, batch, rope, q_start, q_len, q, q_dtype, q_stride, HQ, scale,
+                      head_lo, head_hi, out, out_dtype, out_stride, max_q_len, max_seq_len,
+                      workspace, workspace_bytes, status, stream);
+}

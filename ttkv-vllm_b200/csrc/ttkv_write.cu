@@ -1,0 +1,514 @@
+// The TT-KV write: tokens encoded straight into their paged slots, and the fit tail.
+//
+//   project_kernel       c = M @ pinv for every token of the layer (frozen projection,
+//                        vllm_ttkv/encode.py:301-351), one warp per (token, coefficient)
+//   encode_pack_kernel   one CTA per (token, KV head): the per-token int8 quantisation of c,
+//                        the head's residual R = K - (cq*cs) @ decoder, then the exact top-k lane
+//                        select + quantise + MSB-first pack of the K residual row and the V row,
+//                        written at the token's slot (select_triton.py:157-232); the head-0 CTA
+//                        also writes the coefficient block and its ruler
+//   select_rows_kernel   the same select/pack for caller-supplied (head, token) rows
+//   fit-tail kernels     everything build_k_layer (codec/ttkv_packed_cache.py:337-375) does after
+//                        the SVDs: coefficient quantisation, core quantisation, the decoder
+//                        contraction and its per-row quantisation, zero-padded to the budget
+//
+// Bit-exactness: given the same fp32 inputs the bytes equal the reference writer's. The rules
+// that make that true are each named where they are applied.
+#include <cfloat>
+#include <cmath>
+
+#include "ttkv_common.cuh"
+
+namespace ttkv {
+namespace {
+
+constexpr uint32_t FULL = 0xffffffffu;
+
+// ------------------------------------------------------------------ warp select + pack
+// One warp packs one 128-lane row x (lane L of the warp holds lanes 4L..4L+3) into `dst`
+// (bitmap d/8 bytes, ceil(lanes*bits/8) code bytes, fp16 ruler). `codes` is 128 bytes of
+// per-warp scratch in shared memory.
+//
+// Selection (select_triton.py:180-193): the k-th largest |x| is built one bit at a time on the
+// fp32 magnitude bits (monotone for non-negative floats); every lane above it is kept, then the
+// lowest-index lanes equal to it until exactly k are kept.
+// Ruler (select_triton.py:195-201): max|x| over the row (the largest kept lane), 1 if zero, times
+// the fp32 reciprocal of 2^(bits-1)-1. Code: rint(x / ruler) with a correctly rounded division,
+// clamped, offset by 2^(bits-1) (select_triton.py:202-203).
+__device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes, int bits,
+                                                 uint8_t* dst, uint8_t* codes) {
+    const int L = threadIdx.x & 31;
+    uint32_t u[4];
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) u[i] = __float_as_uint(fabsf(x[i]));
+
+    uint32_t t = 0;
+    for (int b = 30; b >= 0; --b) {
+        const uint32_t cand = t | (1u << b);
+        const int local = int(u[0] >= cand) + int(u[1] >= cand) + int(u[2] >= cand) + int(u[3] >= cand);
+        const int cnt = __reduce_add_sync(FULL, local);
+        if (cnt >= lanes) t = cand;
+    }
+    const int above_local = int(u[0] > t) + int(u[1] > t) + int(u[2] > t) + int(u[3] > t);
+    const int n_above = __reduce_add_sync(FULL, above_local);
+    const int tie_local = int(u[0] == t) + int(u[1] == t) + int(u[2] == t) + int(u[3] == t);
+    // exclusive prefix of ties over lower warp lanes
+    int tie_excl = tie_local;
+    #pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(FULL, tie_excl, off);
+        if (L >= off) tie_excl += v;
+    }
+    tie_excl -= tie_local;
+    bool sel[4];
+    int seen = tie_excl;
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool tie = u[i] == t;
+        seen += int(tie);
+        sel[i] = (u[i] > t) || (tie && seen <= lanes - n_above);
+    }
+    const int sel_local = int(sel[0]) + int(sel[1]) + int(sel[2]) + int(sel[3]);
+    int rank = sel_local;
+    #pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(FULL, rank, off);
+        if (L >= off) rank += v;
+    }
+    rank -= sel_local;                                    // exclusive: rank of this thread's first kept lane
+
+    const uint32_t umax_local = max(max(u[0], u[1]), max(u[2], u[3]));
+    const uint32_t umax = __reduce_max_sync(FULL, umax_local);
+    const float rmax = __uint_as_float(umax);
+    const float sc = __fmul_rn(rmax == 0.f ? 1.f : rmax, inv_ruler(bits));
+    const float lo = -float(1 << (bits - 1)), hi = float((1 << (bits - 1)) - 1);
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (sel[i]) {
+            float qf = rintf(__fdiv_rn(x[i], sc));
+            qf = fminf(fmaxf(qf, lo), hi) + float(1 << (bits - 1));
+            codes[rank] = uint8_t(qf);
+            ++rank;
+        }
+    }
+    // bitmap: lanes 8k..8k+7 live in threads 2k (high nibble) and 2k+1 (low nibble)
+    const uint32_t nib = (uint32_t(sel[0]) << 3) | (uint32_t(sel[1]) << 2) | (uint32_t(sel[2]) << 1) |
+                         uint32_t(sel[3]);
+    const uint32_t other = __shfl_down_sync(FULL, nib, 1);
+    if ((L & 1) == 0) dst[L >> 1] = uint8_t((nib << 4) | other);
+    __syncwarp();
+    // codes: MSB-first stream, row padded to whole bytes (codec/ttkv_packed_cache.py:50-66)
+    const int pb = packed_row_bytes(lanes, bits);
+    for (int by = L; by < pb; by += 32) {
+        uint32_t v = 0;
+        #pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const int pos = by * 8 + b;
+            const int ci = pos / bits;
+            uint32_t bit = 0;
+            if (ci < lanes) bit = (uint32_t(codes[ci]) >> (bits - 1 - pos % bits)) & 1u;
+            v |= bit << (7 - b);
+        }
+        dst[16 + by] = uint8_t(v);
+    }
+    if (L == 0) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(sc));
+        dst[16 + pb] = uint8_t(h & 0xff);
+        dst[16 + pb + 1] = uint8_t(h >> 8);
+    }
+    __syncwarp();
+}
+
+// ------------------------------------------------------------------ frozen projection
+struct ProjParams {
+    int H, r1;
+    const void* k;
+    int k_dtype;
+    int64_t k_stride;
+    const int32_t* tok_dec;
+    const float* pinvs;       // per decoder: [r1, H*d] (pinv transposed)
+    int64_t pinv_stride;
+    int n_decoders;
+    float* c;                 // [n_tok, r1]
+    int32_t* status;
+};
+
+constexpr int PROJ_WARPS = 8;
+
+// grid (ceil(r1 / PROJ_WARPS), n_tok): warp w computes coefficient blockIdx.x*8+w of token
+// blockIdx.y as a 1024-long dot product over the token's K row (m = h*d + j).
+__global__ void __launch_bounds__(PROJ_WARPS * 32) project_kernel(const ProjParams P) {
+    const int t = blockIdx.y;
+    const int w = threadIdx.x >> 5, L = threadIdx.x & 31;
+    const int rr = blockIdx.x * PROJ_WARPS + w;
+    const int HD = P.H * kHeadDim;
+    __shared__ float m_s[8 * kHeadDim];
+    for (int i = threadIdx.x; i < HD; i += blockDim.x)
+        m_s[i] = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + i);
+    __syncthreads();
+    const int di = P.tok_dec[t];
+    if (di < 0 || di >= P.n_decoders) {
+        if (threadIdx.x == 0) report(P.status, TTKV_STATUS_DECODER);
+        return;
+    }
+    if (rr >= P.r1) return;
+    const float* pv = P.pinvs + int64_t(di) * P.pinv_stride + int64_t(rr) * HD;
+    float acc = 0.f;
+    for (int m = L; m < HD; m += 32) acc = fmaf(m_s[m], pv[m], acc);
+    #pragma unroll
+    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(FULL, acc, off);
+    if (L == 0) P.c[int64_t(t) * P.r1 + rr] = acc;
+}
+
+// ------------------------------------------------------------------ encode + pack
+struct EncParams {
+    int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
+    uint8_t* cache;
+    int64_t n_slots, row_bytes;
+    const int64_t* slots;
+    const void* k;
+    int k_dtype;
+    int64_t k_stride;
+    const void* v;
+    int v_dtype;
+    int64_t v_stride;
+    const int32_t* tok_dec;
+    const float* decoders;    // per decoder: [r1, H*d]
+    int64_t dec_stride;
+    int n_decoders;
+    const float* c;           // projected coefficients [n_tok, r1] (frozen path) or null
+    const int8_t* coeff_q;    // given codes [n_tok, r1] (fit path)
+    const float* coeff_scale; // given rulers [n_tok] fp32 (fit path)
+    int32_t* status;
+};
+
+// grid (H, n_tok), 128 threads.
+__global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
+    __shared__ float g_s[kMaxRank];          // cq * cs
+    __shared__ int8_t cq_s[kMaxRank];
+    __shared__ float r_s[kHeadDim];
+    __shared__ uint8_t codes_s[2][128];
+    __shared__ float wmax_s[4];
+    __shared__ float cs_s;
+
+    const int64_t slot = P.slots[t];
+    if (slot < 0 || slot >= P.n_slots) {
+        if (tid == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
+        return;
+    }
+    const int di = P.tok_dec ? P.tok_dec[t] : 0;
+    if (P.decoders && (di < 0 || di >= P.n_decoders)) {
+        if (tid == 0) report(P.status, TTKV_STATUS_DECODER);
+        return;
+    }
+    uint8_t* row = P.cache + slot * P.row_bytes;
+
+    // ---- coefficient codes and ruler
+    if (P.c) {
+        // frozen path (vllm_ttkv/encode.py:329-333): cs = amax|c| * fp32(1/127), 0 -> 1;
+        // cq = clamp(rint(c / cs), -128, 127) with a correctly rounded division
+        float a = 0.f;
+        for (int i = tid; i < P.r1; i += 128) a = fmaxf(a, fabsf(P.c[int64_t(t) * P.r1 + i]));
+        a = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(a)));
+        if (L == 0) wmax_s[w] = a;
+        __syncthreads();
+        if (tid == 0) {
+            const float amax = fmaxf(fmaxf(wmax_s[0], wmax_s[1]), fmaxf(wmax_s[2], wmax_s[3]));
+            float cs = __fmul_rn(amax, inv_ruler(8));
+            cs_s = (cs == 0.f) ? 1.f : cs;
+        }
+        __syncthreads();
+        const float cs = cs_s;
+        for (int i = tid; i < P.r1; i += 128) {
+            const float qf = fminf(fmaxf(rintf(__fdiv_rn(P.c[int64_t(t) * P.r1 + i], cs)), -128.f), 127.f);
+            cq_s[i] = int8_t(qf);
+            g_s[i] = qf * cs;
+        }
+    } else {
+        const float cs = P.coeff_scale[t];
+        if (tid == 0) cs_s = cs;
+        for (int i = tid; i < P.r1; i += 128) {
+            const int8_t q = P.coeff_q[int64_t(t) * P.r1 + i];
+            cq_s[i] = q;
+            g_s[i] = float(q) * cs;
+        }
+    }
+    __syncthreads();
+
+    // ---- residual of this head: R = K - (cq*cs) @ decoder[:, h]   (encode.py:335-336)
+    {
+        const int j = tid;
+        float kd = 0.f;
+        if (P.decoders) {
+            const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * kHeadDim + j;
+            const int64_t stride = int64_t(P.H) * kHeadDim;
+            for (int rr = 0; rr < P.r1; ++rr) kd = fmaf(g_s[rr], dec[rr * stride], kd);
+        }
+        const float kv = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + h * kHeadDim + j);
+        r_s[j] = kv - kd;
+    }
+    __syncthreads();
+
+    if (w == 0) {
+        float x[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = r_s[4 * L + i];
+        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + h * P.k_row, codes_s[0]);
+    } else if (w == 1) {
+        float x[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)
+            x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
+        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + h * P.v_row, codes_s[1]);
+    } else if (w == 2 && h == 0) {
+        // the coefficient block and its fp16 ruler, once per token (encode.py:570-573)
+        for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
+        if (L == 0) {
+            const uint16_t hb = __half_as_ushort(__float2half_rn(cs_s));
+            row[P.coeff_bytes] = uint8_t(hb & 0xff);
+            row[P.coeff_bytes + 1] = uint8_t(hb >> 8);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ standalone rows
+struct RowsParams {
+    uint8_t* cache;
+    int64_t n_slots, row_bytes;
+    const int64_t* slots;
+    int n_tok, heads, field_off, row_stride, lanes, bits;
+    const void* x;
+    int x_dtype;
+    int32_t* status;
+};
+
+// 4 rows per CTA, one warp each; row i = h*n_tok + t (select_triton.py:173-177).
+__global__ void __launch_bounds__(128) select_rows_kernel(const RowsParams P) {
+    __shared__ uint8_t codes_s[4][128];
+    const int w = threadIdx.x >> 5, L = threadIdx.x & 31;
+    const int64_t i = int64_t(blockIdx.x) * 4 + w;
+    if (i >= int64_t(P.n_tok) * P.heads) return;
+    const int t = int(i % P.n_tok), h = int(i / P.n_tok);
+    const int64_t slot = P.slots[t];
+    if (slot < 0 || slot >= P.n_slots) {
+        if (L == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
+        return;
+    }
+    float x[4];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = load_elt(P.x, P.x_dtype, i * kHeadDim + 4 * L + k);
+    warp_select_pack(x, P.lanes, P.bits, P.cache + slot * P.row_bytes + P.field_off + h * P.row_stride,
+                     codes_s[w]);
+}
+
+// ------------------------------------------------------------------ fit tail
+// Per-token coefficient quantisation of the token core G1 [n, r] (ttkv_packed_cache.py:353-356):
+// cs = amax * fp32(1/127), 0 -> 1, cq = clamp(rint(c/cs)); codes zero-padded to `budget`.
+__global__ void __launch_bounds__(32) quant_coeff_kernel(const float* G1, int n, int r, int budget,
+                                                         int8_t* cq, float* cs_out) {
+    const int t = blockIdx.x, L = threadIdx.x;
+    float a = 0.f;
+    for (int i = L; i < r; i += 32) a = fmaxf(a, fabsf(G1[int64_t(t) * r + i]));
+    a = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(a)));
+    float cs = __fmul_rn(a, inv_ruler(8));
+    cs = cs == 0.f ? 1.f : cs;
+    for (int i = L; i < budget; i += 32) {
+        float qf = 0.f;
+        if (i < r) qf = fminf(fmaxf(rintf(__fdiv_rn(G1[int64_t(t) * r + i], cs)), -128.f), 127.f);
+        cq[int64_t(t) * budget + i] = int8_t(qf);
+    }
+    if (L == 0) cs_out[t] = cs;
+}
+
+// quant_cores (codec/ttkv_codec.py:142-163): per row s = max(amax, 1e-12) * fp32(1/127),
+// out = clamp(rint(M/s), -127, 127) * s.
+__global__ void __launch_bounds__(32) quant_core_rows_kernel(const float* M, int cols, float* out) {
+    const int row = blockIdx.x, L = threadIdx.x;
+    const float* m = M + int64_t(row) * cols;
+    float a = 0.f;
+    for (int i = L; i < cols; i += 32) a = fmaxf(a, fabsf(m[i]));
+    a = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(a)));
+    const float s = __fmul_rn(fmaxf(a, 1e-12f), inv_ruler(8));
+    for (int i = L; i < cols; i += 32)
+        out[int64_t(row) * cols + i] = fminf(fmaxf(rintf(__fdiv_rn(m[i], s)), -127.f), 127.f) * s;
+}
+
+// dec[a, h*d + j] = sum_b G2q[a, j, b] * G3q[b, h]   ("ajb,bh->ahj", ttkv_packed_cache.py:361)
+__global__ void decoder_contract_kernel(const float* G2q, const float* G3q, int r2, int H, int d,
+                                        float* dec) {
+    const int a = blockIdx.x;
+    for (int m = threadIdx.x; m < H * d; m += blockDim.x) {
+        const int h = m / d, j = m % d;
+        float acc = 0.f;
+        for (int b = 0; b < r2; ++b)
+            acc = fmaf(G2q[(int64_t(a) * d + j) * r2 + b], G3q[b * H + h], acc);
+        dec[int64_t(a) * H * d + m] = acc;
+    }
+}
+
+// _quant_rows (ttkv_packed_cache.py:170-176) of the decoder and its fp32 form
+// decoder_f = dec_q * fp16(scale) (ttkv_packed_cache.py:290-293), rows past r zero.
+__global__ void __launch_bounds__(256) decoder_quant_kernel(const float* dec, int r, int budget, int cols,
+                                                            int8_t* dec_q, uint16_t* dec_scale,
+                                                            float* decoder) {
+    const int a = blockIdx.x;
+    __shared__ float wmax[8];
+    __shared__ float sc_s;
+    if (a >= r) {
+        for (int i = threadIdx.x; i < cols; i += blockDim.x) decoder[int64_t(a) * cols + i] = 0.f;
+        return;
+    }
+    float m = 0.f;
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, fabsf(dec[int64_t(a) * cols + i]));
+    m = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(m)));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float rmax = 0.f;
+        for (int i = 0; i < int(blockDim.x >> 5); ++i) rmax = fmaxf(rmax, wmax[i]);
+        sc_s = __fmul_rn(rmax == 0.f ? 1.f : rmax, inv_ruler(8));
+    }
+    __syncthreads();
+    const float sc = sc_s;
+    const __half sh = __float2half_rn(sc);
+    const float sf = __half2float(sh);
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+        const float qf = fminf(fmaxf(rintf(__fdiv_rn(dec[int64_t(a) * cols + i], sc)), -128.f), 127.f);
+        dec_q[int64_t(a) * cols + i] = int8_t(qf);
+        decoder[int64_t(a) * cols + i] = qf * sf;
+    }
+    if (threadIdx.x == 0) dec_scale[a] = __half_as_ushort(sh);
+}
+
+int check_cache(const ttkv_cache_t* cache, int need) {
+    if (!cache || !cache->base) return fail(TTKV_ERR_ARG, "cache is null");
+    if (cache->row_bytes < need || cache->n_slots < 0)
+        return fail(TTKV_ERR_ARG, "cache rows are %lld bytes, %d needed", (long long)cache->row_bytes, need);
+    return TTKV_OK;
+}
+
+}  // namespace
+}  // namespace ttkv
+
+using namespace ttkv;
+
+extern "C" size_t ttkv_write_workspace_bytes(const ttkv_layout_t* lay, int32_t n_tok) {
+    if (!lay || n_tok <= 0) return 0;
+    return size_t(n_tok) * lay->r1 * sizeof(float);
+}
+
+extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                const int64_t* slot_mapping, int32_t n_tok, const void* k,
+                                int32_t k_dtype, int64_t k_stride, const void* v, int32_t v_dtype,
+                                int64_t v_stride, const int32_t* tok_dec, const float* decoders,
+                                int64_t dec_stride, const float* pinvs, int64_t pinv_stride,
+                                int32_t n_decoders, const int8_t* coeff_q, const float* coeff_scale,
+                                void* workspace, size_t workspace_bytes, int32_t* status,
+                                void* stream) {
+    if (!lay) return fail(TTKV_ERR_ARG, "layout is null");
+    if (lay->d != kHeadDim) return fail(TTKV_ERR_UNSUPPORTED, "head dim %d: d=128 only", lay->d);
+    if (lay->qbits != 8) return fail(TTKV_ERR_UNSUPPORTED, "qbits=%d: coefficients are int8", lay->qbits);
+    if (lay->r1 > kMaxRank) return fail(TTKV_ERR_UNSUPPORTED, "r1=%d > %d", lay->r1, kMaxRank);
+    if (lay->H > 8) return fail(TTKV_ERR_UNSUPPORTED, "H=%d > 8 KV heads", lay->H);
+    if (lay->res_k < 1 || lay->res_bits < 2 || lay->v_bits < 2 || lay->res_bits > 8 || lay->v_bits > 8)
+        return fail(TTKV_ERR_UNSUPPORTED, "lane widths res_k=%d res_bits=%d v_bits=%d", lay->res_k,
+                    lay->res_bits, lay->v_bits);
+    if (int e = check_cache(cache, lay->blob_bytes)) return e;
+    if (n_tok < 0) return fail(TTKV_ERR_ARG, "n_tok < 0");
+    if (n_tok == 0) return TTKV_OK;
+    if (!slot_mapping || !k || !v) return fail(TTKV_ERR_ARG, "slot_mapping/k/v null");
+    if (k_dtype < TTKV_F32 || k_dtype > TTKV_BF16 || v_dtype < TTKV_F32 || v_dtype > TTKV_BF16)
+        return fail(TTKV_ERR_ARG, "k/v dtype");
+    if (k_stride < int64_t(lay->H) * 128 || v_stride < int64_t(lay->H) * 128)
+        return fail(TTKV_ERR_ARG, "k/v stride below H*d");
+    const bool frozen = pinvs != nullptr;
+    if (!decoders || !tok_dec || n_decoders < 1) return fail(TTKV_ERR_ARG, "decoders/tok_dec missing");
+    if (dec_stride < int64_t(lay->r1) * lay->H * 128) return fail(TTKV_ERR_ARG, "decoder stride");
+    if (frozen && pinv_stride < int64_t(lay->r1) * lay->H * 128) return fail(TTKV_ERR_ARG, "pinv stride");
+    if (!frozen && (!coeff_q || !coeff_scale)) return fail(TTKV_ERR_ARG, "coeff_q/coeff_scale null");
+    if (frozen && (!workspace || workspace_bytes < ttkv_write_workspace_bytes(lay, n_tok)))
+        return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes,
+                    ttkv_write_workspace_bytes(lay, n_tok));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* c = nullptr;
+    if (frozen) {
+        ProjParams pp{};
+        pp.H = lay->H; pp.r1 = lay->r1; pp.k = k; pp.k_dtype = k_dtype; pp.k_stride = k_stride;
+        pp.tok_dec = tok_dec; pp.pinvs = pinvs; pp.pinv_stride = pinv_stride; pp.n_decoders = n_decoders;
+        c = reinterpret_cast<float*>(workspace);
+        pp.c = c; pp.status = status;
+        dim3 grid((lay->r1 + PROJ_WARPS - 1) / PROJ_WARPS, n_tok);
+        project_kernel<<<grid, PROJ_WARPS * 32, 0, st>>>(pp);
+        if (int e = check_launch("project_kernel")) return e;
+    }
+    EncParams ep{};
+    ep.H = lay->H; ep.r1 = lay->r1; ep.res_k = lay->res_k; ep.res_bits = lay->res_bits;
+    ep.v_lanes = lay->v_lanes; ep.v_bits = lay->v_bits; ep.coeff_bytes = lay->coeff_bytes;
+    ep.k_row = lay->k_row_bytes; ep.v_row = lay->v_row_bytes; ep.v_offset = lay->v_offset;
+    ep.cache = cache->base; ep.n_slots = cache->n_slots; ep.row_bytes = cache->row_bytes;
+    ep.slots = slot_mapping; ep.k = k; ep.k_dtype = k_dtype; ep.k_stride = k_stride;
+    ep.v = v; ep.v_dtype = v_dtype; ep.v_stride = v_stride; ep.tok_dec = tok_dec;
+    ep.decoders = decoders; ep.dec_stride = dec_stride; ep.n_decoders = n_decoders;
+    ep.c = c; ep.coeff_q = frozen ? nullptr : coeff_q; ep.coeff_scale = frozen ? nullptr : coeff_scale;
+    ep.status = status;
+    encode_pack_kernel<<<dim3(lay->H, n_tok), 128, 0, st>>>(ep);
+    return check_launch("encode_pack_kernel");
+}
+
+extern "C" int ttkv_select_pack_rows(const ttkv_cache_t* cache, const int64_t* slots, int32_t n_tok,
+                                     const void* x, int32_t x_dtype, int32_t heads, int32_t d,
+                                     int32_t field_off, int32_t row_stride, int32_t lanes,
+                                     int32_t bits, int32_t* status, void* stream) {
+    if (d != kHeadDim) return fail(TTKV_ERR_UNSUPPORTED, "d=%d: rows of 128 lanes only", d);
+    if (lanes < 1 || lanes > d || bits < 2 || bits > 8)
+        return fail(TTKV_ERR_UNSUPPORTED, "lanes=%d bits=%d outside 1..d / 2..8", lanes, bits);
+    if (heads < 1 || n_tok < 0 || field_off < 0 || row_stride < 0) return fail(TTKV_ERR_ARG, "shape");
+    const int need = field_off + (heads - 1) * row_stride + d / 8 + packed_row_bytes(lanes, bits) + 2;
+    if (int e = check_cache(cache, need)) return e;
+    if (n_tok == 0) return TTKV_OK;
+    if (!slots || !x) return fail(TTKV_ERR_ARG, "slots/x null");
+    if (x_dtype < TTKV_F32 || x_dtype > TTKV_BF16) return fail(TTKV_ERR_ARG, "x dtype");
+    RowsParams p{};
+    p.cache = cache->base; p.n_slots = cache->n_slots; p.row_bytes = cache->row_bytes;
+    p.slots = slots; p.n_tok = n_tok; p.heads = heads; p.field_off = field_off;
+    p.row_stride = row_stride; p.lanes = lanes; p.bits = bits; p.x = x; p.x_dtype = x_dtype;
+    p.status = status;
+    const int64_t rows = int64_t(n_tok) * heads;
+    select_rows_kernel<<<unsigned((rows + 3) / 4), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("select_rows_kernel");
+}
+
+extern "C" size_t ttkv_fit_tail_scratch_bytes(int32_t r, int32_t r2, int32_t H, int32_t d) {
+    if (r < 1 || r2 < 1 || H < 1 || d < 1) return 0;
+    return (size_t(r) * d * r2 + size_t(r2) * H + size_t(r) * H * d) * sizeof(float);
+}
+
+extern "C" int ttkv_fit_tail(const float* G1, const float* G2, const float* G3, int32_t n, int32_t r,
+                             int32_t r2, int32_t H, int32_t d, int32_t qbits, int32_t budget,
+                             int8_t* coeff_q, float* coeff_scale, int8_t* dec_q, uint16_t* dec_scale,
+                             float* decoder, void* scratch, size_t scratch_bytes, void* stream) {
+    if (qbits != 8) return fail(TTKV_ERR_UNSUPPORTED, "qbits=%d: the fit tail quantises to int8", qbits);
+    if (!G1 || !G2 || !G3 || !coeff_q || !coeff_scale || !dec_q || !dec_scale || !decoder)
+        return fail(TTKV_ERR_ARG, "null pointer");
+    if (n < 1 || r < 1 || r2 < 1 || H < 1 || d < 1 || budget < r)
+        return fail(TTKV_ERR_ARG, "shape n=%d r=%d r2=%d H=%d d=%d budget=%d", n, r, r2, H, d, budget);
+    if (!scratch || scratch_bytes < ttkv_fit_tail_scratch_bytes(r, r2, H, d))
+        return fail(TTKV_ERR_WORKSPACE, "scratch %zu < %zu bytes", scratch_bytes,
+                    ttkv_fit_tail_scratch_bytes(r, r2, H, d));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* G2q = reinterpret_cast<float*>(scratch);
+    float* G3q = G2q + size_t(r) * d * r2;
+    float* dec = G3q + size_t(r2) * H;
+    quant_coeff_kernel<<<n, 32, 0, st>>>(G1, n, r, budget, coeff_q, coeff_scale);
+    if (int e = check_launch("quant_coeff_kernel")) return e;
+    quant_core_rows_kernel<<<r, 32, 0, st>>>(G2, d * r2, G2q);
+    if (int e = check_launch("quant_core_rows_kernel(G2)")) return e;
+    quant_core_rows_kernel<<<r2, 32, 0, st>>>(G3, H, G3q);
+    if (int e = check_launch("quant_core_rows_kernel(G3)")) return e;
+    decoder_contract_kernel<<<r, 256, 0, st>>>(G2q, G3q, r2, H, d, dec);
+    if (int e = check_launch("decoder_contract_kernel")) return e;
+    decoder_quant_kernel<<<budget, 256, 0, st>>>(dec, r, budget, H * d, dec_q, dec_scale, decoder);
+    return check_launch("decoder_quant_kernel");
+}

@@ -1,0 +1,285 @@
+"""torch-facing wrappers of the C ABI: device tensors in, launches on torch's current stream.
+
+Every function validates shapes and dtypes on the host, hands raw pointers to
+`libttkv_sm100.so`, and never reads a device value back. Device-side refusals (a block index
+outside the cache, a PAD_SLOT_ID slot, a decoder index outside the pool) land in a per-device
+status word; `check_status()` reads it once (one readback) and raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from vllm_ttkv import _lib
+from vllm_ttkv.layout import TTKLayout
+
+_DTYPE = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+_STATUS: dict = {}
+_WORKSPACE: dict = {}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE[t.dtype]
+    except KeyError:
+        raise TypeError(f"dtype {t.dtype} is not one of float32/float16/bfloat16") from None
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"expected a CUDA tensor, got one on {t.device}: the TT-KV ops run "
+                             f"only on the GPU (no CPU path)")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def status_word(device=None) -> torch.Tensor:
+    """The per-device int32 status the kernels report device-side refusals into."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    t = _STATUS.get(dev)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _STATUS[dev] = t
+    return t
+
+
+def reset_status(device=None) -> None:
+    status_word(device).zero_()
+
+
+def check_status(device=None) -> None:
+    """Read the status word (a device readback) and raise if a kernel recorded a refusal."""
+    code = int(status_word(device).item())
+    if code:
+        reset_status(device)
+        msg = _lib.STATUS.get(code, f"code {code}")
+        if code in (1, 4):
+            raise IndexError(f"vllm_ttkv: {msg}")
+        raise RuntimeError(f"vllm_ttkv: {msg}")
+
+
+def workspace(nbytes: int, device, key="read") -> torch.Tensor:
+    """A cached byte buffer of at least `nbytes` (grown, never shrunk) for kernel scratch."""
+    dev = torch.device(device)
+    buf = _WORKSPACE.get((dev, key))
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
+        _WORKSPACE[(dev, key)] = buf
+    return buf
+
+
+def byte_view(cache: torch.Tensor) -> torch.Tensor:
+    """`[n_slots, row_bytes]` uint8 view of a layer's page `[blocks, (1,) block_size, C]` in any
+    dtype (vLLM allocates it in the model dtype with C counted in elements,
+    vllm_ttkv/decode.py:125-157)."""
+    c = cache
+    if c.dim() == 4:
+        if c.shape[1] != 1:
+            raise ValueError(f"expected num_head_slots=1, got a cache of shape {tuple(c.shape)}")
+        c = c[:, 0]
+    if c.dim() != 3:
+        raise ValueError(f"expected a [num_blocks, block_size, C] page, got {tuple(cache.shape)}")
+    try:
+        u8 = c if c.dtype == torch.uint8 else c.view(torch.uint8)
+    except RuntimeError as e:
+        raise RuntimeError(f"the cache page {tuple(cache.shape)} {cache.dtype} cannot be viewed as "
+                           f"bytes ({e})") from e
+    if not u8.is_contiguous():
+        raise ValueError("the cache page must be contiguous")
+    return u8.reshape(-1, u8.shape[-1])
+
+
+def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int) -> _lib.Cache:
+    if flat.dtype != torch.uint8 or flat.dim() != 2:
+        raise ValueError("cache must be a [n_slots, row_bytes] uint8 view")
+    if flat.shape[1] < lay.compressed_bytes_per_token():
+        raise ValueError(f"cache rows are {flat.shape[1]} bytes, the layout needs "
+                         f"{lay.compressed_bytes_per_token()}")
+    return _lib.Cache(flat.data_ptr(), flat.shape[0], flat.stride(0), block_size)
+
+
+def _batch_struct(block_table, seq_lens, decoders, dec_index) -> _lib.Batch:
+    for name, t, dt in (("block_table", block_table, torch.int32), ("seq_lens", seq_lens, torch.int32),
+                        ("dec_index", dec_index, torch.int32), ("decoders", decoders, torch.float32)):
+        if t.dtype != dt:
+            raise TypeError(f"{name} must be {dt}, got {t.dtype}")
+    if block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise ValueError("block_table must be [n_reqs, max_blocks] with unit column stride")
+    if decoders.dim() != 3 or not decoders.is_contiguous():
+        raise ValueError("decoders must be a contiguous [n_decoders, r1, H*d] float32 pool")
+    n = block_table.shape[0]
+    if seq_lens.numel() < n or dec_index.numel() < n:
+        raise ValueError("seq_lens / dec_index shorter than the block table")
+    return _lib.Batch(block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+                      seq_lens.data_ptr(), n, decoders.data_ptr(), decoders.stride(0),
+                      dec_index.data_ptr(), decoders.shape[0])
+
+
+def _rope_struct(table: torch.Tensor) -> _lib.Rope:
+    if table.dim() != 2 or table.shape[1] != 128 or not table.is_contiguous():
+        raise ValueError(f"the RoPE table must be a contiguous [max_pos, 128] cos||sin table, got "
+                         f"{tuple(table.shape)} (partial rotary is refused, vllm_ttkv/decode.py:92)")
+    return _lib.Rope(table.data_ptr(), dtype_code(table), table.shape[0])
+
+
+def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_table: torch.Tensor,
+                 seq_lens: torch.Tensor, decoders: torch.Tensor, dec_index: torch.Tensor,
+                 table: torch.Tensor, q: torch.Tensor, scale: float, out: torch.Tensor,
+                 max_seq_len: int, head_lo: int = 0, head_hi: int | None = None,
+                 status: torch.Tensor | None = None) -> torch.Tensor:
+    """Batched decode read: q [B, HQ, d] (row r = request r) -> out [B, HQ, d] (heads of the KV
+    heads [head_lo, head_hi) written). `cache` is the [n_slots, row_bytes] uint8 view."""
+    _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q, out)
+    head_hi = lay.H if head_hi is None else head_hi
+    B, HQ, d = q.shape
+    if d != 128 or q.stride(2) != 1 or q.stride(1) != 128 or out.stride(2) != 1 or out.stride(1) != 128:
+        raise ValueError("q / out must be [B, HQ, 128] with contiguous rows")
+    if out.shape[0] < B or block_table.shape[0] != B:
+        raise ValueError(f"{B} queries, {block_table.shape[0]} block-table rows, {out.shape[0]} outputs")
+    L = _lib.lib()
+    la = lay.abi()
+    ws_n = L.ttkv_decode_workspace_bytes(C.byref(la), B, HQ, max_seq_len, head_lo, head_hi)
+    ws = workspace(ws_n, q.device)
+    st = status if status is not None else status_word(q.device)
+    c_s = _cache_struct(lay, cache, block_size)
+    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index)
+    r_s = _rope_struct(table)
+    _lib.check(L.ttkv_decode_paged(
+        C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),
+        q.stride(0), HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
+        out.stride(0), int(max_seq_len), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+    return out
+
+
+def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
+                       block_table: torch.Tensor, seq_lens: torch.Tensor, decoders: torch.Tensor,
+                       dec_index: torch.Tensor, table: torch.Tensor, q_start: torch.Tensor,
+                       q_len: torch.Tensor, q: torch.Tensor, scale: float, out: torch.Tensor,
+                       max_q_len: int, max_seq_len: int, head_lo: int = 0,
+                       head_hi: int | None = None, status: torch.Tensor | None = None):
+    """Continuation read: request r's queries are rows q_start[r] .. +q_len[r] of q [N, HQ, d],
+    at positions seq_len - q_len + j, causal over the stored rows."""
+    _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q_start, q_len, q, out)
+    head_hi = lay.H if head_hi is None else head_hi
+    N, HQ, d = q.shape
+    if d != 128 or q.stride(2) != 1 or q.stride(1) != 128 or out.stride(2) != 1 or out.stride(1) != 128:
+        raise ValueError("q / out must be [N, HQ, 128] with contiguous rows")
+    for name, t in (("q_start", q_start), ("q_len", q_len)):
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32")
+    L = _lib.lib()
+    la = lay.abi()
+    B = block_table.shape[0]
+    ws_n = L.ttkv_prefill_workspace_bytes(C.byref(la), B, HQ, max_q_len, max_seq_len, head_lo, head_hi)
+    ws = workspace(ws_n, q.device)
+    st = status if status is not None else status_word(q.device)
+    c_s = _cache_struct(lay, cache, block_size)
+    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index)
+    r_s = _rope_struct(table)
+    _lib.check(L.ttkv_prefill_cont_paged(
+        C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q_start.data_ptr(), q_len.data_ptr(),
+        q.data_ptr(), dtype_code(q), q.stride(0), HQ, float(scale), head_lo, head_hi,
+        out.data_ptr(), dtype_code(out), out.stride(0), int(max_q_len), int(max_seq_len),
+        ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+    return out
+
+
+def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor, k: torch.Tensor,
+                v: torch.Tensor, tok_dec: torch.Tensor, decoders: torch.Tensor,
+                pinvs: torch.Tensor | None = None, coeff_q: torch.Tensor | None = None,
+                coeff_scale: torch.Tensor | None = None, status: torch.Tensor | None = None):
+    """Encode tokens k/v [n, H, d] (raw pre-RoPE K; V) into their slots.
+
+    Frozen path: `pinvs` [n_dec, r1, H*d] (pinv transposed) given -> project + quantise.
+    Fit path: `coeff_q` [n, r1] int8 and `coeff_scale` [n] float32 given."""
+    _need_cuda(cache, slot_mapping, k, v, tok_dec, decoders)
+    n = slot_mapping.numel()
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise TypeError("slot_mapping must be contiguous int64")
+    for name, t in (("k", k), ("v", v)):
+        if t.dim() != 3 or t.shape[1:] != (lay.H, lay.d) or t.stride(2) != 1 or t.stride(1) != lay.d:
+            raise ValueError(f"{name} must be [n, {lay.H}, {lay.d}] with contiguous rows, got "
+                             f"{tuple(t.shape)}")
+        if t.shape[0] < n:
+            raise ValueError(f"{name} holds {t.shape[0]} tokens for {n} slot ids")
+    if tok_dec.dtype != torch.int32 or tok_dec.numel() < n:
+        raise TypeError("tok_dec must be int32 with one entry per token")
+    if decoders.dtype != torch.float32 or decoders.dim() != 3 or not decoders.is_contiguous():
+        raise TypeError("decoders must be a contiguous float32 [n_dec, r1, H*d] pool")
+    L = _lib.lib()
+    la = lay.abi()
+    st = status if status is not None else status_word(k.device)
+    c_s = _cache_struct(lay, cache, 1)
+    ws_n = L.ttkv_write_workspace_bytes(C.byref(la), n)
+    ws = workspace(ws_n, k.device, key="write")
+    if pinvs is not None:
+        if pinvs.shape != decoders.shape or not pinvs.is_contiguous() or pinvs.dtype != torch.float32:
+            raise ValueError("pinvs must match the decoder pool's shape, contiguous float32")
+        pv, pv_stride, cq, cs = pinvs.data_ptr(), pinvs.stride(0), None, None
+    else:
+        if coeff_q is None or coeff_scale is None:
+            raise ValueError("the fit path needs coeff_q and coeff_scale")
+        if coeff_q.dtype != torch.int8 or coeff_q.shape != (n, lay.r1) or not coeff_q.is_contiguous():
+            raise ValueError(f"coeff_q must be contiguous int8 [{n}, {lay.r1}]")
+        if coeff_scale.dtype != torch.float32 or coeff_scale.numel() != n:
+            raise ValueError("coeff_scale must be float32 [n]")
+        pv, pv_stride, cq, cs = None, 0, coeff_q.data_ptr(), coeff_scale.contiguous().data_ptr()
+    _lib.check(L.ttkv_write_paged(
+        C.byref(la), C.byref(c_s), slot_mapping.data_ptr(), n, k.data_ptr(), dtype_code(k),
+        k.stride(0), v.data_ptr(), dtype_code(v), v.stride(0), tok_dec.data_ptr(),
+        decoders.data_ptr(), decoders.stride(0), pv, pv_stride, decoders.shape[0], cq, cs,
+        ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+
+
+def select_pack_rows(cache: torch.Tensor, slots: torch.Tensor, x: torch.Tensor, *, field_off: int,
+                     row_stride: int, lanes: int, bits: int, heads: int, d: int,
+                     status: torch.Tensor | None = None):
+    """`select_triton.write_rows`' contract: x [heads*n_tok, d] in (head, token) order."""
+    _need_cuda(cache, slots, x)
+    if x.dim() != 2 or x.shape[1] != d or not x.is_contiguous():
+        raise ValueError(f"x must be a contiguous [rows, {d}] tensor")
+    n_tok = slots.numel()
+    if x.shape[0] != n_tok * heads:
+        raise ValueError(f"{x.shape[0]} rows for {n_tok} tokens and {heads} heads")
+    sl = slots.to(torch.int64).contiguous()
+    st = status if status is not None else status_word(x.device)
+    c_s = _lib.Cache(cache.data_ptr(), cache.shape[0], cache.stride(0), 1)
+    _lib.check(_lib.lib().ttkv_select_pack_rows(
+        C.byref(c_s), sl.data_ptr(), n_tok, x.data_ptr(), dtype_code(x), heads, d, field_off,
+        row_stride, lanes, bits, st.data_ptr(), _stream()))
+
+
+def fit_tail(G1, G2, G3, budget: int, qbits: int = 8):
+    """Everything build_k_layer does after the SVDs, on the device.
+
+    G1 [n, r], G2 [r, d, r2], G3 [r2, H] float32 -> dict(coeff_q int8 [n, budget], coeff_scale
+    float32 [n], dec_q int8 [r, H*d], dec_scale float16 [r], decoder float32 [budget, H*d])."""
+    _need_cuda(G1, G2, G3)
+    G1, G2, G3 = (t.float().contiguous() for t in (G1, G2, G3))
+    n, r = G1.shape
+    r_, d, r2 = G2.shape
+    H = G3.shape[1]
+    if r_ != r or G3.shape[0] != r2:
+        raise ValueError("core shapes disagree")
+    dev = G1.device
+    out = dict(coeff_q=torch.empty(n, budget, dtype=torch.int8, device=dev),
+               coeff_scale=torch.empty(n, dtype=torch.float32, device=dev),
+               dec_q=torch.empty(r, H * d, dtype=torch.int8, device=dev),
+               dec_scale=torch.empty(r, dtype=torch.float16, device=dev),
+               decoder=torch.empty(budget, H * d, dtype=torch.float32, device=dev))
+    L = _lib.lib()
+    nb = L.ttkv_fit_tail_scratch_bytes(r, r2, H, d)
+    scratch = workspace(nb, dev, key="fit")
+    _lib.check(L.ttkv_fit_tail(
+        G1.data_ptr(), G2.data_ptr(), G3.data_ptr(), n, r, r2, H, d, qbits, budget,
+        out["coeff_q"].data_ptr(), out["coeff_scale"].data_ptr(), out["dec_q"].data_ptr(),
+        out["dec_scale"].data_ptr(), out["decoder"].data_ptr(), scratch.data_ptr(), scratch.numel(),
+        _stream()))
+    return out
