@@ -39,11 +39,33 @@ __device__ __forceinline__ void store_elt(void* p, int dtype, int64_t i, float v
     else reinterpret_cast<float*>(p)[i] = v;
 }
 
+// fp32 -> IEEE fp16 bit pattern (round to nearest even), zero-extended into a 32-bit integer
+// register inside the asm. Splitting the bits into bytes from a 16-bit half-typed register is
+// not safe: a byte store from such a register was compiled as a numeric f16 -> u8 conversion
+// (the low byte came out as the truncated value, e.g. 0x01 for 1.24), so the bit pattern only
+// ever leaves this function as a plain u32.
+__device__ __forceinline__ uint32_t f16_bits(float x) {
+    uint32_t r;
+    asm("{\n\t.reg .b16 h;\n\tcvt.rn.f16.f32 h, %1;\n\tcvt.u32.u16 %0, h;\n\t}" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits) {
+    float x;
+    asm("{\n\t.reg .b16 h;\n\tcvt.u16.u32 h, %1;\n\tcvt.f32.f16 %0, h;\n\t}" : "=f"(x) : "r"(bits));
+    return x;
+}
+
 // An fp16 stored as two little-endian bytes at any (possibly odd) byte offset
 // (vllm_ttkv/layout.py:181,191 write `scale.view(uint8)`).
 __device__ __forceinline__ float f16_at(const uint8_t* p) {
-    const uint16_t bits = uint16_t(p[0]) | (uint16_t(p[1]) << 8);
-    return __half2float(__ushort_as_half(bits));
+    return f16_bits_to_f32(uint32_t(p[0]) | (uint32_t(p[1]) << 8));
+}
+
+__device__ __forceinline__ void store_f16_bytes(uint8_t* p, float x) {
+    const uint32_t b = f16_bits(x);
+    p[0] = uint8_t(b & 0xffu);
+    p[1] = uint8_t((b >> 8) & 0xffu);
 }
 
 // 32 lanes of an MSB-first bitmap as one word with lane l at bit 31-l: bytes are read in

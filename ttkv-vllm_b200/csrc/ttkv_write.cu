@@ -111,11 +111,7 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
         }
         dst[16 + by] = uint8_t(v);
     }
-    if (L == 0) {
-        const uint16_t h = __half_as_ushort(__float2half_rn(sc));
-        dst[16 + pb] = uint8_t(h & 0xff);
-        dst[16 + pb + 1] = uint8_t(h >> 8);
-    }
+    if (L == 0) store_f16_bytes(dst + 16 + pb, sc);
     __syncwarp();
 }
 
@@ -265,11 +261,7 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
     } else if (w == 2 && h == 0) {
         // the coefficient block and its fp16 ruler, once per token (encode.py:570-573)
         for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
-        if (L == 0) {
-            const uint16_t hb = __half_as_ushort(__float2half_rn(cs_s));
-            row[P.coeff_bytes] = uint8_t(hb & 0xff);
-            row[P.coeff_bytes + 1] = uint8_t(hb >> 8);
-        }
+        if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs_s);
     }
 }
 
@@ -372,14 +364,14 @@ __global__ void __launch_bounds__(256) decoder_quant_kernel(const float* dec, in
     }
     __syncthreads();
     const float sc = sc_s;
-    const __half sh = __float2half_rn(sc);
-    const float sf = __half2float(sh);
+    const uint32_t sh = f16_bits(sc);
+    const float sf = f16_bits_to_f32(sh);
     for (int i = threadIdx.x; i < cols; i += blockDim.x) {
         const float qf = fminf(fmaxf(rintf(__fdiv_rn(dec[int64_t(a) * cols + i], sc)), -128.f), 127.f);
         dec_q[int64_t(a) * cols + i] = int8_t(qf);
         decoder[int64_t(a) * cols + i] = qf * sf;
     }
-    if (threadIdx.x == 0) dec_scale[a] = __half_as_ushort(sh);
+    if (threadIdx.x == 0) dec_scale[a] = uint16_t(sh);
 }
 
 int check_cache(const ttkv_cache_t* cache, int need) {

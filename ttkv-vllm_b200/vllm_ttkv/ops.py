@@ -96,6 +96,16 @@ def byte_view(cache: torch.Tensor) -> torch.Tensor:
     return u8.reshape(-1, u8.shape[-1])
 
 
+def _row_stride(t: torch.Tensor, name: str) -> int:
+    """Stride between tokens of a [n, heads, 128] tensor whose [heads, 128] rows are contiguous.
+    Size-1 dimensions may carry any stride (numpy views and broadcasts produce those)."""
+    if t.dim() != 3 or t.shape[2] != 128:
+        raise ValueError(f"{name} must be [n, heads, 128], got {tuple(t.shape)}")
+    if (t.shape[2] > 1 and t.stride(2) != 1) or (t.shape[1] > 1 and t.stride(1) != 128):
+        raise ValueError(f"{name} must have contiguous [heads, 128] rows (strides {t.stride()})")
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1] * 128
+
+
 def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int) -> _lib.Cache:
     if flat.dtype != torch.uint8 or flat.dim() != 2:
         raise ValueError("cache must be a [n_slots, row_bytes] uint8 view")
@@ -139,8 +149,7 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
     _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q, out)
     head_hi = lay.H if head_hi is None else head_hi
     B, HQ, d = q.shape
-    if d != 128 or q.stride(2) != 1 or q.stride(1) != 128 or out.stride(2) != 1 or out.stride(1) != 128:
-        raise ValueError("q / out must be [B, HQ, 128] with contiguous rows")
+    qs, os_ = _row_stride(q, "q"), _row_stride(out, "out")
     if out.shape[0] < B or block_table.shape[0] != B:
         raise ValueError(f"{B} queries, {block_table.shape[0]} block-table rows, {out.shape[0]} outputs")
     L = _lib.lib()
@@ -153,8 +162,8 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
     r_s = _rope_struct(table)
     _lib.check(L.ttkv_decode_paged(
         C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),
-        q.stride(0), HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
-        out.stride(0), int(max_seq_len), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+        qs, HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
+        os_, int(max_seq_len), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
     return out
 
 
@@ -169,8 +178,7 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
     _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q_start, q_len, q, out)
     head_hi = lay.H if head_hi is None else head_hi
     N, HQ, d = q.shape
-    if d != 128 or q.stride(2) != 1 or q.stride(1) != 128 or out.stride(2) != 1 or out.stride(1) != 128:
-        raise ValueError("q / out must be [N, HQ, 128] with contiguous rows")
+    qs, os_ = _row_stride(q, "q"), _row_stride(out, "out")
     for name, t in (("q_start", q_start), ("q_len", q_len)):
         if t.dtype != torch.int32:
             raise TypeError(f"{name} must be int32")
@@ -185,8 +193,8 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
     r_s = _rope_struct(table)
     _lib.check(L.ttkv_prefill_cont_paged(
         C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q_start.data_ptr(), q_len.data_ptr(),
-        q.data_ptr(), dtype_code(q), q.stride(0), HQ, float(scale), head_lo, head_hi,
-        out.data_ptr(), dtype_code(out), out.stride(0), int(max_q_len), int(max_seq_len),
+        q.data_ptr(), dtype_code(q), qs, HQ, float(scale), head_lo, head_hi,
+        out.data_ptr(), dtype_code(out), os_, int(max_q_len), int(max_seq_len),
         ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
     return out
 
@@ -204,9 +212,9 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
         raise TypeError("slot_mapping must be contiguous int64")
     for name, t in (("k", k), ("v", v)):
-        if t.dim() != 3 or t.shape[1:] != (lay.H, lay.d) or t.stride(2) != 1 or t.stride(1) != lay.d:
-            raise ValueError(f"{name} must be [n, {lay.H}, {lay.d}] with contiguous rows, got "
-                             f"{tuple(t.shape)}")
+        if t.dim() != 3 or t.shape[1:] != (lay.H, lay.d):
+            raise ValueError(f"{name} must be [n, {lay.H}, {lay.d}], got {tuple(t.shape)}")
+        _row_stride(t, name)
         if t.shape[0] < n:
             raise ValueError(f"{name} holds {t.shape[0]} tokens for {n} slot ids")
     if tok_dec.dtype != torch.int32 or tok_dec.numel() < n:
@@ -233,7 +241,7 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
         pv, pv_stride, cq, cs = None, 0, coeff_q.data_ptr(), coeff_scale.contiguous().data_ptr()
     _lib.check(L.ttkv_write_paged(
         C.byref(la), C.byref(c_s), slot_mapping.data_ptr(), n, k.data_ptr(), dtype_code(k),
-        k.stride(0), v.data_ptr(), dtype_code(v), v.stride(0), tok_dec.data_ptr(),
+        _row_stride(k, "k"), v.data_ptr(), dtype_code(v), _row_stride(v, "v"), tok_dec.data_ptr(),
         decoders.data_ptr(), decoders.stride(0), pv, pv_stride, decoders.shape[0], cq, cs,
         ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
 
