@@ -134,6 +134,30 @@ int ttkv_decode_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
                       int32_t max_seq_len, void* workspace, size_t workspace_bytes,
                       int32_t* status, void* stream);
 
+/* ---------------------------------------------------------------- decode, allocation-free
+ * No counterpart in the reference: an addition of this library.
+ * The same decode as ttkv_decode_paged for callers that cannot hand the library scratch memory:
+ * hosts that reach it only through this C ABI and have no device allocator of their own (a C or
+ * C++ runtime, an FFI binding without torch), and engines that fix their device-memory budget up
+ * front (vLLM sizes its KV cache from the memory left after a profiling pass, so memory taken
+ * outside its pool mid-serving can push a later allocation out of memory). The split-K partials
+ * go to a static device array of TTKV_NOALLOC_SCRATCH_BYTES that every GPU loading the library
+ * holds until the process exits; the call allocates nothing.
+ *   - a decode needing more scratch than that (ttkv_decode_workspace_bytes) is refused with
+ *     TTKV_ERR_WORKSPACE before any launch;
+ *   - the first call on a device looks up that device's copy of the array (once, with the
+ *     calling thread's current device); make that first call before any stream capture;
+ *   - every call on a device shares the one array and it keeps the last call's contents (every
+ *     byte a launch reads it has written first, so nothing is cleared); calls that can overlap
+ *     on the GPU (two streams, two threads) race on it, so the caller serialises them. */
+#define TTKV_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                              const ttkv_batch_t* batch, const ttkv_rope_t* rope,
+                              const void* q, int32_t q_dtype, int64_t q_stride, int32_t HQ,
+                              float scale, int32_t head_lo, int32_t head_hi,
+                              void* out, int32_t out_dtype, int64_t out_stride,
+                              int32_t max_seq_len, int32_t* status, void* stream);
+
 /* ---------------------------------------------------------------- read: continuation
  * Multi-query read for chunked-prefill / prefix-cache continuations: request r has q_len[r]
  * query tokens at q + (q_start[r] + j)*q_stride, [HQ, d] each, at absolute positions

@@ -19,6 +19,7 @@
 // krt_triton.py:155-266 / v_out_triton.py:159-246 for the continuation, fused and batched.
 #include <cfloat>
 #include <cmath>
+#include <mutex>
 
 #include "ttkv_common.cuh"
 
@@ -603,4 +604,55 @@ extern "C" int ttkv_prefill_cont_paged(const ttkv_layout_t* lay, const ttkv_cach
     return read_entry(true, lay, cache, batch, rope, q_start, q_len, q, q_dtype, q_stride, HQ, scale,
                       head_lo, head_hi, out, out_dtype, out_stride, max_q_len, max_seq_len,
                       workspace, workspace_bytes, status, stream);
+}
+
+// ------------------------------------------------------------------ decode, allocation-free
+// The split-K partials of ttkv_decode_paged_noalloc: a file-scope device array, one copy per GPU
+// that loads the library. Host code must not take its address directly (that is a host-side
+// stand-in); the device address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_decode_scratch[TTKV_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+
+int noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* ptrs[kMaxDevices] = {};
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(TTKV_ERR_UNSUPPORTED, "device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(TTKV_ERR_CUDA, "cudaGetSymbolAddress(decode scratch) on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return TTKV_OK;
+}
+}  // namespace
+
+extern "C" int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                         const ttkv_batch_t* batch, const ttkv_rope_t* rope,
+                                         const void* q, int32_t q_dtype, int64_t q_stride,
+                                         int32_t HQ, float scale, int32_t head_lo, int32_t head_hi,
+                                         void* out, int32_t out_dtype, int64_t out_stride,
+                                         int32_t max_seq_len, int32_t* status, void* stream) {
+    if (int e = check_common(lay, cache, batch, rope, HQ, head_lo, head_hi)) return e;
+    const size_t need = ttkv_decode_workspace_bytes(lay, batch->n_reqs, HQ, max_seq_len, head_lo, head_hi);
+    if (need > size_t(TTKV_NOALLOC_SCRATCH_BYTES))
+        return fail(TTKV_ERR_WORKSPACE,
+                    "this decode (%d requests, max_seq_len %d, HQ %d) needs %zu bytes of scratch but "
+                    "the allocation-free entry point has %u (TTKV_NOALLOC_SCRATCH_BYTES); call "
+                    "ttkv_decode_paged with a workspace instead",
+                    batch->n_reqs, max_seq_len, HQ, need, TTKV_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    if (int e = noalloc_scratch(&scratch)) return e;
+    return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ,
+                      scale, head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, scratch,
+                      size_t(TTKV_NOALLOC_SCRATCH_BYTES), status, stream);
 }

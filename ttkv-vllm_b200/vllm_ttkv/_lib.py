@@ -21,6 +21,7 @@ STATUS = {0: "ok", 1: "block index outside the cache", 2: "block-table row too s
           5: "query range inconsistent with seq_len"}
 
 F32, F16, BF16 = 0, 1, 2
+NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024   # TTKV_NOALLOC_SCRATCH_BYTES
 
 
 class Layout(C.Structure):
@@ -56,6 +57,8 @@ SIGNATURES = {
     "ttkv_decode_workspace_bytes": (SZ, [LP, I32, I32, I32, I32, I32]),
     "ttkv_decode_paged": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P, I32, I64,
                                     I32, P, SZ, P, P]),
+    "ttkv_decode_paged_noalloc": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P,
+                                            I32, I64, I32, P, P]),
     "ttkv_prefill_workspace_bytes": (SZ, [LP, I32, I32, I32, I32, I32, I32]),
     "ttkv_prefill_cont_paged": (C.c_int, [LP, CP, BP, RP, P, P, P, I32, I64, I32, F, I32, I32,
                                           P, I32, I64, I32, I32, P, SZ, P, P]),
