@@ -48,6 +48,7 @@ extern "C" {
 #define TTKV_STATUS_DECODER 3      /* a decoder index outside [0, n_decoders) */
 #define TTKV_STATUS_SLOT_RANGE 4   /* a slot id < 0 (PAD_SLOT_ID) or >= n_slots on a write */
 #define TTKV_STATUS_QUERY 5        /* q_len > seq_len, or a query range outside the batch */
+#define TTKV_STATUS_TIMEOUT 6      /* a bounded wait on the tensor-core pipeline ran out */
 
 /* element types */
 #define TTKV_F32 0

@@ -17,6 +17,7 @@
 // This is vllm_ttkv/impl.py:511-540 (_decode_one) + krt_triton.py:66-151 (_krt_kernel) +
 // softmax + v_out_triton.py:51-118 (_v_out_kernel) for the decode, and impl.py:725-778 with
 // krt_triton.py:155-266 / v_out_triton.py:159-246 for the continuation, fused and batched.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <mutex>
@@ -422,6 +423,8 @@ __global__ void __launch_bounds__(128) merge_kernel(const ReadParams P) {
     store_elt(P.out, P.out_dtype, int64_t(qrow) * P.out_stride + int64_t(head_q) * 128 + lane, v);
 }
 
+#include "ttkv_decode_tc.cuh"
+
 // ------------------------------------------------------------------ host side
 int qblock_for(int G, bool multi) {
     if (!multi) return 1;
@@ -451,6 +454,52 @@ Plan make_plan(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_q, int max_
     pl.part_o_bytes = rows * pl.n_splits * 128 * sizeof(float);
     pl.part_ml_bytes = rows * pl.n_splits * 2 * sizeof(float);
     pl.smem = smem_bytes(lay->r1, G * pl.qb, lay->k_row_bytes, lay->v_row_bytes);
+    return pl;
+}
+
+int sm_count() {
+    static int cached = 0;
+    if (cached) return cached;
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+        cached = n;
+    else
+        cudaGetLastError();                                   // clear; plan for a full B200
+    return cached ? cached : 148;
+}
+
+// Whether the tensor-core decode serves this layout (the fp32 kernel serves the rest).
+bool tc_serves(const ttkv_layout_t* lay, int HQ) {
+    const int G = HQ / lay->H;
+    return lay->d == 128 && lay->qbits == 8 && G >= 1 && G <= kMaxG && lay->r1 <= 192 &&
+           tc::tc_geom(lay, G).smem > 0;
+}
+
+// Splits for the tensor-core decode: one resident CTA per SM, 128-token tiles; minimise
+// (waves x tiles per CTA) with a small charge per extra split.
+Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads) {
+    Plan pl{};
+    const int G = HQ / lay->H;
+    pl.qb = 1;
+    pl.n_qblk = 1;
+    const int tiles = std::max(1, (max_seq + tc::TM - 1) / tc::TM);
+    const int pairs = std::max(1, n_reqs * n_heads);
+    const int sms = sm_count();
+    double best = 1e30;
+    int best_s = 1;
+    for (int s = 1; s <= std::min(tiles, 64); ++s) {
+        const int waves = (pairs * s + sms - 1) / sms;
+        const int per = (tiles + s - 1) / s;
+        const double cost = double(waves) * per + 0.05 * s;
+        if (cost < best) { best = cost; best_s = s; }
+    }
+    pl.chunk = ((tiles + best_s - 1) / best_s) * tc::TM;
+    pl.n_splits = std::max(1, (max_seq + pl.chunk - 1) / pl.chunk);
+    const size_t rows = size_t(n_reqs) * n_heads * G;
+    pl.part_o_bytes = rows * pl.n_splits * 128 * sizeof(float);
+    pl.part_ml_bytes = rows * pl.n_splits * 2 * sizeof(float);
+    pl.smem = size_t(tc::tc_geom(lay, G).smem);
     return pl;
 }
 
@@ -512,6 +561,34 @@ int launch_g(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     return check_launch("merge_kernel");
 }
 
+template <int G>
+int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const Plan& pl, int n_reqs, cudaStream_t st) {
+    auto k = tc::decode_tc_kernel<G>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T.smem) != cudaSuccess)
+        return fail(TTKV_ERR_CUDA, "shared memory %d bytes refused", T.smem);
+    dim3 grid(pl.n_splits, P.n_heads, n_reqs);
+    k<<<grid, tc::NTHR, T.smem, st>>>(P, T);
+    if (int e = check_launch("decode_tc_kernel")) return e;
+    dim3 mg(P.G, P.n_heads, n_reqs);
+    merge_kernel<<<mg, 128, 0, st>>>(P);
+    return check_launch("merge_kernel");
+}
+
+int launch_tc(const ReadParams& P, const ttkv_layout_t* lay, const Plan& pl, int n_reqs, cudaStream_t st) {
+    const tc::TcGeom T = tc::tc_geom(lay, P.G);
+    switch (P.G) {
+        case 1: return launch_tc_g<1>(P, T, pl, n_reqs, st);
+        case 2: return launch_tc_g<2>(P, T, pl, n_reqs, st);
+        case 3: return launch_tc_g<3>(P, T, pl, n_reqs, st);
+        case 4: return launch_tc_g<4>(P, T, pl, n_reqs, st);
+        case 5: return launch_tc_g<5>(P, T, pl, n_reqs, st);
+        case 6: return launch_tc_g<6>(P, T, pl, n_reqs, st);
+        case 7: return launch_tc_g<7>(P, T, pl, n_reqs, st);
+        case 8: return launch_tc_g<8>(P, T, pl, n_reqs, st);
+    }
+    return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
+}
+
 template <bool MULTI>
 int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     switch (P.G) {
@@ -536,7 +613,12 @@ extern "C" size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t 
                                               int32_t max_seq_len, int32_t head_lo, int32_t head_hi) {
     if (!lay || lay->H < 1 || HQ < lay->H || head_hi <= head_lo) return 0;
     const Plan pl = make_plan(lay, n_reqs, HQ, 1, max_seq_len, head_hi - head_lo, false);
-    return pl.part_o_bytes + pl.part_ml_bytes;
+    size_t need = pl.part_o_bytes + pl.part_ml_bytes;
+    if (tc_serves(lay, HQ)) {
+        const Plan pt = make_plan_tc(lay, n_reqs, HQ, max_seq_len, head_hi - head_lo);
+        need = std::max(need, pt.part_o_bytes + pt.part_ml_bytes);
+    }
+    return need;
 }
 
 extern "C" size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
@@ -566,7 +648,10 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                     max_seq_len - 1, (long long)rope->rows);
     if (batch->n_reqs == 0 || max_seq_len == 0) return TTKV_OK;
     const int n_heads = head_hi - head_lo;
-    const Plan pl = make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
+    const bool use_tc = !multi && tc_serves(lay, HQ) &&
+                        (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0;
+    const Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads)
+                           : make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
     if (pl.smem > 227 * 1024) return fail(TTKV_ERR_UNSUPPORTED, "r1=%d needs %zu B of shared memory", lay->r1, pl.smem);
     if (!workspace || ws_bytes < pl.part_o_bytes + pl.part_ml_bytes)
         return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, pl.part_o_bytes + pl.part_ml_bytes);
@@ -579,6 +664,7 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
     P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (use_tc) return launch_tc(P, lay, pl, batch->n_reqs, st);
     return multi ? launch<true>(P, pl, batch->n_reqs, st) : launch<false>(P, pl, batch->n_reqs, st);
 }
 
