@@ -325,10 +325,12 @@ def main():
     torch.cuda.synchronize(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index if world == 1 else local) as clk:
-        ev0.record()
-        run_steps(args.steps)
+        torch.cuda.cudart().cudaProfilerStart()          # a profiler run with
+        ev0.record()                                     # --profile-from-start off sees only
+        run_steps(args.steps)                            # the timed steps
         ev1.record()
         torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStop()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)

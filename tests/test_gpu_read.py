@@ -166,7 +166,7 @@ def test_continuation_with_one_query_equals_decode():
                            d["idx"], d["table"], torch.tensor([0, 1], dtype=torch.int32, device="cuda"),
                            torch.ones(2, dtype=torch.int32, device="cuda"), d["q"], 128 ** -0.5, out,
                            1, 77)
-    np.testing.assert_allclose(out.cpu().numpy(), dec, atol=1e-6)
+    np.testing.assert_allclose(out.cpu().numpy(), dec, atol=1e-5)   # two different kernels
 
 
 def test_block_outside_the_cache_is_refused_on_device():

@@ -328,22 +328,36 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const bool valid = tok < t_end;
         const unsigned char* srow = st + tid * T.srow;
 
-        // ---- A: this token's coefficients as fp16, zero past r1 (and for an invalid token)
-        for (int cidx = 0; cidx < T.kp16 / 8; ++cidx) {
-            uint32_t wv[4];
+        // ---- A: this token's coefficients as fp16, zero past r1 (and for an invalid token).
+        // int8 -> fp16 exactly: flip the sign bit (b + 128 as a byte), place the byte under the
+        // fp16 exponent of 1024 (0x64__ = 1024 + byte), subtract 1152.
+        for (int c16 = 0; c16 < T.kp16 / 16; ++c16) {
+            uint4 raw = valid ? *reinterpret_cast<const uint4*>(srow + 16 * c16) : make_uint4(0, 0, 0, 0);
+            const int left = P.r1 - 16 * c16;                       // coefficient bytes in this chunk
+            uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
             #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                uint32_t hh[2];
-                #pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int rr = cidx * 8 + 2 * i + k;
-                    const int c = (valid && rr < P.r1) ? int(int8_t(srow[rr])) : 0;
-                    hh[k] = small_int_f16(c);
-                }
-                wv[i] = hh[0] | (hh[1] << 16);
+                const int keep = left - 4 * i;                      // bytes of this word that are coefficients
+                const uint32_t mask = keep >= 4 ? 0xffffffffu : keep <= 0 ? 0u : (0xffffffffu >> (8 * (4 - keep)));
+                wds[i] &= mask;
             }
+            uint32_t hv[8];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t x = wds[i] ^ 0x80808080u;
+                const uint32_t lo2 = __byte_perm(x, 0x64646464u, 0x4140);   // bytes 0,1 -> two halves
+                const uint32_t hi2 = __byte_perm(x, 0x64646464u, 0x4342);   // bytes 2,3
+                const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+                const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo2), bias);
+                const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi2), bias);
+                hv[2 * i] = *reinterpret_cast<const uint32_t*>(&a);
+                hv[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            const int cidx = 2 * c16;
             *reinterpret_cast<uint4*>(amat + (cidx >> 3) * ATOM_BYTES + kmajor_off(tid, cidx & 7)) =
-                make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(amat + ((cidx + 1) >> 3) * ATOM_BYTES + kmajor_off(tid, (cidx + 1) & 7)) =
+                make_uint4(hv[4], hv[5], hv[6], hv[7]);
         }
         // ---- V^T (MN-major): this token's V lanes as exact small integers, zero if invalid
         const unsigned char* vrow = srow + T.cb + T.kr + voff;
@@ -416,7 +430,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const float krs = valid ? f16_at(krow + 16 + P.k_pb) : 0.f;
         const float csp = (valid ? f16_at(srow + P.coeff_bytes) : 0.f) * s_up;
         const int pos = valid ? tok : t_begin;
-        const int64_t trow = int64_t(min(pos, int(P.table_rows - 1))) * 128;
+        const uint16_t* trow = reinterpret_cast<const uint16_t*>(P.table) +
+                               int64_t(min(pos, int(P.table_rows - 1))) * 128;
+        const bool tbf16 = P.table_dtype == TTKV_BF16;
 
         if (!mbar_wait(&M->mbar, phase)) timed_out = true;
         phase ^= 1u;
@@ -430,6 +446,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
             float alo[32], ahi[32];
+            uint4 cs4[4], sn4[4];                                   // 32 cos + 32 sin, 16-bit
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                cs4[i] = __ldg(reinterpret_cast<const uint4*>(trow + 32 * c) + i);
+                sn4[i] = __ldg(reinterpret_cast<const uint4*>(trow + 64 + 32 * c) + i);
+            }
             tmem_ld32(t_row + uint32_t(32 * c), alo);
             tmem_ld32(t_row + uint32_t(64 + 32 * c), ahi);
             tmem_wait_ld();
@@ -450,8 +472,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 }
                 const float klo = fmaf(alo[l], csp, rl);
                 const float khi = fmaf(ahi[l], csp, rh);
-                const float cz = load_elt(P.table, P.table_dtype, trow + jl);
-                const float sz = load_elt(P.table, P.table_dtype, trow + 64 + jl);
+                const uint32_t cw = reinterpret_cast<const uint32_t*>(&cs4[l >> 3])[(l >> 1) & 3];
+                const uint32_t sw = reinterpret_cast<const uint32_t*>(&sn4[l >> 3])[(l >> 1) & 3];
+                const uint32_t cb = (l & 1) ? (cw >> 16) : (cw & 0xffffu);
+                const uint32_t sb = (l & 1) ? (sw >> 16) : (sw & 0xffffu);
+                const float cz = tbf16 ? __uint_as_float(cb << 16) : f16_bits_to_f32(cb);
+                const float sz = tbf16 ? __uint_as_float(sb << 16) : f16_bits_to_f32(sb);
                 const float ylo = klo * cz - khi * sz;
                 const float yhi = khi * cz + klo * sz;
                 #pragma unroll

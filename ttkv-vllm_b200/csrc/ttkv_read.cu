@@ -648,7 +648,8 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                     max_seq_len - 1, (long long)rope->rows);
     if (batch->n_reqs == 0 || max_seq_len == 0) return TTKV_OK;
     const int n_heads = head_hi - head_lo;
-    const bool use_tc = !multi && tc_serves(lay, HQ) &&
+    const bool use_tc = !multi && tc_serves(lay, HQ) && rope->dtype != TTKV_F32 &&
+                        (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0;
     const Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads)
                            : make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
