@@ -472,12 +472,14 @@ int sm_count() {
 // Whether the tensor-core decode serves this layout (the fp32 kernel serves the rest).
 bool tc_serves(const ttkv_layout_t* lay, int HQ) {
     const int G = HQ / lay->H;
+    // code windows hold 8 codes in 32 bits: widths up to 4 bits
     return lay->d == 128 && lay->qbits == 8 && G >= 1 && G <= kMaxG && lay->r1 <= 192 &&
+           lay->res_bits <= 4 && lay->v_bits <= 4 && lay->res_k <= 128 && lay->v_lanes <= 128 &&
            tc::tc_geom(lay, G).smem > 0;
 }
 
 // Splits for the tensor-core decode: one resident CTA per SM, 128-token tiles; minimise
-// (waves x tiles per CTA) with a small charge per extra split.
+// waves x (tiles per CTA + the set-up of a CTA, about 3/4 of a tile).
 Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads) {
     Plan pl{};
     const int G = HQ / lay->H;
@@ -491,7 +493,7 @@ Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int
     for (int s = 1; s <= std::min(tiles, 64); ++s) {
         const int waves = (pairs * s + sms - 1) / sms;
         const int per = (tiles + s - 1) / s;
-        const double cost = double(waves) * per + 0.05 * s;
+        const double cost = double(waves) * (per + 0.75);
         if (cost < best) { best = cost; best_s = s; }
     }
     pl.chunk = ((tiles + best_s - 1) / best_s) * tc::TM;
