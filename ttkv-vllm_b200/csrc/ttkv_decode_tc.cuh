@@ -6,20 +6,24 @@
 // current 128-token tile is TMEM lane t; warpgroup c handles a quarter of that token's 128 head
 // lanes (the RoPE pairs j, j+64 for j in [16c, 16c+16) of K, the V lanes [32c, 32c+32)). Per tile:
 //
-//   stage    cp.async (16 B) of each token's coefficient block, this head's K residual row and V
-//            row into shared memory, double-buffered across tiles
-//   A        coefficients int8 -> fp16 (exact) in the canonical K-major SW128 layout
-//   MMA 1    acc[128 tokens x 128 lanes] = A . B_hi + A . B_lo  (fp32 in TMEM), where B is the
-//            head's slice of the request's decoder, pre-scaled by a power of two and split into
-//            fp16 hi + lo so the product is accurate to ~2^-22 (a single fp16 operand moved
-//            attention outputs by 4.4e-4 on the parity store; bf16 by 2.7e-3)
-//   decode   while MMA 1 runs: the packed K residual and V codes, eight lanes (one bitmap byte) at a
-//            time without branches: a 32-bit window of the code stream at the byte's first code,
-//            and per bitmap nibble a table of right shifts that brings each kept lane's code to
-//            the bottom (dropped lanes shift by 32 and read 0)
+//   stage    16-byte cp.async copies, chunk-fastest over the tile's tokens, completing on an
+//            mbarrier per unit: this head's K and V rows (two buffers, two tiles ahead), the
+//            coefficient block (one buffer, one tile ahead of its conversion) and the RoPE row
+//            (one buffer, rows padded to 272 B)
+//   A        coefficients int8 -> fp16 (exact) in the canonical K-major SW128 layout, converted
+//            for the next tile as soon as this tile's MMA 1 has read A
+//   MMA 1    acc[128 tokens x 128 lanes] = A . B_hi + A . B_lo  (fp32 in TMEM, two column sets
+//            so the next tile's MMA runs under this tile's softmax), where B is the head's slice
+//            of the request's decoder, pre-scaled by a power of two and split into fp16 hi + lo so
+//            the product is accurate to ~2^-22 (a single fp16 operand moved attention outputs by
+//            4.4e-4 on the parity store; bf16 by 2.7e-3)
+//   decode   the packed K residual and V codes, eight lanes (one bitmap byte) at a time without
+//            branches: a 32-bit window of the code stream at the byte's first code, and per bitmap
+//            nibble a table of right shifts that brings each kept lane's code to the bottom
+//            (dropped lanes shift by 32 and read 0)
 //   epilogue k = acc * (cs * 2^e) + residual; RoPE by the token's own position; partial scores of
-//            the G query heads over this warpgroup's lanes, summed across warpgroups in smem;
-//            online softmax over the tile by warpgroup 0
+//            the G query heads over this warpgroup's lanes, summed across warpgroups through
+//            TMEM; online softmax over the tile, warpgroup g owning query head g
 //   MMA 2    O^T[128 lanes x 16] = V^T . P', V^T = the tile's V codes (exact small integers in
 //            fp16, MN-major so each token writes its lanes contiguously), P' = p * V ruler split
 //            into hi (columns 0..G-1) and lo (columns G..2G-1); read back during the next tile
@@ -32,8 +36,8 @@ namespace tc {
 constexpr int TM = 128;                 // tokens per tile = UMMA M = TMEM lanes
 constexpr int NWG = 4;                  // warpgroups; each owns a quarter of every token's lanes
 constexpr int NTHR = 128 * NWG;
-constexpr uint32_t TMEM_COLS = 256;     // power of two >= 128 (recon) + 16 (PV)
-constexpr uint32_t PV_COL = 128;
+constexpr uint32_t TMEM_COLS = 512;     // 2 x 128 (recon, double-buffered) + 16 (PV) + 32 (partial scores)
+constexpr uint32_t PV_COL = 256;
 constexpr int ATOM_BYTES = 128 * 128;   // one SW128 K-major atom column: 128 rows x 128 B
 constexpr int APV_BYTES = 32768;        // V^T: 128 tokens x 128 lanes fp16
 constexpr int BPV_BYTES = 4096;         // P': 16 rows x 128 tokens fp16
@@ -66,10 +70,6 @@ __device__ __forceinline__ void tc_before() {
 }
 __device__ __forceinline__ void tc_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// Barrier over warpgroup 0 only (named barrier 1).
-__device__ __forceinline__ void wg0_sync() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
@@ -146,11 +146,34 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+
+// The one arrival of a TMA phase, announcing the bytes its copies will deliver.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// Arrive on `bar` once every earlier cp.async of this thread has landed (no pending-count
+// increment: the barrier is initialised with one arrival per thread).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+// Fetch a TMA map's descriptor ahead of its first use.
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled TMA load of the box at element (x, y) of `map` into this CTA's shared memory, its bytes
+// counted on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // Byte offset of (row, 16-byte chunk) in a K-major SW128 atom column of 128-byte rows.
 __device__ __forceinline__ uint32_t kmajor_off(int row, int chunk) {
@@ -274,12 +297,27 @@ __device__ __forceinline__ uint32_t bitmap_byte(const uint32_t (&bw)[4], int g) 
 }
 
 struct TcGeom {            // host-computed shared-memory plan
-    int natom, nstage;     // K atoms of 64 ranks; staging buffers
+    int natom;             // K atoms of 64 ranks
     int kp16;              // r1 rounded up to 16 (the MMA K extent)
-    int cb, kr, vr, srow;  // staged bytes per token: coefficient block, K region, V region, total
-    int off_bhi, off_blo, off_a, off_apv, off_bpv, off_q, off_red, off_lut, off_misc, off_stage;
+    int cb, cf_pitch;      // staged coefficient block per token (coefficients + scale, 16-byte
+                           // blocks) and its row pitch in shared memory
+    int cf_swz;            // 7: 16-byte block c of token u is stored at block c ^ (u & 7)
+    int kr, vr, kvrow;     // staged K region, V region, and the row pitch of both
+    int nkv;               // K/V staging buffers (2: filled a tile ahead; 1: after the tile's reads)
+    int rope_smem;         // 1: the tile's RoPE rows are staged in shared memory
+    int off_bhi, off_blo, off_a, off_apv, off_bpv, off_q, off_lut, off_misc, off_bt, off_cf, off_kv, off_rp;
     int smem;              // dynamic shared memory requested (includes 1 KB alignment slack)
 };
+
+// The TMA map of a launch's RoPE table: boxes of 128 rows x 64 values (the cos or the sin half).
+struct TcMaps {
+    CUtensorMap rope;
+};
+
+constexpr int RP_BOX = 128 * 128;        // one TMA box of RoPE rows: 128 positions x 64 x 16-bit
+constexpr int BT_CAP = 512;              // block-table entries a CTA caches (its token range)
+constexpr int KV_PAD = 16;               // code windows may read a few bytes past the last row
+constexpr uint32_t RED_COL = 272;        // TMEM columns of the partial scores: [warpgroup][8 heads]
 
 struct TcMisc {
     float red_max[4][kMaxG];
@@ -287,12 +325,41 @@ struct TcMisc {
     float m[kMaxG];
     float l[kMaxG];
     float maxabs[NTHR / 32];
-    uint64_t mbar_r, mbar_pv;
+    uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2];
     uint32_t tmem_base;
 };
 
+// Query heads whose softmax a warpgroup owns: g = wg + NWG * i, i < HPW.
+constexpr int HPW = (kMaxG + NWG - 1) / NWG;
+constexpr int MMA_TID = NTHR - 32;       // lane 0 of the last warp issues every MMA
+constexpr int RP_TID = NTHR - 64;        // lane 0 of the warp before it issues the RoPE loads
+
+// Named barrier over the 128 threads of warpgroup `wg` (ids 1..4; 0 is __syncthreads).
+__device__ __forceinline__ void wg_sync(int wg) {
+    asm volatile("bar.sync %0, 128;" :: "r"(wg + 1) : "memory");
+}
+
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    return __uint_as_float(r);
+}
+
+// 8 consecutive fp32 columns of this thread's TMEM lane (then tcgen05.wait::st before a barrier).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+        :: "r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+           "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+           "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 template <int G>
-__global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, const TcGeom T) {
+__global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, const TcGeom T,
+                                                             const __grid_constant__ TcMaps maps) {
     extern __shared__ __align__(1024) unsigned char smem_dyn[];
     // align inside the shared window by pointer arithmetic, so every access stays a shared access
     unsigned char* base = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
@@ -301,11 +368,13 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     unsigned char* amat = base + T.off_a;
     unsigned char* apv = base + T.off_apv;
     unsigned char* bpv = base + T.off_bpv;
-    float* qs = reinterpret_cast<float*>(base + T.off_q);
-    float* red = reinterpret_cast<float*>(base + T.off_red);
+    float* qs = reinterpret_cast<float*>(base + T.off_q);        // [g][pair i2][q_2i2, q_2i2+1, q_64+2i2, q_65+2i2]
     uint4* lutk = reinterpret_cast<uint4*>(base + T.off_lut);
     uint4* lutv = lutk + 16;
     TcMisc* M = reinterpret_cast<TcMisc*>(base + T.off_misc);
+    unsigned char* cfb = base + T.off_cf;                         // [token][cf_pitch]
+    unsigned char* kvb = base + T.off_kv;                         // [buffer][token][K region | V region]
+    unsigned char* rpb = base + T.off_rp;                         // [cos | sin][token][128 B], SW128
 
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const int wg = tid >> 7, t = tid & 127;
@@ -334,6 +403,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             bad = true;
         }
     }
+    if (!bad && t_begin < t_end && (t_end - 1) / P.block_size - t_begin / P.block_size + 1 > BT_CAP) {
+        report(P.status, TTKV_STATUS_ROW_SHORT);           // the plan keeps a split within BT_CAP blocks
+        bad = true;
+    }
     const int64_t row_base = (int64_t(r) * P.n_heads + hl) * G;
     if (bad || t_begin >= t_end) {
         if (tid < G) {
@@ -344,10 +417,137 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             for (int g = 0; g < G; ++g) P.part_o[((row_base + g) * P.n_splits + split) * 128 + t] = 0.f;
         return;
     }
+    const int n_tiles = (t_end - t_begin + TM - 1) / TM;
+
+    // ---- staging. Per tile, 16-byte cp.async copies laid out chunk-fastest over the tile's tokens
+    // (a warp's copies cover a few consecutive slot fields, not 32 scattered rows), the issue cost
+    // shared by every warp: the coefficient blocks (one buffer, refilled after the softmax
+    // barrier for the tile after next) and this head's K and V fields (T.nkv buffers, refilled at
+    // the top of the tile before), each field exactly the 16-byte blocks covering it, never past
+    // the blob. Every thread arrives once per phase on the unit's mbarrier after its own copies
+    // (cp.async.mbarrier.arrive.noinc). The tile's RoPE rows are consecutive positions of the
+    // table: two TMA boxes (cos, sin) of 128 rows, 128-byte swizzled, from one thread.
+    const int kfield = P.coeff_bytes + 2 + h * P.k_row;
+    const int vfield = P.v_offset + h * P.v_row;
+    const int koff = kfield & 15, voff = vfield & 15;
+    const int cch = T.cb >> 4;
+    const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
+    const int nkvc = kch + vch;
+    // division by the chunk counts and the block size as a multiply-high (operands < 2^32 / divisor)
+    const uint32_t mul_cf = uint32_t((0x100000000ull + cch - 1) / cch);
+    const uint32_t mul_kv = uint32_t((0x100000000ull + nkvc - 1) / nkvc);
+    const uint32_t bsz = uint32_t(P.block_size);
+    const uint64_t mul_bs = (0x100000000ull + bsz - 1) / bsz;
+    const int blk0 = t_begin / P.block_size;
+    const int32_t* bts = reinterpret_cast<const int32_t*>(base + T.off_bt);
+    auto slot_at = [&](int tok) -> int64_t {
+        const uint32_t blk = uint32_t((uint64_t(uint32_t(tok)) * mul_bs) >> 32);
+        return int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
+    };
+    auto ntok = [&](int tile) { return tile < n_tiles ? min(TM, t_end - (t_begin + tile * TM)) : 0; };
+    auto kv_buf = [&](int tile) { return T.nkv == 2 ? (tile & 1) : 0; };
+    auto issue_cf = [&](int tile) {
+        const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
+        for (int i = tid; i < n; i += NTHR) {
+            const uint32_t u = __umulhi(uint32_t(i), mul_cf), c = uint32_t(i) - u * uint32_t(cch);
+            cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
+                       P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
+        }
+        cp_async_arrive(&M->mb_cf);
+    };
+    auto issue_kv = [&](int tile) {
+        const int b = kv_buf(tile), t0k = t_begin + tile * TM, n = ntok(tile) * nkvc;
+        unsigned char* dstb = kvb + size_t(b) * TM * T.kvrow;
+        for (int i = tid; i < n; i += NTHR) {
+            const uint32_t u = __umulhi(uint32_t(i), mul_kv), c = uint32_t(i) - u * uint32_t(nkvc);
+            const uint8_t* src = P.cache + slot_at(t0k + int(u)) * P.row_bytes;
+            unsigned char* dst = dstb + u * T.kvrow;
+            if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
+            else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
+        }
+        cp_async_arrive(&M->mb_kv[b]);
+    };
+    auto issue_rp = [&](int tile) {                                // RP_TID only; the buffer is free
+        mbar_expect_tx(&M->mb_rp, uint32_t(2 * RP_BOX));
+        tma_load_2d(rpb, &maps.rope, 0, t_begin + tile * TM, &M->mb_rp);
+        tma_load_2d(rpb + RP_BOX, &maps.rope, 64, t_begin + tile * TM, &M->mb_rp);
+    };
+    // phase parities of the staging mbarriers, and which have copies in flight
+    uint32_t par_cf = 0, par_rp = 0, par_kv0 = 0, par_kv1 = 0;
+    bool pend_cf = false, pend_rp = false, pend_kv0 = false, pend_kv1 = false;
+    bool timed_out = false;
+    auto wait_cf = [&]() {
+        if (!mbar_wait(&M->mb_cf, par_cf)) timed_out = true; else { par_cf ^= 1u; pend_cf = false; }
+    };
+    auto wait_rp = [&]() {
+        if (!mbar_wait(&M->mb_rp, par_rp)) timed_out = true; else { par_rp ^= 1u; pend_rp = false; }
+    };
+    auto wait_kv = [&](int b) {
+        if (!mbar_wait(&M->mb_kv[b], b ? par_kv1 : par_kv0)) timed_out = true;
+        else if (b) { par_kv1 ^= 1u; pend_kv1 = false; }
+        else { par_kv0 ^= 1u; pend_kv0 = false; }
+    };
+    auto mark_kv = [&](int tile) { if (kv_buf(tile)) pend_kv1 = true; else pend_kv0 = true; };
+
+    // ---- A: a token's coefficients as fp16 (16 per chunk, chunks wg, wg + NWG, ...), zero past r1
+    // and for an invalid token. int8 -> fp16 exactly: flip the sign bit (b + 128 as a byte), place
+    // the byte under the fp16 exponent of 1024 (0x64__ = 1024 + byte), subtract 1152.
+    auto convert_a = [&](bool valid) {
+        const unsigned char* srow = cfb + t * T.cf_pitch;
+        const int swz = t & T.cf_swz;
+        for (int c16 = wg; c16 < T.kp16 / 16; c16 += NWG) {
+            uint4 raw = valid ? *reinterpret_cast<const uint4*>(srow + 16 * (c16 ^ swz)) : make_uint4(0, 0, 0, 0);
+            const int left = P.r1 - 16 * c16;                       // coefficient bytes in this chunk
+            uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+            if (left < 16) {
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int keep = left - 4 * i;                  // bytes of this word that are coefficients
+                    const uint32_t mask = keep >= 4 ? 0xffffffffu : keep <= 0 ? 0u : (0xffffffffu >> (8 * (4 - keep)));
+                    wds[i] &= mask;
+                }
+            }
+            uint32_t hv[8];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t x = wds[i] ^ 0x80808080u;
+                const uint32_t lo2 = __byte_perm(x, 0x64646464u, 0x4140);   // bytes 0,1 -> two halves
+                const uint32_t hi2 = __byte_perm(x, 0x64646464u, 0x4342);   // bytes 2,3
+                const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+                const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo2), bias);
+                const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi2), bias);
+                hv[2 * i] = *reinterpret_cast<const uint32_t*>(&a);
+                hv[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            const int cidx = 2 * c16;
+            *reinterpret_cast<uint4*>(amat + (cidx >> 3) * ATOM_BYTES + kmajor_off(t, cidx & 7)) =
+                make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(amat + ((cidx + 1) >> 3) * ATOM_BYTES + kmajor_off(t, (cidx + 1) & 7)) =
+                make_uint4(hv[4], hv[5], hv[6], hv[7]);
+        }
+        // the token's coefficient scale: fp16 at bytes coeff_bytes, +1 (they may sit in two blocks)
+        auto byte_at = [&](int b) { return uint32_t(srow[16 * ((b >> 4) ^ swz) + (b & 15)]); };
+        const int sb = P.coeff_bytes;
+        return valid ? f16_bits_to_f32(byte_at(sb) | (byte_at(sb + 1) << 8)) : 0.f;
+    };
 
     // ---- set-up: TMEM, barriers, tables, operands that live for the whole CTA
     if (w == 0) tmem_alloc(&M->tmem_base, TMEM_COLS);
-    if (tid == 0) { mbar_init(&M->mbar_r, 1); mbar_init(&M->mbar_pv, 1); }
+    if (tid == RP_TID && T.rope_smem) tma_prefetch_desc(&maps.rope);
+    if (tid == 0) {
+        mbar_init(&M->mb_r, 1);
+        mbar_init(&M->mb_pv, 1);
+        mbar_init(&M->mb_cf, NTHR);
+        mbar_init(&M->mb_rp, 1);
+        mbar_init(&M->mb_kv[0], NTHR);
+        mbar_init(&M->mb_kv[1], NTHR);
+    }
+    {
+        int32_t* btw = reinterpret_cast<int32_t*>(base + T.off_bt);
+        const int nblk = (t_end - 1) / P.block_size - blk0 + 1;        // <= BT_CAP (checked above)
+        for (int i = tid; i < nblk; i += NTHR) btw[i] = brow[blk0 + i];
+    }
+
     if (tid < kMaxG) { M->m[tid] = -INFINITY; M->l[tid] = 0.f; }
     if (tid < 32) {
         const int n = tid & 15, bits = tid < 16 ? P.res_bits : P.v_bits;
@@ -357,7 +557,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     for (int i = tid; i < BPV_BYTES / 16; i += NTHR) reinterpret_cast<uint4*>(bpv)[i] = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < G * 128; i += NTHR) {
         const int g = i >> 7, j = i & 127;
-        qs[i] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
+        const int slot = (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1);
+        qs[slot] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
     }
     // decoder slice: power-of-two scale so max|D| * 2^-e lies in [2^13, 2^14), then fp16 hi + lo
     const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * 128 + t;
@@ -366,7 +567,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     for (int rr = wg; rr < P.r1; rr += NWG) mx = fmaxf(mx, fabsf(dec[rr * dstride]));
     mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
     if (lane == 0) M->maxabs[w] = mx;
-    __syncthreads();
+    __syncthreads();                                  // barriers initialised, block-table slice cached
+    issue_cf(0);
+    issue_kv(0);
+    if (tid == RP_TID && T.rope_smem) issue_rp(0);
+    pend_cf = true; pend_kv0 = true;
+    if (T.rope_smem) pend_rp = true;
     mx = 0.f;
     #pragma unroll
     for (int i = 0; i < NTHR / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
@@ -395,46 +601,44 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
 
-    // ---- staging of one tile: 16-byte chunks of each token's three regions
-    const int kfield = P.coeff_bytes + 2 + h * P.k_row;
-    const int vfield = P.v_offset + h * P.v_row;
-    const int koff = kfield & 15, voff = vfield & 15;
-    // chunks this head needs: exactly the 16-byte blocks covering each field, never past the blob
-    const int cch = T.cb >> 4;
-    const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
-    const int nch = cch + kch + vch;
-    unsigned char* stage0 = base + T.off_stage;
-    auto issue_stage = [&](int t0, unsigned char* st) {
-        const int ntok = min(TM, t_end - t0);
-        for (int i = tid; i < ntok * nch; i += NTHR) {
-            const int tt = i / nch, c = i - tt * nch;
-            const int tok = t0 + tt;
-            const int64_t slot = int64_t(brow[tok / P.block_size]) * P.block_size + tok % P.block_size;
-            const uint8_t* src = P.cache + slot * P.row_bytes;
-            int gofs, sofs;
-            if (c < cch) {
-                gofs = c * 16;
-                sofs = c * 16;
-            } else if (c < cch + kch) {
-                gofs = (kfield - koff) + (c - cch) * 16;
-                sofs = T.cb + (c - cch) * 16;
-            } else {
-                gofs = (vfield - voff) + (c - cch - kch) * 16;
-                sofs = T.cb + T.kr + (c - cch - kch) * 16;
-            }
-            cp_async16(st + tt * T.srow + sofs, src + gofs);
+    // MMA issue (one thread). The start-address field of a descriptor is its low 14 bits (16-byte
+    // units, shared addresses < 2^18 B), so a k-step offset is added to the descriptor directly.
+    const uint64_t dA = sw128_desc(smem_u32(amat), 16, 1024), dH = sw128_desc(smem_u32(bhi), 16, 1024),
+                   dL = sw128_desc(smem_u32(blo), 16, 1024);
+    const uint64_t dV = sw128_desc(smem_u32(apv), 1024, 2048), dP = sw128_desc(smem_u32(bpv), 16, 1024);
+    auto issue_recon = [&](uint32_t d_tmem) {
+        constexpr uint32_t IDESC_R = idesc_f16(128, 128, false, false);
+        for (int ks = 0; ks < T.kp16 / 16; ++ks) {
+            const uint64_t k16 = uint64_t(((ks >> 2) * ATOM_BYTES + (ks & 3) * 32) >> 4);
+            mma_f16(d_tmem, dA + k16, dH + k16, IDESC_R, ks > 0 ? 1u : 0u);
+            mma_f16(d_tmem, dA + k16, dL + k16, IDESC_R, 1u);
         }
-        cp_async_commit();
+        mma_commit(&M->mb_r);
+    };
+    auto issue_pv = [&](uint32_t d_tmem) {
+        constexpr uint32_t IDESC_PV = idesc_f16(128, 16, true, false);
+        #pragma unroll
+        for (int ks = 0; ks < TM / 16; ++ks)
+            mma_f16(d_tmem, dV + uint64_t((ks * 4096) >> 4),
+                    dP + uint64_t(((ks >> 2) * 2048 + (ks & 3) * 32) >> 4), IDESC_PV, ks > 0 ? 1u : 0u);
+        mma_commit(&M->mb_pv);
     };
 
+    // ---- first tile: its coefficient block, its A, its reconstruction (TMEM columns 0..127)
+    wait_cf();
+    float csp_next = convert_a(t_begin + t < t_end) * s_up;        // coefficient scale x 2^e of the tile
+    fence_async_smem();
     tc_before();
     __syncthreads();
     tc_after();
     const uint32_t taddr = M->tmem_base;
     const uint32_t t_row = taddr + (uint32_t(32 * (w & 3)) << 16);    // this warp's TMEM lanes
+    if (tid == MMA_TID) issue_recon(taddr);
+    if (n_tiles > 1) {                                              // every conversion of tile 0 is done
+        issue_cf(1);
+        pend_cf = true;
+    }
 
-    constexpr uint32_t IDESC_R = idesc_f16(128, 128, false, false);
-    constexpr uint32_t IDESC_PV = idesc_f16(128, 16, true, false);
     const int kbits = P.res_bits, vbits = P.v_bits;
     const uint32_t kflip = flip_mask(kbits), vflip = flip_mask(vbits);
     const uint32_t khalf = 1u << (kbits - 1), vhalf = 1u << (vbits - 1);
@@ -445,82 +649,46 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const __half2 vbias2 = __floats2half2_rn(1024.f + float(vhalf), 1024.f + float(vhalf));
     const bool tbf16 = P.table_dtype == TTKV_BF16;
     const float scale = P.scale;
+    const float4* qs4 = reinterpret_cast<const float4*>(qs);
 
-    float o[G], corr_prev[G];
+    float o[HPW], corr_prev[HPW];
     #pragma unroll
-    for (int g = 0; g < G; ++g) { o[g] = 0.f; corr_prev[g] = 0.f; }
+    for (int i = 0; i < HPW; ++i) { o[i] = 0.f; corr_prev[i] = 0.f; }
     uint32_t ph_r = 0, ph_pv = 0;
-    bool r_pending = false, pv_pending = false, timed_out = false;
+    bool r_pending = true, pv_pending = false;
 
-    issue_stage(t_begin, stage0);
-    int it = 0;
-    for (int t0 = t_begin; t0 < t_end; t0 += TM, ++it) {
-        unsigned char* st = stage0 + size_t(T.nstage == 2 ? (it & 1) : 0) * (TM * T.srow);
-        cp_async_wait_all();
-        __syncthreads();                                                   // tile landed
-        if (T.nstage == 2 && t0 + TM < t_end)
-            issue_stage(t0 + TM, stage0 + size_t((it + 1) & 1) * (TM * T.srow));
-
+    for (int it = 0; it < n_tiles; ++it) {
+        const int t0 = t_begin + it * TM;
+        const bool has_next = it + 1 < n_tiles;
+        const int kb = kv_buf(it);
         const int tok = t0 + t;
         const bool valid = tok < t_end;
-        const unsigned char* srow = st + t * T.srow;
-        const uint32_t srow_off = uint32_t(srow - base);
+        const unsigned char* kvrow = kvb + (size_t(kb) * TM + t) * T.kvrow;
+        const uint32_t kv_off = uint32_t(kvrow - base);
+        // the next tile's K/V fields, into the other buffer (read by the tile before this one)
+        if (T.nkv == 2 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }
+        const uint32_t rcol = uint32_t(it & 1) * 128u;                 // this tile's reconstruction columns
+        const float csp = csp_next;
 
-        // ---- A: this token's coefficients as fp16, zero past r1 (and for an invalid token).
-        // int8 -> fp16 exactly: flip the sign bit (b + 128 as a byte), place the byte under the
-        // fp16 exponent of 1024 (0x64__ = 1024 + byte), subtract 1152.
-        for (int c16 = wg; c16 < T.kp16 / 16; c16 += NWG) {
-            uint4 raw = valid ? *reinterpret_cast<const uint4*>(srow + 16 * c16) : make_uint4(0, 0, 0, 0);
-            const int left = P.r1 - 16 * c16;                       // coefficient bytes in this chunk
-            uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+        // ---- this token's RoPE row from global memory when it is not staged (used in the epilogue)
+        uint4 cosw[2], sinw[2];
+        if (!T.rope_smem) {
+            const uint16_t* trow = reinterpret_cast<const uint16_t*>(P.table) +
+                                   int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128;
             #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int keep = left - 4 * i;                      // bytes of this word that are coefficients
-                const uint32_t mask = keep >= 4 ? 0xffffffffu : keep <= 0 ? 0u : (0xffffffffu >> (8 * (4 - keep)));
-                wds[i] &= mask;
+            for (int hp = 0; hp < 2; ++hp) {
+                cosw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 16 * wg + 8 * hp));
+                sinw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 64 + 16 * wg + 8 * hp));
             }
-            uint32_t hv[8];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t x = wds[i] ^ 0x80808080u;
-                const uint32_t lo2 = __byte_perm(x, 0x64646464u, 0x4140);   // bytes 0,1 -> two halves
-                const uint32_t hi2 = __byte_perm(x, 0x64646464u, 0x4342);   // bytes 2,3
-                const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
-                const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo2), bias);
-                const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi2), bias);
-                hv[2 * i] = *reinterpret_cast<const uint32_t*>(&a);
-                hv[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&b);
-            }
-            const int cidx = 2 * c16;
-            *reinterpret_cast<uint4*>(amat + (cidx >> 3) * ATOM_BYTES + kmajor_off(t, cidx & 7)) =
-                make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            *reinterpret_cast<uint4*>(amat + ((cidx + 1) >> 3) * ATOM_BYTES + kmajor_off(t, (cidx + 1) & 7)) =
-                make_uint4(hv[4], hv[5], hv[6], hv[7]);
         }
-        fence_async_smem();
-        tc_before();
-        __syncthreads();
-        tc_after();
 
-        // ---- MMA 1: reconstruction
-        if (tid == 0) {
-            const uint32_t a0 = smem_u32(amat), h0 = smem_u32(bhi), l0 = smem_u32(blo);
-            for (int ks = 0; ks < T.kp16 / 16; ++ks) {
-                const uint32_t kofs = uint32_t((ks >> 2) * ATOM_BYTES + (ks & 3) * 32);
-                const uint64_t ad = sw128_desc(a0 + kofs, 16, 1024);
-                mma_f16(taddr, ad, sw128_desc(h0 + kofs, 16, 1024), IDESC_R, ks > 0 ? 1u : 0u);
-                mma_f16(taddr, ad, sw128_desc(l0 + kofs, 16, 1024), IDESC_R, 1u);
-            }
-            mma_commit(&M->mbar_r);
-        }
-        r_pending = true;
-
-        // ---- while MMA 1 runs: K residual lanes [16wg, 16wg+16) and [64+16wg, 64+16wg+16)
-        const uint32_t kf = srow_off + uint32_t(T.cb + koff);            // K field in smem
-        float rkl[16], rkh[16];
-        float krs, csp;
+        // ---- K residual: code windows of the bitmap bytes of lanes [16wg, 16wg+16) and
+        // [64+16wg, 64+16wg+16) (bytes 2wg+hp and 8+2wg+hp); the fields are cut in the epilogue
+        wait_kv(kb);
+        uint32_t kwin[4], kbyte[4];
+        float krs;
         {
-            const uint4* kp = reinterpret_cast<const uint4*>(srow + T.cb);
+            const uint4* kp = reinterpret_cast<const uint4*>(kvrow);
             uint32_t bw[4];
             bitmap_words(kp[0], kp[1], koff, bw);
             if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
@@ -531,45 +699,39 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             pre[2] = pre[1] + __popc(bw[1]);
             pre[3] = pre[2] + __popc(bw[2]);
             #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                #pragma unroll
-                for (int gi = 0; gi < 2; ++gi) {
-                    const int grp = 8 * half + 2 * wg + gi;
-                    const uint32_t byte = bitmap_byte(bw, grp);
-                    const int rank = byte_rank(bw, pre, grp);
-                    const uint32_t win = window32(base, kf + 16u, uint32_t(rank * kbits)) ^ kflip;
-                    uint32_t f[8];
-                    group_fields(win, byte, kbits, lutk, f);
-                    #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const float v = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
-                        if (half == 0) rkl[8 * gi + k] = v; else rkh[8 * gi + k] = v;
-                    }
-                }
+            for (int q = 0; q < 4; ++q) {
+                const int grp = (q & 1 ? 8 : 0) + 2 * wg + (q >> 1);
+                kbyte[q] = bitmap_byte(bw, grp);
+                kwin[q] = window32(base, kv_off + uint32_t(koff + 16), uint32_t(byte_rank(bw, pre, grp) * kbits)) ^ kflip;
             }
-            krs = valid ? f16_at(srow + T.cb + koff + 16 + P.k_pb) : 0.f;
-            csp = (valid ? f16_at(srow + P.coeff_bytes) : 0.f) * s_up;
+            krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
         }
 
-        // ---- PV of the previous tile: fold into o (warpgroup 0), then V^T may be overwritten
+        // ---- PV of the previous tile: each warpgroup folds its query heads into o
         if (pv_pending) {
-            if (!mbar_wait(&M->mbar_pv, ph_pv)) timed_out = true;
+            if (!mbar_wait(&M->mb_pv, ph_pv)) timed_out = true;
             else { ph_pv ^= 1u; pv_pending = false; }
             tc_after();
-            if (wg == 0 && !__any_sync(0xffffffffu, timed_out)) {
-                float d[16];
-                tmem_ld16(t_row + PV_COL, d);
-                tmem_wait_ld();
+            if (wg < G && !__any_sync(0xffffffffu, timed_out)) {
                 #pragma unroll
-                for (int g = 0; g < G; ++g) o[g] = fmaf(o[g], corr_prev[g], d[g] + d[G + g]);
+                for (int i = 0; i < HPW; ++i) {
+                    const int g = wg + NWG * i;
+                    if (g < G) {
+                        const float dh = tmem_ld1(t_row + PV_COL + uint32_t(g));
+                        const float dl = tmem_ld1(t_row + PV_COL + uint32_t(G + g));
+                        tmem_wait_ld();
+                        o[i] = fmaf(o[i], corr_prev[i], dh + dl);
+                    }
+                }
             }
         }
 
         // ---- V^T (MN-major): lanes [32wg, 32wg+32) of this token as exact small integers
         float vrs;
         {
-            const uint32_t vfo = srow_off + uint32_t(T.cb + T.kr + voff);
-            const uint4* vp = reinterpret_cast<const uint4*>(srow + T.cb + T.kr);
+            const unsigned char* vrow = kvrow + T.kr;
+            const uint32_t vfo = kv_off + uint32_t(T.kr + voff);
+            const uint4* vp = reinterpret_cast<const uint4*>(vrow);
             uint32_t bw[4];
             bitmap_words(vp[0], vp[1], voff, bw);
             if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
@@ -595,31 +757,60 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                                               (((ch & 7) ^ (t & 7)) << 4));
                 *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
             }
-            vrs = valid ? f16_at(srow + T.cb + T.kr + voff + 16 + P.v_pb) : 0.f;
+            vrs = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
+        }
+
+        // ---- MMA 1 of this tile done: A is free for the next tile's coefficients
+        if (r_pending) {
+            if (!mbar_wait(&M->mb_r, ph_r)) timed_out = true;
+            else { ph_r ^= 1u; r_pending = false; }
+        }
+        tc_after();
+        if (has_next) {
+            wait_cf();
+            csp_next = convert_a(t0 + TM + t < t_end) * s_up;
         }
 
         // ---- epilogue: rebuild, patch, rotate, partial scores over this warpgroup's lanes
-        if (!mbar_wait(&M->mbar_r, ph_r)) timed_out = true;
-        else { ph_r ^= 1u; r_pending = false; }
-        tc_after();
-        float2 s2[G];
+        if (T.rope_smem) {
+            wait_rp();
+            // row t of each box: 16-byte block c stored at block c ^ (t & 7)
+            const unsigned char* rc = rpb + t * 128;
+            #pragma unroll
+            for (int hp = 0; hp < 2; ++hp) {
+                const int c = (2 * wg + hp) ^ (t & 7);
+                cosw[hp] = *reinterpret_cast<const uint4*>(rc + 16 * c);
+                sinw[hp] = *reinterpret_cast<const uint4*>(rc + RP_BOX + 16 * c);
+            }
+        }
+        float sp[8];
         #pragma unroll
-        for (int g = 0; g < G; ++g) s2[g] = make_float2(0.f, 0.f);
+        for (int g = 0; g < 8; ++g) sp[g] = 0.f;
         if (!__any_sync(0xffffffffu, timed_out)) {
-            const uint16_t* trow = reinterpret_cast<const uint16_t*>(P.table) +
-                                   int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128;
+            float2 s2[G];
+            #pragma unroll
+            for (int g = 0; g < G; ++g) s2[g] = make_float2(0.f, 0.f);
             const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
             const float2 neg1 = make_float2(-1.f, -1.f);
             #pragma unroll
             for (int hp = 0; hp < 2; ++hp) {                        // 8 RoPE pairs at a time
                 const int j0 = 16 * wg + 8 * hp;
                 float al[8], ah[8];
-                tmem_ld8(t_row + uint32_t(j0), al);
-                tmem_ld8(t_row + uint32_t(64 + j0), ah);
-                const uint4 cw = __ldg(reinterpret_cast<const uint4*>(trow + j0));
-                const uint4 sw = __ldg(reinterpret_cast<const uint4*>(trow + 64 + j0));
+                tmem_ld8(t_row + rcol + uint32_t(j0), al);
+                tmem_ld8(t_row + rcol + uint32_t(64 + j0), ah);
+                float rl[8], rh[8];
+                {
+                    uint32_t f[8];
+                    group_fields(kwin[2 * hp], kbyte[2 * hp], kbits, lutk, f);
+                    #pragma unroll
+                    for (int k = 0; k < 8; ++k) rl[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
+                    group_fields(kwin[2 * hp + 1], kbyte[2 * hp + 1], kbits, lutk, f);
+                    #pragma unroll
+                    for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
+                }
                 tmem_wait_ld();
-                const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w}, swv[4] = {sw.x, sw.y, sw.z, sw.w};
+                const uint32_t cwv[4] = {cosw[hp].x, cosw[hp].y, cosw[hp].z, cosw[hp].w};
+                const uint32_t swv[4] = {sinw[hp].x, sinw[hp].y, sinw[hp].z, sinw[hp].w};
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) {                       // lanes j0+2i, j0+2i+1
                     float2 cz, sz;
@@ -630,130 +821,158 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                         cz = __half22float2(*reinterpret_cast<const __half2*>(&cwv[i]));
                         sz = __half22float2(*reinterpret_cast<const __half2*>(&swv[i]));
                     }
-                    const int li = 8 * hp + 2 * i;
-                    const float2 kl = f2fma(make_float2(rkl[li], rkl[li + 1]), krs2,
+                    const float2 kl = f2fma(make_float2(rl[2 * i], rl[2 * i + 1]), krs2,
                                             f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
-                    const float2 kh = f2fma(make_float2(rkh[li], rkh[li + 1]), krs2,
+                    const float2 kh = f2fma(make_float2(rh[2 * i], rh[2 * i + 1]), krs2,
                                             f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
                     const float2 yl = f2fma(f2mul(kh, neg1), sz, f2mul(kl, cz));
                     const float2 yh = f2fma(kl, sz, f2mul(kh, cz));
                     #pragma unroll
                     for (int g = 0; g < G; ++g) {
-                        const float2 ql = *reinterpret_cast<const float2*>(qs + g * 128 + j0 + 2 * i);
-                        const float2 qh = *reinterpret_cast<const float2*>(qs + g * 128 + 64 + j0 + 2 * i);
-                        s2[g] = f2fma(ql, yl, f2fma(qh, yh, s2[g]));
+                        const float4 qq = qs4[g * 32 + (j0 >> 1) + i];
+                        s2[g] = f2fma(make_float2(qq.x, qq.y), yl, f2fma(make_float2(qq.z, qq.w), yh, s2[g]));
                     }
                 }
             }
+            #pragma unroll
+            for (int g = 0; g < G; ++g) sp[g] = s2[g].x + s2[g].y;
+            tmem_st8(t_row + RED_COL + uint32_t(8 * wg), sp);     // partial scores -> TMEM
+            tmem_wait_st();
         }
-        #pragma unroll
-        for (int g = 0; g < G; ++g) red[(wg * G + g) * 128 + t] = s2[g].x + s2[g].y;
-        fence_async_smem();                                        // V^T for MMA 2
-        if (__syncthreads_or(timed_out)) { timed_out = true; break; }
 
-        // ---- online softmax over the tile (warpgroup 0: thread t = token t)
-        if (wg == 0) {
-            float sc[G], m_new[G], corr[G];
+        const bool cf_refill = it + 2 < n_tiles;
+        fence_async_smem();                                          // V^T, next A for the MMAs
+        tc_before();
+        if (__syncthreads_or(timed_out)) { timed_out = true; break; }
+        tc_after();
+
+        // ---- MMA 1 of the next tile into the other reconstruction columns (under the softmax
+        // and the next tile's decode), and the refills of the staging units this tile released
+        if (has_next) {
+            if (tid == MMA_TID) issue_recon(taddr + (rcol ^ 128u));
+            r_pending = true;
+        }
+        if (T.nkv == 1 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }   // the buffer is free now
+        if (cf_refill) { issue_cf(it + 2); pend_cf = true; }
+        if (T.rope_smem && has_next) {
+            if (tid == RP_TID) issue_rp(it + 1);
+            pend_rp = true;
+        }
+
+        // ---- online softmax over the tile: warpgroup wg owns query heads wg, wg + NWG, ...
+        if (wg < G) {
+            float sc[HPW], m_new[HPW], corr[HPW];
             #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float v = red[g * 128 + t];
-                #pragma unroll
-                for (int c = 1; c < NWG; ++c) v += red[(c * G + g) * 128 + t];
-                sc[g] = valid ? v * scale : -INFINITY;
-                float mxg = sc[g];
-                #pragma unroll
-                for (int off = 16; off; off >>= 1) mxg = fmaxf(mxg, __shfl_xor_sync(0xffffffffu, mxg, off));
-                if (lane == 0) M->red_max[w][g] = mxg;
-            }
-            wg0_sync();
-            #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float tmax = fmaxf(fmaxf(M->red_max[0][g], M->red_max[1][g]),
-                                         fmaxf(M->red_max[2][g], M->red_max[3][g]));
-                const float m_old = M->m[g];
-                m_new[g] = fmaxf(m_old, tmax);
-                const float pg = (m_new[g] == -INFINITY || sc[g] == -INFINITY) ? 0.f : expf(sc[g] - m_new[g]);
-                corr[g] = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new[g]);
-                float sum = pg;
-                #pragma unroll
-                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                if (lane == 0) M->red_sum[w][g] = sum;
-                // P' = p * V ruler as fp16 hi (column g) + lo (column G + g); this token is K index t
-                const float pv = pg * vrs;
-                const uint32_t hb = f16_bits(pv);
-                const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
-                const int kt = t & 63, atom = t >> 6;
-                #pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int n = k == 0 ? g : G + g;
-                    const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
-                                                  (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
-                    *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
+            for (int i = 0; i < HPW; ++i) {
+                const int g = wg + NWG * i;
+                sc[i] = -INFINITY; m_new[i] = -INFINITY; corr[i] = 0.f;
+                if (g < G) {
+                    float v = 0.f;
+                    #pragma unroll
+                    for (int c = 0; c < NWG; ++c) v += tmem_ld1(t_row + RED_COL + uint32_t(8 * c + g));
+                    tmem_wait_ld();
+                    sc[i] = valid ? v * scale : -INFINITY;
+                    float mxg = sc[i];
+                    #pragma unroll
+                    for (int off = 16; off; off >>= 1) mxg = fmaxf(mxg, __shfl_xor_sync(0xffffffffu, mxg, off));
+                    if (lane == 0) M->red_max[w & 3][g] = mxg;
                 }
             }
-            wg0_sync();
-            if (t < G) {
+            wg_sync(wg);
+            #pragma unroll
+            for (int i = 0; i < HPW; ++i) {
+                const int g = wg + NWG * i;
+                if (g < G) {
+                    const float tmax = fmaxf(fmaxf(M->red_max[0][g], M->red_max[1][g]),
+                                             fmaxf(M->red_max[2][g], M->red_max[3][g]));
+                    const float m_old = M->m[g];
+                    m_new[i] = fmaxf(m_old, tmax);
+                    const float pg = (m_new[i] == -INFINITY || sc[i] == -INFINITY) ? 0.f : expf(sc[i] - m_new[i]);
+                    corr[i] = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new[i]);
+                    float sum = pg;
+                    #pragma unroll
+                    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                    if (lane == 0) M->red_sum[w & 3][g] = sum;
+                    // P' = p * V ruler as fp16 hi (column g) + lo (column G + g); this token is K index t
+                    const float pv = pg * vrs;
+                    const uint32_t hb = f16_bits(pv);
+                    const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
+                    const int kt = t & 63, atom = t >> 6;
+                    #pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int n = k == 0 ? g : G + g;
+                        const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
+                                                      (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
+                        *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
+                    }
+                }
+            }
+            wg_sync(wg);
+            if (t == 0) {
                 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    if (t == g) {
+                for (int i = 0; i < HPW; ++i) {
+                    const int g = wg + NWG * i;
+                    if (g < G) {
                         const float tsum = M->red_sum[0][g] + M->red_sum[1][g] + M->red_sum[2][g] + M->red_sum[3][g];
-                        M->l[g] = M->l[g] * corr[g] + tsum;
-                        M->m[g] = m_new[g];
+                        M->l[g] = M->l[g] * corr[i] + tsum;
+                        M->m[g] = m_new[i];
                     }
                 }
             }
             #pragma unroll
-            for (int g = 0; g < G; ++g) corr_prev[g] = corr[g];
+            for (int i = 0; i < HPW; ++i) corr_prev[i] = corr[i];
         }
         fence_async_smem();
         tc_before();
         __syncthreads();
         tc_after();
 
-        // ---- MMA 2: O^T[lane][col] = V^T . P'  (8 K-steps of 16 tokens); read in the next tile
-        if (tid == 0) {
-            const uint32_t a0 = smem_u32(apv), b0 = smem_u32(bpv);
-            for (int ks = 0; ks < TM / 16; ++ks) {
-                const uint64_t ad = sw128_desc(a0 + uint32_t(ks * 4096), 1024, 2048);
-                const uint64_t bd = sw128_desc(b0 + uint32_t((ks >> 2) * 2048 + (ks & 3) * 32), 16, 1024);
-                mma_f16(taddr + PV_COL, ad, bd, IDESC_PV, ks > 0 ? 1u : 0u);
-            }
-            mma_commit(&M->mbar_pv);
-        }
+        // ---- MMA 2 of this tile: O^T = V^T . P', read back during the next tile
+        if (tid == MMA_TID) issue_pv(taddr + PV_COL);
         pv_pending = true;
-        if (T.nstage == 1 && t0 + TM < t_end) issue_stage(t0 + TM, stage0);   // every read of the stage is done
     }
 
     // ---- the last tile's PV
     if (!timed_out && pv_pending) {
-        if (!mbar_wait(&M->mbar_pv, ph_pv)) timed_out = true;
+        if (!mbar_wait(&M->mb_pv, ph_pv)) timed_out = true;
         else { ph_pv ^= 1u; pv_pending = false; }
         tc_after();
-        if (wg == 0 && !__any_sync(0xffffffffu, timed_out)) {
-            float d[16];
-            tmem_ld16(t_row + PV_COL, d);
-            tmem_wait_ld();
+        if (wg < G && !__any_sync(0xffffffffu, timed_out)) {
             #pragma unroll
-            for (int g = 0; g < G; ++g) o[g] = fmaf(o[g], corr_prev[g], d[g] + d[G + g]);
+            for (int i = 0; i < HPW; ++i) {
+                const int g = wg + NWG * i;
+                if (g < G) {
+                    const float dh = tmem_ld1(t_row + PV_COL + uint32_t(g));
+                    const float dl = tmem_ld1(t_row + PV_COL + uint32_t(G + g));
+                    tmem_wait_ld();
+                    o[i] = fmaf(o[i], corr_prev[i], dh + dl);
+                }
+            }
         }
     }
     timed_out = __syncthreads_or(timed_out);
 
-    // ---- drain and release: anything still in flight gets one more bounded wait before TMEM is freed
+    // ---- drain and release: anything still in flight gets one more bounded wait before TMEM and
+    // the shared memory are released
     if (timed_out) {
         if (tid == 0) report(P.status, TTKV_STATUS_TIMEOUT);
-        if (r_pending) mbar_wait(&M->mbar_r, ph_r);
-        if (pv_pending) mbar_wait(&M->mbar_pv, ph_pv);
+        if (r_pending) mbar_wait(&M->mb_r, ph_r);
+        if (pv_pending) mbar_wait(&M->mb_pv, ph_pv);
+        if (pend_cf) mbar_wait(&M->mb_cf, par_cf);
+        if (pend_rp) mbar_wait(&M->mb_rp, par_rp);
+        if (pend_kv0) mbar_wait(&M->mb_kv[0], par_kv0);
+        if (pend_kv1) mbar_wait(&M->mb_kv[1], par_kv1);
     }
-    cp_async_wait_all();
     tc_before();
     __syncthreads();
     tc_after();
     if (w == 0) tmem_dealloc(taddr, TMEM_COLS);
-    if (wg == 0) {
+    if (wg < G) {
         #pragma unroll
-        for (int g = 0; g < G; ++g)
-            P.part_o[((row_base + g) * P.n_splits + split) * 128 + t] = timed_out ? 0.f : o[g];
+        for (int i = 0; i < HPW; ++i) {
+            const int g = wg + NWG * i;
+            if (g < G) P.part_o[((row_base + g) * P.n_splits + split) * 128 + t] = timed_out ? 0.f : o[i];
+        }
     }
     if (tid < G) {
         P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
@@ -765,6 +984,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
 inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
 // The shared-memory plan of decode_tc_kernel for a layout, or smem == 0 if it does not fit.
+// Preference: two K/V buffers with staged RoPE rows, then one K/V buffer, then RoPE rows read
+// from global memory.
 inline TcGeom tc_geom(const ttkv_layout_t* lay, int G) {
     TcGeom T{};
     T.kp16 = round_up(lay->r1, 16);
@@ -777,15 +998,21 @@ inline TcGeom tc_geom(const ttkv_layout_t* lay, int G) {
         kr = std::max(kr, round_up((kf & 15) + lay->k_row_bytes, 16));
         vr = std::max(vr, round_up((vf & 15) + lay->v_row_bytes, 16));
     }
-    // the bitmap is read as the two 16-byte chunks holding it
+    // each bitmap is read as the two 16-byte blocks holding it
     T.kr = std::max(kr, 32);
     T.vr = std::max(vr, 32);
-    T.srow = T.cb + T.kr + T.vr;
+    // row pitches an odd number of 16-byte blocks: a warp's 32 rows then spread over all banks
+    T.kvrow = T.kr + T.vr;
+    if (((T.kvrow >> 4) & 1) == 0) T.kvrow += 16;
+    // coefficient rows: an odd number of blocks as they are, a multiple of 8 XOR-swizzled, else padded
+    const int cch = T.cb >> 4;
+    T.cf_swz = (cch % 8 == 0) ? 7 : 0;
+    T.cf_pitch = T.cb + ((cch & 1) == 0 && cch % 8 != 0 ? 16 : 0);
     const int atoms = T.natom * ATOM_BYTES;
-    const int q_bytes = round_up(G * 128 * 4, 1024);
-    const int red_bytes = round_up(NWG * G * 128 * 4, 1024);
+    const int q_bytes = round_up(G * 128 * 4, 128);
     const int misc = round_up(int(sizeof(TcMisc)), 128);
-    for (int ns = 2; ns >= 1; --ns) {
+    const int pref[4][2] = {{2, 1}, {1, 1}, {2, 0}, {1, 0}};      // {K/V buffers, staged RoPE}
+    for (const auto& pr : pref) {
         int off = 0;
         T.off_bhi = off; off += atoms;
         T.off_blo = off; off += atoms;
@@ -793,11 +1020,15 @@ inline TcGeom tc_geom(const ttkv_layout_t* lay, int G) {
         T.off_apv = off; off += APV_BYTES;
         T.off_bpv = off; off += BPV_BYTES;
         T.off_q = off; off += q_bytes;
-        T.off_red = off; off += red_bytes;
         T.off_lut = off; off += LUT_BYTES;
         T.off_misc = off; off += misc;
-        T.off_stage = off; off += ns * TM * T.srow + STAGE_PAD;
-        T.nstage = ns;
+        T.off_bt = off; off += BT_CAP * 4;
+        T.off_cf = off; off += TM * T.cf_pitch;
+        T.off_kv = off; off += pr[0] * TM * T.kvrow + KV_PAD;      // code windows read a few bytes past
+        off = round_up(off, 1024);                                 // a 128-byte-swizzled TMA box
+        T.off_rp = off; off += pr[1] * 2 * RP_BOX;
+        T.nkv = pr[0];
+        T.rope_smem = pr[1];
         T.smem = off + 1024;
         if (T.smem <= 227 * 1024) return T;
     }

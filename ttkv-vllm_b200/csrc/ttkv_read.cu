@@ -17,8 +17,12 @@
 // This is vllm_ttkv/impl.py:511-540 (_decode_one) + krt_triton.py:66-151 (_krt_kernel) +
 // softmax + v_out_triton.py:51-118 (_v_out_kernel) for the decode, and impl.py:725-778 with
 // krt_triton.py:155-266 / v_out_triton.py:159-246 for the continuation, fused and batched.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cfloat>
+#include <cstring>
 #include <cmath>
 #include <mutex>
 
@@ -479,8 +483,10 @@ bool tc_serves(const ttkv_layout_t* lay, int HQ) {
 }
 
 // Splits for the tensor-core decode: one resident CTA per SM, 128-token tiles; minimise
-// waves x (tiles per CTA + the set-up of a CTA, about 3/4 of a tile).
-Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads) {
+// waves x (tiles per CTA + the set-up of a CTA, about 3/4 of a tile). A split spans at most
+// tc::BT_CAP blocks of `block_size` tokens (the block-table slice a CTA caches); block_size 1 gives
+// the most splits, so a workspace sized for it covers every block size.
+Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads, int block_size) {
     Plan pl{};
     const int G = HQ / lay->H;
     pl.qb = 1;
@@ -490,9 +496,11 @@ Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int
     const int sms = sm_count();
     double best = 1e30;
     int best_s = 1;
-    for (int s = 1; s <= std::min(tiles, 64); ++s) {
+    for (int s = 1; s <= tiles; ++s) {
         const int waves = (pairs * s + sms - 1) / sms;
         const int per = (tiles + s - 1) / s;
+        if ((per * tc::TM + block_size - 1) / block_size + 1 > tc::BT_CAP) continue;
+        if (s > 64 && best < 1e30) break;
         const double cost = double(waves) * (per + 0.75);
         if (cost < best) { best = cost; best_s = s; }
     }
@@ -563,30 +571,65 @@ int launch_g(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     return check_launch("merge_kernel");
 }
 
+// A 2-D TMA map: `rows` rows of `d0` elements of `dt`, `stride` bytes apart; boxes of b0 x b1
+// elements, swizzled by the box's inner width (16 bytes: none). False if the driver's encoder is
+// unavailable or refuses the tensor.
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t d0, uint64_t rows,
+               uint64_t stride, uint32_t b0, uint32_t b1, int box_bytes) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        cudaGetLastError();
+    });
+    if (!encode || rows < 1) return false;
+    const CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : box_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : box_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    const cuuint64_t dims[2] = {d0, rows};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The TMA map of a tensor-core decode launch (the RoPE table, only when its rows are staged).
+bool tc_maps(tc::TcMaps* M, const tc::TcGeom& T, const ReadParams& P) {
+    memset(M, 0, sizeof(*M));
+    if (!T.rope_smem) return true;
+    return encode_2d(&M->rope, CU_TENSOR_MAP_DATA_TYPE_UINT16, P.table, 128, uint64_t(P.table_rows), 256, 64, 128, 128);
+}
+
 template <int G>
-int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const Plan& pl, int n_reqs, cudaStream_t st) {
+int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
+                cudaStream_t st) {
     auto k = tc::decode_tc_kernel<G>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T.smem) != cudaSuccess)
         return fail(TTKV_ERR_CUDA, "shared memory %d bytes refused", T.smem);
     dim3 grid(pl.n_splits, P.n_heads, n_reqs);
-    k<<<grid, tc::NTHR, T.smem, st>>>(P, T);
+    k<<<grid, tc::NTHR, T.smem, st>>>(P, T, maps);
     if (int e = check_launch("decode_tc_kernel")) return e;
     dim3 mg(P.G, P.n_heads, n_reqs);
     merge_kernel<<<mg, 128, 0, st>>>(P);
     return check_launch("merge_kernel");
 }
 
-int launch_tc(const ReadParams& P, const ttkv_layout_t* lay, const Plan& pl, int n_reqs, cudaStream_t st) {
-    const tc::TcGeom T = tc::tc_geom(lay, P.G);
+int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
+              cudaStream_t st) {
     switch (P.G) {
-        case 1: return launch_tc_g<1>(P, T, pl, n_reqs, st);
-        case 2: return launch_tc_g<2>(P, T, pl, n_reqs, st);
-        case 3: return launch_tc_g<3>(P, T, pl, n_reqs, st);
-        case 4: return launch_tc_g<4>(P, T, pl, n_reqs, st);
-        case 5: return launch_tc_g<5>(P, T, pl, n_reqs, st);
-        case 6: return launch_tc_g<6>(P, T, pl, n_reqs, st);
-        case 7: return launch_tc_g<7>(P, T, pl, n_reqs, st);
-        case 8: return launch_tc_g<8>(P, T, pl, n_reqs, st);
+        case 1: return launch_tc_g<1>(P, T, maps, pl, n_reqs, st);
+        case 2: return launch_tc_g<2>(P, T, maps, pl, n_reqs, st);
+        case 3: return launch_tc_g<3>(P, T, maps, pl, n_reqs, st);
+        case 4: return launch_tc_g<4>(P, T, maps, pl, n_reqs, st);
+        case 5: return launch_tc_g<5>(P, T, maps, pl, n_reqs, st);
+        case 6: return launch_tc_g<6>(P, T, maps, pl, n_reqs, st);
+        case 7: return launch_tc_g<7>(P, T, maps, pl, n_reqs, st);
+        case 8: return launch_tc_g<8>(P, T, maps, pl, n_reqs, st);
     }
     return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
 }
@@ -617,7 +660,7 @@ extern "C" size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t 
     const Plan pl = make_plan(lay, n_reqs, HQ, 1, max_seq_len, head_hi - head_lo, false);
     size_t need = pl.part_o_bytes + pl.part_ml_bytes;
     if (tc_serves(lay, HQ)) {
-        const Plan pt = make_plan_tc(lay, n_reqs, HQ, max_seq_len, head_hi - head_lo);
+        const Plan pt = make_plan_tc(lay, n_reqs, HQ, max_seq_len, head_hi - head_lo, 1);
         need = std::max(need, pt.part_o_bytes + pt.part_ml_bytes);
     }
     return need;
@@ -650,15 +693,24 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                     max_seq_len - 1, (long long)rope->rows);
     if (batch->n_reqs == 0 || max_seq_len == 0) return TTKV_OK;
     const int n_heads = head_hi - head_lo;
-    const bool use_tc = !multi && tc_serves(lay, HQ) && rope->dtype != TTKV_F32 &&
-                        (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
-                        (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0;
-    const Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads)
+    // the tensor-core kernel divides token indices by the block size as a 32-bit multiply-high and
+    // stages slots with TMA maps (when the driver cannot encode them the fp32 kernel serves)
+    bool use_tc = !multi && tc_serves(lay, HQ) && rope->dtype != TTKV_F32 &&
+                  (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0 &&
+                  (int64_t(max_seq_len) + 256) * cache->block_size < (int64_t(1) << 30);
+    ReadParams P = base_params(lay, cache, batch, rope);
+    tc::TcGeom T{};
+    tc::TcMaps maps;
+    if (use_tc) {
+        T = tc::tc_geom(lay, HQ / lay->H);
+        use_tc = tc_maps(&maps, T, P);
+    }
+    const Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads, cache->block_size)
                            : make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
     if (pl.smem > 227 * 1024) return fail(TTKV_ERR_UNSUPPORTED, "r1=%d needs %zu B of shared memory", lay->r1, pl.smem);
     if (!workspace || ws_bytes < pl.part_o_bytes + pl.part_ml_bytes)
         return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, pl.part_o_bytes + pl.part_ml_bytes);
-    ReadParams P = base_params(lay, cache, batch, rope);
     P.q = q; P.q_dtype = q_dtype; P.q_stride = q_stride; P.HQ = HQ; P.G = HQ / lay->H;
     P.q_start = multi ? q_start : nullptr; P.q_len = multi ? q_len : nullptr;
     P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
@@ -667,7 +719,7 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
     P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (use_tc) return launch_tc(P, lay, pl, batch->n_reqs, st);
+    if (use_tc) return launch_tc(P, T, maps, pl, batch->n_reqs, st);
     return multi ? launch<true>(P, pl, batch->n_reqs, st) : launch<false>(P, pl, batch->n_reqs, st);
 }
 
