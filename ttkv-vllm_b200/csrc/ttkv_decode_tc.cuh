@@ -334,6 +334,13 @@ constexpr int HPW = (kMaxG + NWG - 1) / NWG;
 constexpr int MMA_TID = NTHR - 32;       // lane 0 of the last warp issues every MMA
 constexpr int RP_TID = NTHR - 64;        // lane 0 of the warp before it issues the RoPE loads
 
+// Max over the warp (sm_100a redux on fp32).
+__device__ __forceinline__ float warp_max(float v) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // Named barrier over the 128 threads of warpgroup `wg` (ids 1..4; 0 is __syncthreads).
 __device__ __forceinline__ void wg_sync(int wg) {
     asm volatile("bar.sync %0, 128;" :: "r"(wg + 1) : "memory");
@@ -651,9 +658,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const float scale = P.scale;
     const float4* qs4 = reinterpret_cast<const float4*>(qs);
 
-    float o[HPW], corr_prev[HPW];
+    float o[HPW], corr_prev[HPW], m_prev[HPW], lsum[HPW];
     #pragma unroll
-    for (int i = 0; i < HPW; ++i) { o[i] = 0.f; corr_prev[i] = 0.f; }
+    for (int i = 0; i < HPW; ++i) { o[i] = 0.f; corr_prev[i] = 0.f; m_prev[i] = -INFINITY; lsum[i] = 0.f; }
     uint32_t ph_r = 0, ph_pv = 0;
     bool r_pending = true, pv_pending = false;
 
@@ -859,7 +866,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             pend_rp = true;
         }
 
-        // ---- online softmax over the tile: warpgroup wg owns query heads wg, wg + NWG, ...
+        // ---- online softmax over the tile: warpgroup wg owns query heads wg, wg + NWG, ... The tile
+        // max is one warp reduction and one warpgroup barrier; each thread keeps the running sum
+        // of its own tokens (rescaled with the max), reduced once after the last tile
         if (wg < G) {
             float sc[HPW], m_new[HPW], corr[HPW];
             #pragma unroll
@@ -872,9 +881,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                     for (int c = 0; c < NWG; ++c) v += tmem_ld1(t_row + RED_COL + uint32_t(8 * c + g));
                     tmem_wait_ld();
                     sc[i] = valid ? v * scale : -INFINITY;
-                    float mxg = sc[i];
-                    #pragma unroll
-                    for (int off = 16; off; off >>= 1) mxg = fmaxf(mxg, __shfl_xor_sync(0xffffffffu, mxg, off));
+                    const float mxg = warp_max(sc[i]);
                     if (lane == 0) M->red_max[w & 3][g] = mxg;
                 }
             }
@@ -889,10 +896,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                     m_new[i] = fmaxf(m_old, tmax);
                     const float pg = (m_new[i] == -INFINITY || sc[i] == -INFINITY) ? 0.f : expf(sc[i] - m_new[i]);
                     corr[i] = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new[i]);
-                    float sum = pg;
-                    #pragma unroll
-                    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                    if (lane == 0) M->red_sum[w & 3][g] = sum;
+                    lsum[i] = fmaf(lsum[i], corr[i], pg);
                     // P' = p * V ruler as fp16 hi (column g) + lo (column G + g); this token is K index t
                     const float pv = pg * vrs;
                     const uint32_t hb = f16_bits(pv);
@@ -907,25 +911,21 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                     }
                 }
             }
-            wg_sync(wg);
-            if (t == 0) {
-                #pragma unroll
-                for (int i = 0; i < HPW; ++i) {
-                    const int g = wg + NWG * i;
-                    if (g < G) {
-                        const float tsum = M->red_sum[0][g] + M->red_sum[1][g] + M->red_sum[2][g] + M->red_sum[3][g];
-                        M->l[g] = M->l[g] * corr[i] + tsum;
-                        M->m[g] = m_new[i];
-                    }
-                }
-            }
             #pragma unroll
-            for (int i = 0; i < HPW; ++i) corr_prev[i] = corr[i];
+            for (int i = 0; i < HPW; ++i) { corr_prev[i] = corr[i]; m_prev[i] = m_new[i]; }
         }
         fence_async_smem();
         tc_before();
         __syncthreads();
         tc_after();
+        // running max of each query head (every thread of its warpgroup has read the old one)
+        if (wg < G && t == 0) {
+            #pragma unroll
+            for (int i = 0; i < HPW; ++i) {
+                const int g = wg + NWG * i;
+                if (g < G) M->m[g] = m_prev[i];
+            }
+        }
 
         // ---- MMA 2 of this tile: O^T = V^T . P', read back during the next tile
         if (tid == MMA_TID) issue_pv(taddr + PV_COL);
@@ -947,6 +947,19 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                     tmem_wait_ld();
                     o[i] = fmaf(o[i], corr_prev[i], dh + dl);
                 }
+            }
+        }
+    }
+    // the softmax denominators: each owning warp's token sums, added up across its warpgroup
+    if (wg < G) {
+        #pragma unroll
+        for (int i = 0; i < HPW; ++i) {
+            const int g = wg + NWG * i;
+            if (g < G) {
+                float sum = lsum[i];
+                #pragma unroll
+                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                if (lane == 0) M->red_sum[w & 3][g] = sum;
             }
         }
     }
@@ -976,7 +989,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     }
     if (tid < G) {
         P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
-        P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 1] = timed_out ? 0.f : M->l[tid];
+        const float l = M->red_sum[0][tid] + M->red_sum[1][tid] + M->red_sum[2][tid] + M->red_sum[3][tid];
+        P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 1] = timed_out ? 0.f : l;
     }
 }
 

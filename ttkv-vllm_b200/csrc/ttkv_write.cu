@@ -149,8 +149,15 @@ __global__ void __launch_bounds__(PROJ_WARPS * 32) project_kernel(const ProjPara
     }
     if (rr >= P.r1) return;
     const float* pv = P.pinvs + int64_t(di) * P.pinv_stride + int64_t(rr) * HD;
-    float acc = 0.f;
-    for (int m = L; m < HD; m += 32) acc = fmaf(m_s[m], pv[m], acc);
+    // four independent partial sums (HD = H*128 is a multiple of 128) keep four loads in flight
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int m = L; m < HD; m += 128) {
+        a0 = fmaf(m_s[m], pv[m], a0);
+        a1 = fmaf(m_s[m + 32], pv[m + 32], a1);
+        a2 = fmaf(m_s[m + 64], pv[m + 64], a2);
+        a3 = fmaf(m_s[m + 96], pv[m + 96], a3);
+    }
+    float acc = (a0 + a1) + (a2 + a3);
     #pragma unroll
     for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(FULL, acc, off);
     if (L == 0) P.c[int64_t(t) * P.r1 + rr] = acc;
@@ -240,7 +247,17 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
         if (P.decoders) {
             const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * kHeadDim + j;
             const int64_t stride = int64_t(P.H) * kHeadDim;
-            for (int rr = 0; rr < P.r1; ++rr) kd = fmaf(g_s[rr], dec[rr * stride], kd);
+            // four independent partial sums keep four decoder loads in flight
+            float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
+            int rr = 0;
+            for (; rr + 4 <= P.r1; rr += 4) {
+                k0 = fmaf(g_s[rr], dec[rr * stride], k0);
+                k1 = fmaf(g_s[rr + 1], dec[(rr + 1) * stride], k1);
+                k2 = fmaf(g_s[rr + 2], dec[(rr + 2) * stride], k2);
+                k3 = fmaf(g_s[rr + 3], dec[(rr + 3) * stride], k3);
+            }
+            for (; rr < P.r1; ++rr) k0 = fmaf(g_s[rr], dec[rr * stride], k0);
+            kd = (k0 + k1) + (k2 + k3);
         }
         const float kv = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + h * kHeadDim + j);
         r_s[j] = kv - kd;
