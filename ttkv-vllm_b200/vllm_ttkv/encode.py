@@ -20,6 +20,12 @@ from vllm_ttkv import ops
 from vllm_ttkv.layout import TTKLayout, config
 
 
+def active_config() -> dict:
+    """The allocation named by VLLM_TTKV_CONFIG (default `safe`), as used for every fit."""
+    import os
+    return config(os.environ.get("VLLM_TTKV_CONFIG", "safe"))
+
+
 def check_cfg_matches_layout(lay: TTKLayout, cfg: dict) -> None:
     """The layout must have been built from this allocation (vllm_ttkv/encode.py:103-135)."""
     want = dict(qbits=cfg["qbits"], res_k=max(int(lay.d * cfg["res_frac"]), 1),

@@ -138,10 +138,11 @@ def pool_for_layer(layer_name: str, lay: TTKLayout, device) -> DecoderPool:
     return pool
 
 
-def register_decoder(layer_name: str, key: int, decoder) -> None:
-    """Publish a request's fitted decoder for this layer (host registry + device pool)."""
+def register_decoder(layer_name: str, key: int, decoder, lay: TTKLayout | None = None) -> None:
+    """Publish a request's fitted decoder for this layer (host registry + device pool); `lay` is the
+    layer's layout when it does not come from the calibration table."""
     _DECODERS[(layer_name, key)] = decoder
-    lay = layout_for_layer(layer_name)
+    lay = lay if lay is not None else layout_for_layer(layer_name)
     if lay is not None and decoder.decoder_f.is_cuda:
         slot = request_slot(key, create=True)
         pool_for_layer(layer_name, lay, decoder.decoder_f.device).put(slot, decoder)
