@@ -1,8 +1,9 @@
 """Benchmark: batched TT-KV decode step on Llama-3.2-3B-shaped layers.
 
 One STEP = for each of the 28 layers: encode the step's new token of every request into its slot
-(frozen projection + residual/V select-pack, `ttkv_write_paged`) and read every request's whole
-store (`ttkv_decode_paged`: reconstruct, patch, rotate, score, online softmax, V readout).
+(frozen projection + residual/V select-pack in one clustered launch, `ttkv_write_paged`) and read
+every request's whole store (`ttkv_decode_paged`: reconstruct, patch, rotate, score, online
+softmax, V readout). Each layer's launches are replayed from a CUDA graph (`--no-graph`: eager).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -35,6 +36,12 @@ for _p in (ROOT, ROOT / "ttkv-vllm_b200"):
         sys.path.insert(0, str(_p))
 
 METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs peak"
+
+# DRAM bytes (read + write) of ONE decode launch, from the ncu capture summarised in
+# profiles/decode_tc_cfg1.md: layer 9 (r1 = 110) of this workload, 8 requests x 4323 rows.
+# The per-launch `traffic` of the roofline scales it by algorithmic bytes (the kernel reads each
+# slot byte once, so traffic grows in proportion to the rows and widths a launch reads).
+CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 36.4e6 + 0.004e6}
 
 
 def _peaks():
@@ -188,17 +195,82 @@ class Workload:
         io = 2 * self.B * (self.HQ * n_heads // self.H) * 128 * 2
         return self.B * self.max_seq * per_tok + dec + io
 
-    def step(self, head_lo=0, head_hi=8, gather=None):
+    def layer_step(self, l, head_lo=0, head_hi=8):
+        """One layer: write the step's token of every request, then read every request's store."""
         from vllm_ttkv import encode, ops
+        lay = self.layouts[l]
+        encode.write_frozen(self.caches[l], self.new_slots, self.k_new[l], self.v_new[l],
+                            self.dec_index, self.decoders[l], self.pinvT[l], lay)
+        ops.decode_paged(lay, self.caches[l], self.bs, self.block_table, self.seq_lens,
+                         self.decoders[l], self.dec_index, self.table, self.q[l], self.scale,
+                         self.out[l], self.max_seq, head_lo, head_hi)
+
+    def step(self, head_lo=0, head_hi=8, gather=None):
         for l in range(self.L):
-            lay = self.layouts[l]
-            encode.write_frozen(self.caches[l], self.new_slots, self.k_new[l], self.v_new[l],
-                                self.dec_index, self.decoders[l], self.pinvT[l], lay)
-            ops.decode_paged(lay, self.caches[l], self.bs, self.block_table, self.seq_lens,
-                             self.decoders[l], self.dec_index, self.table, self.q[l], self.scale,
-                             self.out[l], self.max_seq, head_lo, head_hi)
+            self.layer_step(l, head_lo, head_hi)
             if gather is not None:
                 gather(l)
+
+
+# ---------------------------------------------------------------------------- plugin e2e
+def plugin_e2e(wl, steps, warmup, device):
+    """The step through the reference-facing plugin, `TTKVAttentionImpl.forward`, once per layer:
+    the raw key handed over by the rotary capture's stash, q/k/v copied in from pinned host memory
+    and every layer's output copied back, one new metadata object (and step plan) per step.
+    Returns (ms per step, h2d bytes, d2h bytes)."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from vllm_ttkv import encode, metadata, patch, rope_store
+    from vllm_ttkv.impl import TTKVAttentionImpl
+    impl = TTKVAttentionImpl(wl.HQ, 128, wl.scale, wl.H)
+    keys = [int(x) for x in wl.block_table[:, 0].tolist()]
+    layers = []
+    for l in range(wl.L):
+        lay = wl.layouts[l]
+        layer = SimpleNamespace(layer_name=f"model.layers.{l}.self_attn.attn", ttkv_layout=lay,
+                                rotary_emb=SimpleNamespace(cos_sin_cache=wl.table))
+        for r in range(wl.B):
+            kd = encode.KDecoder(wl.decoders[l][r])
+            kd._pinvT = wl.pinvT[l][r]
+            rope_store.register_decoder(layer.layer_name, keys[r], kd, lay=lay)
+        page = wl.caches[l].view(-1, 1, wl.bs, wl.caches[l].shape[1])
+        layers.append((layer, page))
+    pin_q = [x.cpu().pin_memory() for x in wl.q]
+    pin_k = [x.cpu().pin_memory() for x in wl.k_new]
+    pin_v = [x.cpu().pin_memory() for x in wl.v_new]
+    pin_o = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in wl.out]
+    h2d = sum(x.numel() * x.element_size() for x in pin_q + pin_k + pin_v)
+    d2h = sum(x.numel() * x.element_size() for x in pin_o)
+    qsl_cpu = torch.arange(wl.B + 1, dtype=torch.int32)
+    qsl = qsl_cpu.to(device)
+
+    def step():
+        md = metadata.TTKVAttentionMetadata(
+            seq_lens=wl.seq_lens, slot_mapping=wl.new_slots, block_table=wl.block_table,
+            query_start_loc=qsl, query_start_loc_cpu=qsl_cpu, num_actual_tokens=wl.B,
+            max_query_len=1, max_seq_len=wl.max_seq, ttkv_serial=metadata.next_serial())
+        for l, (layer, page) in enumerate(layers):
+            wl.q[l].copy_(pin_q[l], non_blocking=True)
+            wl.k_new[l].copy_(pin_k[l], non_blocking=True)
+            wl.v_new[l].copy_(pin_v[l], non_blocking=True)
+            patch.stash_raw_k(layer.layer_name, wl.k_new[l], None, wl.table)
+            impl.forward(layer, wl.q[l], None, wl.v_new[l], page, md, wl.out[l])
+            pin_o[l].copy_(wl.out[l], non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    rope_store.clear_decoders()
+    rope_store.clear_stores()
+    return e0.elapsed_time(e1) / steps, h2d, d2h
 
 
 # ---------------------------------------------------------------------------- CPU baseline
@@ -266,7 +338,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=8)
@@ -274,6 +346,8 @@ def main():
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--cfg", default="safe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every layer eagerly instead of replaying per-layer CUDA graphs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -303,21 +377,44 @@ def main():
     wl = Workload(args.batch, args.ctx, r1s, args.cfg, device, torch.bfloat16, seed=0)
     setup_s = time.perf_counter() - t0
 
-    gather = None
+    G = wl.HQ // H
+    nh = head_hi - head_lo
+    shard = full = None
     if world > 1:
-        G = wl.HQ // H
-        nh = head_hi - head_lo
         shard = [torch.empty(wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
         full = [torch.empty(world, wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
 
-        def gather(l):
+    def layer_work(l):
+        """The layer's launches on this rank (what a layer graph holds): write, read, and the copy
+        of this rank's head outputs into the all-gather's send buffer."""
+        wl.layer_step(l, head_lo, head_hi)
+        if shard is not None:
             shard[l].copy_(wl.out[l][:, head_lo * G:head_hi * G])
-            dist.all_gather_into_tensor(full[l], shard[l])
+
+    graphs = None
 
     def run_steps(k):
         for _ in range(k):
-            wl.step(head_lo, head_hi, gather)
+            for l in range(wl.L):
+                if graphs is not None:
+                    graphs[l].replay()
+                else:
+                    layer_work(l)
+                if full is not None:                       # collectives stay outside the graphs
+                    dist.all_gather_into_tensor(full[l], shard[l])
 
+    run_steps(args.warmup)
+    if not args.no_graph:
+        # one CUDA graph per layer, captured after the warm-up allocated every workspace; the
+        # replays launch exactly the kernels the eager layer launches
+        torch.cuda.synchronize(device)
+        graphs = []
+        for l in range(wl.L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                layer_work(l)
+            graphs.append(g)
+        torch.cuda.synchronize(device)
     run_steps(args.warmup)
     torch.cuda.synchronize(device)
     if world > 1:
@@ -361,6 +458,9 @@ def main():
     dec_total_ms = sum(dec_ms) / reps                          # all layers' decode launches, per step
     alg_bytes = sum(wl.read_bytes(l, n_heads) for l in range(wl.L))
     achieved = alg_bytes / (dec_total_ms * 1e-3) / 1e9
+    # algorithmic reconstruction FLOPs, (cq*cs) @ D over the heads read (the fp16 hi/lo split of
+    # D doubles the tensor-core work actually issued; that is not counted)
+    recon_flops = sum(wl.B * wl.max_seq * 2 * wl.r1s[l] * n_heads * 128 for l in range(wl.L))
     hbm, tc, peak_kind = _peaks()
 
     # ---- e2e: the same step through the C-ABI with host buffers copied in and out every step
@@ -376,7 +476,7 @@ def main():
             wl.q[l].copy_(pin_q[l], non_blocking=True)
             wl.k_new[l].copy_(pin_k[l], non_blocking=True)
             wl.v_new[l].copy_(pin_v[l], non_blocking=True)
-        wl.step(head_lo, head_hi, gather)
+        run_steps(1)
         for l in range(wl.L):
             pin_o[l].copy_(wl.out[l], non_blocking=True)
 
@@ -396,6 +496,13 @@ def main():
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
 
+    plugin = None
+    if world == 1:
+        p_ms, p_h2d, p_d2h = plugin_e2e(wl, args.steps, args.warmup, device)
+        plugin = {"value": args.batch / (p_ms * 1e-3), "unit": "tok/s", "ms_per_step": p_ms,
+                  "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
+                  "api": "TTKVAttentionImpl.forward per layer (write + decode), new metadata per step"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         per = cpu_sample((args.batch, args.ctx, r1s, args.cfg), sample_layers=(9,))
@@ -405,7 +512,12 @@ def main():
                "sample": f"1 (request, layer) pair (layer 9, r1={r1s[9]}, n={args.ctx}): oracle "
                          f"frozen write of one token + decode read, scaled x{args.batch * len(r1s)}"}
 
-    launches = wl.L * 2 + wl.L * 2                                # write (project+pack) + read (split+merge)
+    # per layer: write (write_frozen_kernel) + read (decode_tc_kernel + merge_kernel)
+    launches = wl.L * 3
+    cap = CAPTURED_LAUNCH["layer"]
+    traffic = None
+    if cap < wl.L and n_heads == H:
+        traffic = CAPTURED_LAUNCH["dram_bytes"] * (alg_bytes / wl.L) / wl.read_bytes(cap, n_heads)
     if rank == 0:
         line = {"metric": METRIC, "value": args.batch / (ms * 1e-3), "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -418,18 +530,29 @@ def main():
                            "kv_heads_per_rank": n_heads,
                            "l2": "inputs larger than L2 (slots %.0f MB/step)" % (
                                sum(wl.slot_bytes(l) for l in range(wl.L)) / 1e6),
-                           "parallelism": f"kv-head shard x{world}" if world > 1 else "single"},
+                           "parallelism": f"kv-head shard x{world}" if world > 1 else "single",
+                           "launch": "one CUDA graph per layer (write + read)" if graphs else "eager"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                             "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
-                             "kernel": "attn_split_kernel + merge_kernel (ttkv_decode_paged)",
+                             "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
+                             "kernel": "decode_tc_kernel<3> + merge_kernel (ttkv_decode_paged)",
+                             "alg_bytes_per_launch": alg_bytes / wl.L,
+                             "launch_us": dec_total_ms * 1e3 / wl.L,
+                             "traffic_source": "ncu dram__bytes_read+write of the layer-%d launch, "
+                                               "scaled per launch by algorithmic bytes" % cap,
+                             "tensor_tflops": recon_flops / (dec_total_ms * 1e-3) / 1e12,
+                             "tensor_frac": recon_flops / (dec_total_ms * 1e-3) / 1e12 / tc,
                              "decode_ms_per_step": dec_total_ms},
                 "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
                 "gpu_launches": launches * args.steps, "clocks": clocks,
                 "setup_s": round(setup_s, 1), "fit_s": round(wl.fit_s, 1)}
+        if plugin is not None:
+            line["e2e_plugin"] = plugin
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
+    graphs = None
+    torch.cuda.synchronize(device)
     if world > 1:
         dist.destroy_process_group()
 

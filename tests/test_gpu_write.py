@@ -149,8 +149,11 @@ def test_write_given_coefficients_is_bit_exact():
     assert (got == want).mean() > 0.995
 
 
-def test_frozen_write_matches_oracle_end_to_end():
-    st, g, K, V, tok_dec = _frozen_case(seed=1, n_tok=9)
+@pytest.mark.parametrize("r1", [32, 143, 208])
+def test_frozen_write_matches_oracle_end_to_end(r1):
+    """r1 <= 200: the fused cluster write; 208: its two slices exceed shared memory, so the
+    two-launch write (projection, then encode + pack) runs."""
+    st, g, K, V, tok_dec = _frozen_case(seed=1, n_tok=9, r1=r1)
     got = _write_gpu(g, K, V, tok_dec, st["decoders"], pinvT=st["pinvT"])
     want = []
     for t in range(K.shape[1]):

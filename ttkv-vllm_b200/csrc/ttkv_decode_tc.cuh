@@ -43,11 +43,6 @@ constexpr int APV_BYTES = 32768;        // V^T: 128 tokens x 128 lanes fp16
 constexpr int BPV_BYTES = 4096;         // P': 16 rows x 128 tokens fp16
 constexpr int LUT_BYTES = 2 * 16 * 16;  // K and V shift tables, 16 nibbles x 4 lanes x u32
 constexpr int STAGE_PAD = 16;           // code windows may read up to 7 bytes past a field
-constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s at 2 GHz
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 // Shared-memory matrix descriptor for tcgen05 (start, LBO, SBO in 16-byte units; version 1;
 // layout type 2 = 128-byte swizzle). Field positions follow the sm_100 UMMA descriptor.
@@ -62,9 +57,6 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b
            (uint32_t(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void fence_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tc_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -83,28 +75,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  :: "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-    return ok != 0;
-}
-
-// Bounded wait for an mbarrier phase: false after ~2 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!mbar_try(bar, parity))
-        if (clock64() - t0 > WAIT_CYCLES) return false;
-    return true;
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
@@ -146,34 +116,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-
-// The one arrival of a TMA phase, announcing the bytes its copies will deliver.
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-// Arrive on `bar` once every earlier cp.async of this thread has landed (no pending-count
-// increment: the barrier is initialised with one arrival per thread).
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
-}
-
-// Fetch a TMA map's descriptor ahead of its first use.
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// 2-D tiled TMA load of the box at element (x, y) of `map` into this CTA's shared memory, its bytes
-// counted on `bar`. No multicast.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // Byte offset of (row, 16-byte chunk) in a K-major SW128 atom column of 128-byte rows.
 __device__ __forceinline__ uint32_t kmajor_off(int row, int chunk) {

@@ -26,6 +26,7 @@
 #include <cmath>
 #include <mutex>
 
+#include "ttkv_async.cuh"
 #include "ttkv_common.cuh"
 
 namespace ttkv {
@@ -569,33 +570,6 @@ int launch_g(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     dim3 mg(P.qmax * P.G, P.n_heads, n_reqs);
     merge_kernel<<<mg, 128, 0, st>>>(P);
     return check_launch("merge_kernel");
-}
-
-// A 2-D TMA map: `rows` rows of `d0` elements of `dt`, `stride` bytes apart; boxes of b0 x b1
-// elements, swizzled by the box's inner width (16 bytes: none). False if the driver's encoder is
-// unavailable or refuses the tensor.
-bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t d0, uint64_t rows,
-               uint64_t stride, uint32_t b0, uint32_t b1, int box_bytes) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-        cudaGetLastError();
-    });
-    if (!encode || rows < 1) return false;
-    const CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : box_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
-                                : box_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
-    const cuuint64_t dims[2] = {d0, rows};
-    const cuuint64_t strides[1] = {stride};
-    const cuuint32_t box[2] = {b0, b1};
-    const cuuint32_t estr[2] = {1, 1};
-    return encode(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // The TMA map of a tensor-core decode launch (the RoPE table, only when its rows are staged).

@@ -17,6 +17,7 @@
 #include <cfloat>
 #include <cmath>
 
+#include "ttkv_async.cuh"
 #include "ttkv_common.cuh"
 
 namespace ttkv {
@@ -116,6 +117,7 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
 }
 
 // ------------------------------------------------------------------ frozen projection
+// (the two-launch frozen write, for pools the fused kernel cannot map)
 struct ProjParams {
     int H, r1;
     const void* k;
@@ -282,6 +284,184 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
     }
 }
 
+// ------------------------------------------------------------------ fused frozen write
+// The frozen write of a token in ONE launch: a cluster of H CTAs per token, CTA h = KV head h.
+//
+//   copy      two 2-D TMA boxes (no multicast) bring this head's 128 columns of the request's
+//             transposed pseudo-inverse and of its decoder, r1 rows each, into shared memory;
+//             meanwhile warp 7 packs the head's V row and the head's K row is staged
+//   project   partial coefficients over this head's columns, c_h[i] = sum_j K[h*d+j] pinvT[i][h*d+j]
+//   reduce    c[i] = sum over the cluster's CTAs of c_h[i], read from their shared memory (DSMEM),
+//             in rank order, so every CTA holds the same c
+//   quantise  cs = amax|c| * fp32(1/127) (0 -> 1), cq = clamp(rint(c / cs))   (encode.py:329-333)
+//   residual  R = K - (cq*cs) @ decoder[:, h]                                  (encode.py:335-336)
+//   pack      the K residual row; CTA 0 also writes the coefficient block and its ruler
+//
+// Every CTA of a cluster handles the same token, so the early exits (a bad slot or decoder index)
+// are taken by all of them together, before the first cluster barrier.
+struct FrozenParams {
+    int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
+    uint8_t* cache;
+    int64_t n_slots, row_bytes;
+    const int64_t* slots;
+    const void* k;
+    int k_dtype;
+    int64_t k_stride;
+    const void* v;
+    int v_dtype;
+    int64_t v_stride;
+    const int32_t* tok_dec;
+    int n_decoders;
+    int32_t* status;
+};
+
+// The decoder pool and the pinv pool as 2-D fp32 tensors [n_decoders * r1 rows, H*d], boxes of
+// 128 columns x r1 rows.
+struct FrozenMaps {
+    CUtensorMap pinv, dec;
+};
+
+constexpr int WF_THREADS = 256;
+constexpr size_t kFusedWriteSmemMax = 200 * 1024;      // the two slices, r1 <= 200
+constexpr int32_t kMaxGridY = 65535;
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// This CTA's shared-memory word `p` as seen from CTA `rank` of the cluster.
+__device__ __forceinline__ float ld_peer(const float* p, int rank) {
+    uint32_t a;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+
+// grid (H, n_tok), cluster (H, 1, 1), 256 threads; dynamic shared memory 2 * r1 * 512 bytes.
+__global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenParams P,
+                                                                  const __grid_constant__ FrozenMaps M) {
+    extern __shared__ __align__(128) unsigned char wf_dyn[];
+    float* pinv_s = reinterpret_cast<float*>(wf_dyn);       // [r1][128]
+    float* dec_s = pinv_s + P.r1 * kHeadDim;                 // [r1][128]
+    __shared__ __align__(16) float k_s[kHeadDim];
+    __shared__ float cpart_s[kMaxRank];                      // read by every CTA of the cluster
+    __shared__ float g_s[kMaxRank];
+    __shared__ int8_t cq_s[kMaxRank];
+    __shared__ float kd_s[2][kHeadDim];
+    __shared__ uint8_t codes_s[2][128];
+    __shared__ float wmax_s[WF_THREADS / 32];
+    __shared__ float cs_s;
+    __shared__ __align__(8) uint64_t bar;
+
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
+    const int64_t slot = P.slots[t];
+    if (slot < 0 || slot >= P.n_slots) {
+        if (tid == 0 && h == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
+        return;
+    }
+    const int di = P.tok_dec[t];
+    if (di < 0 || di >= P.n_decoders) {
+        if (tid == 0 && h == 0) report(P.status, TTKV_STATUS_DECODER);
+        return;
+    }
+    uint8_t* row = P.cache + slot * P.row_bytes;
+
+    if (tid == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    if (tid == 0) {
+        mbar_expect_tx(&bar, uint32_t(2 * P.r1 * kHeadDim * sizeof(float)));
+        tma_load_2d(pinv_s, &M.pinv, h * kHeadDim, di * P.r1, &bar);
+        tma_load_2d(dec_s, &M.dec, h * kHeadDim, di * P.r1, &bar);
+    }
+    if (tid < kHeadDim) k_s[tid] = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + h * kHeadDim + tid);
+    if (w == 7) {                                            // V needs nothing from the projection
+        float x[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)
+            x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
+        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + h * P.v_row, codes_s[1]);
+    }
+    const bool landed = mbar_wait(&bar, 0);
+    const bool bad = __syncthreads_or(!landed);              // also publishes k_s
+    if (bad && tid == 0) report(P.status, TTKV_STATUS_TIMEOUT);
+
+    // ---- this head's partial coefficients: warp w takes rows w, w+8, ...
+    if (!bad) {
+        const float4 kv = reinterpret_cast<const float4*>(k_s)[L];
+        for (int i = w; i < P.r1; i += WF_THREADS / 32) {
+            const float4 p = reinterpret_cast<const float4*>(pinv_s + i * kHeadDim)[L];
+            float a = kv.x * p.x;
+            a = fmaf(kv.y, p.y, a);
+            a = fmaf(kv.z, p.z, a);
+            a = fmaf(kv.w, p.w, a);
+            #pragma unroll
+            for (int off = 16; off; off >>= 1) a += __shfl_xor_sync(FULL, a, off);
+            if (L == 0) cpart_s[i] = a;
+        }
+    }
+    cluster_arrive();
+    cluster_wait();                                          // every head's partials are visible
+
+    float c = 0.f;
+    if (!bad && tid < P.r1)
+        for (int j = 0; j < P.H; ++j) c += ld_peer(&cpart_s[tid], j);
+    cluster_arrive();                                        // done reading the peers (waited at exit)
+
+    // ---- quantise the coefficients (every CTA, identical inputs -> identical codes)
+    float a = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(fabsf(c))));
+    if (L == 0) wmax_s[w] = a;
+    __syncthreads();
+    if (tid == 0) {
+        float amax = wmax_s[0];
+        #pragma unroll
+        for (int i = 1; i < WF_THREADS / 32; ++i) amax = fmaxf(amax, wmax_s[i]);
+        const float cs = __fmul_rn(amax, inv_ruler(8));
+        cs_s = (cs == 0.f) ? 1.f : cs;
+    }
+    __syncthreads();
+    const float cs = cs_s;
+    if (tid < P.r1) {
+        const float qf = fminf(fmaxf(rintf(__fdiv_rn(c, cs)), -128.f), 127.f);
+        cq_s[tid] = int8_t(qf);
+        g_s[tid] = qf * cs;
+    }
+    __syncthreads();
+
+    // ---- (cq*cs) @ decoder[:, h]: the two thread halves take the two halves of the rows
+    if (!bad) {
+        const int half = tid >> 7, j = tid & 127;
+        const int mid = (P.r1 + 1) >> 1;
+        const int i0 = half ? mid : 0, i1 = half ? P.r1 : mid;
+        float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
+        int i = i0;
+        for (; i + 4 <= i1; i += 4) {
+            k0 = fmaf(g_s[i], dec_s[i * kHeadDim + j], k0);
+            k1 = fmaf(g_s[i + 1], dec_s[(i + 1) * kHeadDim + j], k1);
+            k2 = fmaf(g_s[i + 2], dec_s[(i + 2) * kHeadDim + j], k2);
+            k3 = fmaf(g_s[i + 3], dec_s[(i + 3) * kHeadDim + j], k3);
+        }
+        for (; i < i1; ++i) k0 = fmaf(g_s[i], dec_s[i * kHeadDim + j], k0);
+        kd_s[half][j] = (k0 + k1) + (k2 + k3);
+    }
+    __syncthreads();
+
+    if (!bad && w == 0) {
+        float x[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = k_s[4 * L + i] - (kd_s[0][4 * L + i] + kd_s[1][4 * L + i]);
+        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + h * P.k_row, codes_s[0]);
+    } else if (!bad && w == 1 && h == 0) {
+        for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
+        if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs);
+    }
+    cluster_wait();                                          // no CTA leaves while a peer reads it
+    if (bad) mbar_wait(&bar, 0);                             // let late copies land (bounded) first
+}
+
 // ------------------------------------------------------------------ standalone rows
 struct RowsParams {
     uint8_t* cache;
@@ -398,6 +578,87 @@ int check_cache(const ttkv_cache_t* cache, int need) {
     return TTKV_OK;
 }
 
+// The fused frozen write when the pools map as 2-D TMA tensors and the slices fit in shared
+// memory: returns 0 when launched, a negative error code, or 1 to take the two-launch path.
+int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_cache_t* cache, const int64_t* slots,
+                        int32_t n_tok, const void* k, int32_t k_dtype, int64_t k_stride, const void* v,
+                        int32_t v_dtype, int64_t v_stride, const int32_t* tok_dec, const float* decoders,
+                        int64_t dec_stride, const float* pinvs, int64_t pinv_stride, int32_t n_decoders,
+                        int32_t* status, cudaStream_t st) {
+    const int64_t cols = int64_t(lay->H) * kHeadDim;
+    const size_t dyn = size_t(2) * lay->r1 * kHeadDim * sizeof(float);
+    if (lay->H > 8 || dec_stride != lay->r1 * cols || pinv_stride != lay->r1 * cols ||
+        (reinterpret_cast<uintptr_t>(decoders) & 15) || (reinterpret_cast<uintptr_t>(pinvs) & 15) ||
+        dyn > kFusedWriteSmemMax)
+        return 1;
+    FrozenMaps maps;
+    const uint64_t rows = uint64_t(n_decoders) * lay->r1;
+    if (!encode_2d(&maps.pinv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pinvs, cols, rows, cols * 4, kHeadDim,
+                   lay->r1, 0) ||
+        !encode_2d(&maps.dec, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, decoders, cols, rows, cols * 4, kHeadDim,
+                   lay->r1, 0))
+        return 1;
+    if (cudaFuncSetAttribute(write_frozen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    {   // the H CTAs of a cluster must fit on the GPU at once (asked once per shape)
+        static int last_h = -1;
+        static size_t last_dyn = 0;
+        static bool last_ok = false;
+        if (lay->H != last_h || dyn != last_dyn) {
+            cudaLaunchConfig_t q{};
+            q.gridDim = dim3(lay->H, 1);
+            q.blockDim = dim3(WF_THREADS);
+            q.dynamicSmemBytes = dyn;
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = lay->H;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int n = 0;
+            last_ok = cudaOccupancyMaxActiveClusters(&n, write_frozen_kernel, &q) == cudaSuccess && n > 0;
+            cudaGetLastError();
+            last_h = lay->H;
+            last_dyn = dyn;
+        }
+        if (!last_ok) return 1;
+    }
+    FrozenParams P{};
+    P.H = lay->H; P.r1 = lay->r1; P.res_k = lay->res_k; P.res_bits = lay->res_bits;
+    P.v_lanes = lay->v_lanes; P.v_bits = lay->v_bits; P.coeff_bytes = lay->coeff_bytes;
+    P.k_row = lay->k_row_bytes; P.v_row = lay->v_row_bytes; P.v_offset = lay->v_offset;
+    P.cache = cache->base; P.n_slots = cache->n_slots; P.row_bytes = cache->row_bytes;
+    P.k_dtype = k_dtype; P.k_stride = k_stride; P.v_dtype = v_dtype; P.v_stride = v_stride;
+    P.n_decoders = n_decoders; P.status = status;
+    const int esz_k = k_dtype == TTKV_F32 ? 4 : 2, esz_v = v_dtype == TTKV_F32 ? 4 : 2;
+    for (int32_t t0 = 0; t0 < n_tok; t0 += kMaxGridY) {      // grid.y is at most 65535 tokens
+        const int32_t nt = n_tok - t0 < kMaxGridY ? n_tok - t0 : kMaxGridY;
+        P.slots = slots + t0;
+        P.tok_dec = tok_dec + t0;
+        P.k = static_cast<const char*>(k) + int64_t(t0) * k_stride * esz_k;
+        P.v = static_cast<const char*>(v) + int64_t(t0) * v_stride * esz_v;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(lay->H, nt);
+        cfg.blockDim = dim3(WF_THREADS);
+        cfg.dynamicSmemBytes = dyn;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = lay->H;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, write_frozen_kernel, P, maps);
+        if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "write_frozen_kernel: %s", cudaGetErrorString(e));
+    }
+    return 0;
+}
+
 }  // namespace
 }  // namespace ttkv
 
@@ -441,6 +702,12 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
         return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes,
                     ttkv_write_workspace_bytes(lay, n_tok));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (frozen) {
+        const int r = launch_frozen_fused(lay, cache, slot_mapping, n_tok, k, k_dtype, k_stride, v, v_dtype,
+                                          v_stride, tok_dec, decoders, dec_stride, pinvs, pinv_stride,
+                                          n_decoders, status, st);
+        if (r <= 0) return r;                                // launched (0) or failed (< 0)
+    }
     float* c = nullptr;
     if (frozen) {
         ProjParams pp{};

@@ -68,7 +68,7 @@ class StepPlan:
     """Everything about a step that does not depend on the layer, read back and checked once."""
 
     __slots__ = ("serial", "qsl", "seq_lens", "n_reqs", "n_dec", "prefills", "keys", "block_size",
-                 "n_slots", "_dec_rows", "_cont")
+                 "n_slots", "_dec_rows", "_cont", "_frozen")
 
     def __init__(self, md, block_size: int, n_slots: int, serial: int):
         if md.query_start_loc is None or md.seq_lens is None or md.block_table is None:
@@ -103,6 +103,25 @@ class StepPlan:
         validate_slot_ids(md.slot_mapping, self.qsl[-1], n_slots)
         self._dec_rows = None
         self._cont = None
+        self._frozen = {}
+
+    def frozen_write(self, frozen: tuple, device):
+        """(token rows, pool row per token) of the write for the frozen requests `frozen` (request,
+        pool row) pairs; the same for every layer of the step, so built once. Token rows are a
+        (start, end) range when the requests are contiguous, else an index tensor."""
+        got = self._frozen.get(frozen)
+        if got is None:
+            reqs = [r for r, _ in frozen]
+            counts = torch.tensor([self.qsl[r + 1] - self.qsl[r] for r in reqs])
+            rows = torch.repeat_interleave(torch.tensor([p for _, p in frozen], dtype=torch.int32),
+                                           counts).to(device)
+            if reqs == list(range(reqs[0], reqs[-1] + 1)):
+                tok = (self.qsl[reqs[0]], self.qsl[reqs[-1] + 1])
+            else:
+                tok = torch.cat([torch.arange(self.qsl[r], self.qsl[r + 1]) for r in reqs]).to(device)
+            got = (tok, rows)
+            self._frozen[frozen] = got
+        return got
 
     def dec_rows(self, device) -> torch.Tensor:
         """Pool rows of the decode requests (the same row in every layer)."""
@@ -226,23 +245,14 @@ class TTKVAttentionImpl(_ImplBase):
             register_decoder(name, k, fk.decoder, lay=lay)
         if frozen:
             pool = pool_for_layer(name, lay, device)
-            first, last = frozen[0][0], frozen[-1][0]
-            contiguous = [r for r, _ in frozen] == list(range(first, last + 1))
-            if contiguous:                          # the usual case: every request frozen, in order
-                s, e = plan.qsl[first], plan.qsl[last + 1]
-                rows = torch.repeat_interleave(
-                    torch.tensor([p for _, p in frozen], dtype=torch.int32),
-                    torch.tensor([plan.qsl[r + 1] - plan.qsl[r] for r, _ in frozen])).to(device)
-                encode.write_frozen(cache, slots[s:e].contiguous(), K[s:e], V[s:e], rows,
-                                    pool.decoders, pool.pinvT, lay)
+            tok, rows = plan.frozen_write(tuple(frozen), device)
+            if isinstance(tok, tuple):              # the usual case: every request frozen, in order
+                s, e = tok
+                encode.write_frozen(cache, slots[s:e], K[s:e], V[s:e], rows, pool.decoders,
+                                    pool.pinvT, lay)
             else:
-                idx = torch.cat([torch.arange(plan.qsl[r], plan.qsl[r + 1]) for r, _ in frozen]).to(device)
-                rows = torch.repeat_interleave(
-                    torch.tensor([p for _, p in frozen], dtype=torch.int32),
-                    torch.tensor([plan.qsl[r + 1] - plan.qsl[r] for r, _ in frozen])).to(device)
-                encode.write_frozen(cache, slots.index_select(0, idx).contiguous(),
-                                    K.index_select(0, idx), V.index_select(0, idx), rows,
-                                    pool.decoders, pool.pinvT, lay)
+                encode.write_frozen(cache, slots.index_select(0, tok), K.index_select(0, tok),
+                                    V.index_select(0, tok), rows, pool.decoders, pool.pinvT, lay)
         return table
 
     # ------------------------------------------------------------------ the reads
