@@ -367,29 +367,24 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    from vllm_ttkv.shard import HeadShard
     H = 8
-    if H % world:
-        raise SystemExit(f"{world} ranks do not divide the {H} KV heads")
-    head_lo, head_hi = rank * H // world, (rank + 1) * H // world
+    sh = HeadShard(H, 24, world, rank) if world > 1 else None    # raises unless N divides the heads
+    head_lo, head_hi = (sh.head_lo, sh.head_hi) if sh else (0, H)
 
     r1s = (S.LLAMA32_3B_R1 * ((args.layers + 27) // 28))[:args.layers]
     t0 = time.perf_counter()
     wl = Workload(args.batch, args.ctx, r1s, args.cfg, device, torch.bfloat16, seed=0)
     setup_s = time.perf_counter() - t0
 
-    G = wl.HQ // H
-    nh = head_hi - head_lo
-    shard = full = None
-    if world > 1:
-        shard = [torch.empty(wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
-        full = [torch.empty(world, wl.B, G * nh, 128, dtype=wl.dtype, device=device) for _ in range(wl.L)]
+    bufs = [sh.buffers(wl.B, 128, wl.dtype, device) for _ in range(wl.L)] if sh else None
 
     def layer_work(l):
         """The layer's launches on this rank (what a layer graph holds): write, read, and the copy
-        of this rank's head outputs into the all-gather's send buffer."""
+        of this rank's query heads into the all-gather's send buffer."""
         wl.layer_step(l, head_lo, head_hi)
-        if shard is not None:
-            shard[l].copy_(wl.out[l][:, head_lo * G:head_hi * G])
+        if sh is not None:
+            sh.pack(wl.out[l], bufs[l][0])
 
     graphs = None
 
@@ -400,8 +395,9 @@ def main():
                     graphs[l].replay()
                 else:
                     layer_work(l)
-                if full is not None:                       # collectives stay outside the graphs
-                    dist.all_gather_into_tensor(full[l], shard[l])
+                if sh is not None:                         # collectives stay outside the graphs
+                    sh.gather(*bufs[l])
+                    sh.assemble(bufs[l][1], wl.out[l])     # every rank ends with all heads
 
     run_steps(args.warmup)
     if not args.no_graph:

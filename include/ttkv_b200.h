@@ -192,9 +192,13 @@ int ttkv_prefill_cont_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
  *   V        -- top-v_lanes per head row, quantised and packed.
  * Byte-identical to the reference's fused writer (vllm_ttkv/encode.py:511-579 _fused_write,
  * select_triton.py:157-232) given the same fp32 coefficients and residual; ties in magnitude
- * keep the lowest lane. Replaces encode_frozen(_batch) + _fused_write for a whole layer in two
- * launches instead of ~20 launches per request. The frozen path needs
- * ttkv_write_workspace_bytes(lay, n_tok) bytes of workspace (the projected coefficients). */
+ * keep the lowest lane. Replaces encode_frozen(_batch) + _fused_write for a whole layer in one
+ * launch instead of ~20 launches per request: on the frozen path a cluster of H CTAs per token
+ * (one per KV head) projects, reduces the coefficients over the cluster's shared memory,
+ * quantises and packs; when the pools' [r1, 128] slices do not fit shared memory (r1 > 200) or
+ * are not 16-byte aligned with the pool stride r1*H*d, a projection launch and a pack launch do
+ * the same. The frozen path needs ttkv_write_workspace_bytes(lay, n_tok) bytes of workspace
+ * (the projected coefficients of the two-launch form). */
 size_t ttkv_write_workspace_bytes(const ttkv_layout_t* lay, int32_t n_tok);
 int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
                      const int64_t* slot_mapping, int32_t n_tok,

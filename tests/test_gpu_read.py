@@ -99,6 +99,21 @@ def test_decode_long_context_split_merge():
     assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
 
 
+def test_decode_schedule_over_more_requests_than_one_scan_chunk():
+    """520 short requests: the device-side schedule sums the batch's tiles 512 requests at a time,
+    and most CTAs get runs that cross several (request, head) pairs."""
+    lens = np.random.default_rng(8).integers(1, 300, 520)
+    st = stores.make_store(8, lens, cfg="safe", r1=24)
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_decode_block_size_one_grows_the_grid_in_waves():
+    """With one token per block a CTA's cached block-table slice covers only 3 tiles, so 4 x 2100
+    tokens x 8 heads (544 tiles) need more CTAs than SMs."""
+    st = stores.make_store(9, [2100, 2100, 1900, 2050], cfg="safe", r1=32, block_size=1)
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
 def test_rotation_is_per_row_negative_control():
     """Reading with the angle table shifted by one position must change the scores a lot --
     the failure this path is shaped around is a silent mis-rotation (reference.py:1-30)."""

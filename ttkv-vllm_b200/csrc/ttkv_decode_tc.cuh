@@ -2,9 +2,13 @@
 //
 // Included by ttkv_read.cu inside its anonymous namespace (shares ReadParams and the merge).
 //
-// One CTA = (request, KV head, token split), four warpgroups (512 threads). Token t of the
-// current 128-token tile is TMEM lane t; warpgroup c handles a quarter of that token's 128 head
-// lanes (the RoPE pairs j, j+64 for j in [16c, 16c+16) of K, the V lanes [32c, 32c+32)). Per tile:
+// The launch is one CTA per SM (more only when a block-table slice would overflow), four warpgroups
+// (512 threads) each. The work is the list of (request, KV head, 128-token tile) units, request-
+// major; CTA c takes the c-th equal share of it, computed on the device from seq_lens, and walks
+// it as segments, one per (request, KV head) it touches, each leaving a partial (o, max, sum) that
+// merge_sk_kernel combines. Within a segment, token t of the current tile is TMEM lane t;
+// warpgroup c handles a quarter of that token's 128 head lanes (the RoPE pairs j, j+64 for j in
+// [16c, 16c+16) of K, the V lanes [32c, 32c+32)). Per tile:
 //
 //   stage    16-byte cp.async copies, chunk-fastest over the tile's tokens, completing on an
 //            mbarrier per unit: this head's K and V rows (two buffers, two tiles ahead), the
@@ -267,6 +271,9 @@ struct TcMisc {
     float m[kMaxG];
     float l[kMaxG];
     float maxabs[NTHR / 32];
+    int scan[NTHR / 32];
+    int sched_r;
+    long long sched_before;
     uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2];
     uint32_t tmem_base;
 };
@@ -274,6 +281,8 @@ struct TcMisc {
 // Query heads whose softmax a warpgroup owns: g = wg + NWG * i, i < HPW.
 constexpr int HPW = (kMaxG + NWG - 1) / NWG;
 constexpr int MMA_TID = NTHR - 32;       // lane 0 of the last warp issues every MMA
+constexpr int MAX_R1 = 192;              // largest r1 the tensor-core decode serves
+constexpr int DEC_CHUNKS = (MAX_R1 / 8 + NWG - 1) / NWG;   // 8-row decoder chunks per warpgroup
 constexpr int RP_TID = NTHR - 64;        // lane 0 of the warp before it issues the RoPE loads
 
 // Max over the warp (sm_100a redux on fp32).
@@ -306,6 +315,33 @@ __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Tiles of a request (a request with no rows has none).
+__device__ __forceinline__ int req_tiles(int seq) { return seq > 0 ? (seq + TM - 1) / TM : 0; }
+
+// Exclusive prefix sum of v over the CTA's threads in thread order, and the CTA's total. Every
+// thread of the CTA calls it; `wsum` is NTHR / 32 ints of shared memory.
+__device__ __forceinline__ int cta_scan(int v, int* wsum, int& total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = v;
+    #pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    int pre = 0;
+    total = 0;
+    #pragma unroll
+    for (int i = 0; i < NTHR / 32; ++i) {
+        const int sw = wsum[i];
+        if (i < w) pre += sw;
+        total += sw;
+    }
+    __syncthreads();
+    return pre + x - v;
+}
+
 template <int G>
 __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, const TcGeom T,
                                                              const __grid_constant__ TcMaps maps) {
@@ -327,100 +363,85 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
 
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const int wg = tid >> 7, t = tid & 127;
-    const int split = blockIdx.x, hl = blockIdx.y, r = blockIdx.z;
-    const int h = P.head_lo + hl;
-    const int seq = P.seq_lens[r];
+    const int nh = P.n_heads;
 
-    // ---- validation (uniform across the CTA)
-    const int di = P.dec_index[r];
-    bool bad = false;
-    if (di < 0 || di >= P.n_decoders) { report(P.status, TTKV_STATUS_DECODER); bad = true; }
-    const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
-    if (!bad && blocks_needed > P.bt_cols) { report(P.status, TTKV_STATUS_ROW_SHORT); bad = true; }
-    const int t_begin = split * P.chunk;
-    const int t_end = min(seq, t_begin + P.chunk);
-    const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
-    if (!bad && t_begin < t_end) {
-        const int64_t n_blocks = P.n_slots / P.block_size;
-        int local_bad = 0;
-        for (int b = t_begin / P.block_size + tid; b <= (t_end - 1) / P.block_size; b += NTHR) {
-            const int32_t blk = brow[b];
-            if (blk < 0 || blk >= n_blocks) local_bad = 1;
+    // ---- the schedule. Units are (request, KV head, 128-token tile) in request-major order;
+    // T = n_heads * sum over requests of their tiles, from the device's seq_lens. CTA c takes the
+    // units [c*T/n, (c+1)*T/n) of the n CTAs, so every SM gets the same amount of work whatever
+    // the batch's lengths; a run that crosses a (request, head) boundary is processed as one
+    // segment per pair, each leaving a partial (o, max, sum) for the merge.
+    int64_t T_units, lo, hi;
+    int r = 0;
+    int64_t before = 0;
+    if (P.n_reqs <= NTHR) {                       // one pass: thread i holds request i
+        const int v = tid < P.n_reqs ? req_tiles(P.seq_lens[tid]) : 0;
+        int tot;
+        const int ex = cta_scan(v, M->scan, tot);
+        T_units = int64_t(tot) * nh;
+        lo = int64_t(blockIdx.x) * T_units / gridDim.x;
+        hi = int64_t(blockIdx.x + 1) * T_units / gridDim.x;
+        if (tid < P.n_reqs && int64_t(ex) * nh <= lo && lo < int64_t(ex + v) * nh) {
+            M->sched_r = tid;
+            M->sched_before = ex;
         }
-        if (__syncthreads_or(local_bad)) {
-            if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
-            bad = true;
+    } else {                                      // the total first, then the request holding lo
+        int64_t tiles_all = 0;
+        for (int base0 = 0; base0 < P.n_reqs; base0 += NTHR) {
+            const int i = base0 + tid;
+            int tot;
+            cta_scan(i < P.n_reqs ? req_tiles(P.seq_lens[i]) : 0, M->scan, tot);
+            tiles_all += tot;
+        }
+        T_units = tiles_all * nh;
+        lo = int64_t(blockIdx.x) * T_units / gridDim.x;
+        hi = int64_t(blockIdx.x + 1) * T_units / gridDim.x;
+        int64_t acc = 0;
+        for (int base0 = 0; base0 < P.n_reqs && acc * nh <= lo; base0 += NTHR) {
+            const int i = base0 + tid;
+            const int v = i < P.n_reqs ? req_tiles(P.seq_lens[i]) : 0;
+            int tot;
+            const int ex = cta_scan(v, M->scan, tot);
+            if (i < P.n_reqs && (acc + ex) * nh <= lo && lo < (acc + ex + v) * nh) {
+                M->sched_r = i;
+                M->sched_before = acc + ex;
+            }
+            acc += tot;                                        // uniform: the CTA's sum
         }
     }
-    if (!bad && t_begin < t_end && (t_end - 1) / P.block_size - t_begin / P.block_size + 1 > BT_CAP) {
-        report(P.status, TTKV_STATUS_ROW_SHORT);           // the plan keeps a split within BT_CAP blocks
-        bad = true;
-    }
-    const int64_t row_base = (int64_t(r) * P.n_heads + hl) * G;
-    if (bad || t_begin >= t_end) {
+    __syncthreads();
+    if (lo >= hi) return;                                      // uniform: nothing for this CTA
+    r = M->sched_r;
+    before = M->sched_before;
+    int64_t unit = lo;
+
+    auto empty_partial = [&](int64_t slot) {
         if (tid < G) {
-            P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 0] = -INFINITY;
-            P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 1] = 0.f;
+            P.part_ml[(slot * G + tid) * 2 + 0] = -INFINITY;
+            P.part_ml[(slot * G + tid) * 2 + 1] = 0.f;
         }
         if (wg == 0)
-            for (int g = 0; g < G; ++g) P.part_o[((row_base + g) * P.n_splits + split) * 128 + t] = 0.f;
-        return;
-    }
-    const int n_tiles = (t_end - t_begin + TM - 1) / TM;
+            for (int g = 0; g < G; ++g) P.part_o[(slot * G + g) * 128 + t] = 0.f;
+    };
 
-    // ---- staging. Per tile, 16-byte cp.async copies laid out chunk-fastest over the tile's tokens
-    // (a warp's copies cover a few consecutive slot fields, not 32 scattered rows), the issue cost
-    // shared by every warp: the coefficient blocks (one buffer, refilled after the softmax
-    // barrier for the tile after next) and this head's K and V fields (T.nkv buffers, refilled at
-    // the top of the tile before), each field exactly the 16-byte blocks covering it, never past
-    // the blob. Every thread arrives once per phase on the unit's mbarrier after its own copies
-    // (cp.async.mbarrier.arrive.noinc). The tile's RoPE rows are consecutive positions of the
-    // table: two TMA boxes (cos, sin) of 128 rows, 128-byte swizzled, from one thread.
-    const int kfield = P.coeff_bytes + 2 + h * P.k_row;
-    const int vfield = P.v_offset + h * P.v_row;
-    const int koff = kfield & 15, voff = vfield & 15;
-    const int cch = T.cb >> 4;
-    const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
-    const int nkvc = kch + vch;
-    // division by the chunk counts and the block size as a multiply-high (operands < 2^32 / divisor)
-    const uint32_t mul_cf = uint32_t((0x100000000ull + cch - 1) / cch);
-    const uint32_t mul_kv = uint32_t((0x100000000ull + nkvc - 1) / nkvc);
-    const uint32_t bsz = uint32_t(P.block_size);
-    const uint64_t mul_bs = (0x100000000ull + bsz - 1) / bsz;
-    const int blk0 = t_begin / P.block_size;
-    const int32_t* bts = reinterpret_cast<const int32_t*>(base + T.off_bt);
-    auto slot_at = [&](int tok) -> int64_t {
-        const uint32_t blk = uint32_t((uint64_t(uint32_t(tok)) * mul_bs) >> 32);
-        return int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
-    };
-    auto ntok = [&](int tile) { return tile < n_tiles ? min(TM, t_end - (t_begin + tile * TM)) : 0; };
+    // ---- set-up for the CTA's lifetime: TMEM, barriers, shift tables, the zero columns of P'
+    if (w == 0) tmem_alloc(&M->tmem_base, TMEM_COLS);
+    if (tid == RP_TID && T.rope_smem) tma_prefetch_desc(&maps.rope);
+    if (tid == 0) {
+        mbar_init(&M->mb_r, 1);
+        mbar_init(&M->mb_pv, 1);
+        mbar_init(&M->mb_cf, NTHR);
+        mbar_init(&M->mb_rp, 1);
+        mbar_init(&M->mb_kv[0], NTHR);
+        mbar_init(&M->mb_kv[1], NTHR);
+    }
+    if (tid < 32) {
+        const int n = tid & 15, bits = tid < 16 ? P.res_bits : P.v_bits;
+        (tid < 16 ? lutk : lutv)[n] =
+            make_uint4(lut_shift(n, 0, bits), lut_shift(n, 1, bits), lut_shift(n, 2, bits), lut_shift(n, 3, bits));
+    }
+    for (int i = tid; i < BPV_BYTES / 16; i += NTHR) reinterpret_cast<uint4*>(bpv)[i] = make_uint4(0, 0, 0, 0);
+
     auto kv_buf = [&](int tile) { return T.nkv == 2 ? (tile & 1) : 0; };
-    auto issue_cf = [&](int tile) {
-        const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
-        for (int i = tid; i < n; i += NTHR) {
-            const uint32_t u = __umulhi(uint32_t(i), mul_cf), c = uint32_t(i) - u * uint32_t(cch);
-            cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
-                       P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
-        }
-        cp_async_arrive(&M->mb_cf);
-    };
-    auto issue_kv = [&](int tile) {
-        const int b = kv_buf(tile), t0k = t_begin + tile * TM, n = ntok(tile) * nkvc;
-        unsigned char* dstb = kvb + size_t(b) * TM * T.kvrow;
-        for (int i = tid; i < n; i += NTHR) {
-            const uint32_t u = __umulhi(uint32_t(i), mul_kv), c = uint32_t(i) - u * uint32_t(nkvc);
-            const uint8_t* src = P.cache + slot_at(t0k + int(u)) * P.row_bytes;
-            unsigned char* dst = dstb + u * T.kvrow;
-            if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
-            else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
-        }
-        cp_async_arrive(&M->mb_kv[b]);
-    };
-    auto issue_rp = [&](int tile) {                                // RP_TID only; the buffer is free
-        mbar_expect_tx(&M->mb_rp, uint32_t(2 * RP_BOX));
-        tma_load_2d(rpb, &maps.rope, 0, t_begin + tile * TM, &M->mb_rp);
-        tma_load_2d(rpb + RP_BOX, &maps.rope, 64, t_begin + tile * TM, &M->mb_rp);
-    };
     // phase parities of the staging mbarriers, and which have copies in flight
     uint32_t par_cf = 0, par_rp = 0, par_kv0 = 0, par_kv1 = 0;
     bool pend_cf = false, pend_rp = false, pend_kv0 = false, pend_kv1 = false;
@@ -480,76 +501,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         return valid ? f16_bits_to_f32(byte_at(sb) | (byte_at(sb + 1) << 8)) : 0.f;
     };
 
-    // ---- set-up: TMEM, barriers, tables, operands that live for the whole CTA
-    if (w == 0) tmem_alloc(&M->tmem_base, TMEM_COLS);
-    if (tid == RP_TID && T.rope_smem) tma_prefetch_desc(&maps.rope);
-    if (tid == 0) {
-        mbar_init(&M->mb_r, 1);
-        mbar_init(&M->mb_pv, 1);
-        mbar_init(&M->mb_cf, NTHR);
-        mbar_init(&M->mb_rp, 1);
-        mbar_init(&M->mb_kv[0], NTHR);
-        mbar_init(&M->mb_kv[1], NTHR);
-    }
-    {
-        int32_t* btw = reinterpret_cast<int32_t*>(base + T.off_bt);
-        const int nblk = (t_end - 1) / P.block_size - blk0 + 1;        // <= BT_CAP (checked above)
-        for (int i = tid; i < nblk; i += NTHR) btw[i] = brow[blk0 + i];
-    }
-
-    if (tid < kMaxG) { M->m[tid] = -INFINITY; M->l[tid] = 0.f; }
-    if (tid < 32) {
-        const int n = tid & 15, bits = tid < 16 ? P.res_bits : P.v_bits;
-        (tid < 16 ? lutk : lutv)[n] =
-            make_uint4(lut_shift(n, 0, bits), lut_shift(n, 1, bits), lut_shift(n, 2, bits), lut_shift(n, 3, bits));
-    }
-    for (int i = tid; i < BPV_BYTES / 16; i += NTHR) reinterpret_cast<uint4*>(bpv)[i] = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < G * 128; i += NTHR) {
-        const int g = i >> 7, j = i & 127;
-        const int slot = (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1);
-        qs[slot] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
-    }
-    // decoder slice: power-of-two scale so max|D| * 2^-e lies in [2^13, 2^14), then fp16 hi + lo
-    const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * 128 + t;
-    const int64_t dstride = int64_t(P.H) * 128;
-    float mx = 0.f;
-    for (int rr = wg; rr < P.r1; rr += NWG) mx = fmaxf(mx, fabsf(dec[rr * dstride]));
-    mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
-    if (lane == 0) M->maxabs[w] = mx;
-    __syncthreads();                                  // barriers initialised, block-table slice cached
-    issue_cf(0);
-    issue_kv(0);
-    if (tid == RP_TID && T.rope_smem) issue_rp(0);
-    pend_cf = true; pend_kv0 = true;
-    if (T.rope_smem) pend_rp = true;
-    mx = 0.f;
-    #pragma unroll
-    for (int i = 0; i < NTHR / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
-    int e = 0;
-    if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
-    e = max(-100, min(100, e));
-    const float s_down = __uint_as_float(uint32_t(127 - e) << 23);   // 2^-e
-    const float s_up = __uint_as_float(uint32_t(127 + e) << 23);     // 2^e
-    for (int cidx = wg; cidx < T.kp16 / 8; cidx += NWG) {
-        uint32_t hw[4], lw[4];
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            uint32_t hh[2], ll[2];
-            #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const int rr = cidx * 8 + 2 * i + k;
-                const float v = rr < P.r1 ? dec[rr * dstride] * s_down : 0.f;
-                hh[k] = f16_bits(v);
-                ll[k] = f16_bits(v - f16_bits_to_f32(hh[k]));
-            }
-            hw[i] = hh[0] | (hh[1] << 16);
-            lw[i] = ll[0] | (ll[1] << 16);
-        }
-        const uint32_t off = uint32_t((cidx >> 3) * ATOM_BYTES) + kmajor_off(t, cidx & 7);
-        *reinterpret_cast<uint4*>(bhi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
-
     // MMA issue (one thread). The start-address field of a descriptor is its low 14 bits (16-byte
     // units, shared addresses < 2^18 B), so a k-step offset is added to the descriptor directly.
     const uint64_t dA = sw128_desc(smem_u32(amat), 16, 1024), dH = sw128_desc(smem_u32(bhi), 16, 1024),
@@ -573,21 +524,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         mma_commit(&M->mb_pv);
     };
 
-    // ---- first tile: its coefficient block, its A, its reconstruction (TMEM columns 0..127)
-    wait_cf();
-    float csp_next = convert_a(t_begin + t < t_end) * s_up;        // coefficient scale x 2^e of the tile
-    fence_async_smem();
-    tc_before();
-    __syncthreads();
-    tc_after();
-    const uint32_t taddr = M->tmem_base;
-    const uint32_t t_row = taddr + (uint32_t(32 * (w & 3)) << 16);    // this warp's TMEM lanes
-    if (tid == MMA_TID) issue_recon(taddr);
-    if (n_tiles > 1) {                                              // every conversion of tile 0 is done
-        issue_cf(1);
-        pend_cf = true;
-    }
-
     const int kbits = P.res_bits, vbits = P.v_bits;
     const uint32_t kflip = flip_mask(kbits), vflip = flip_mask(vbits);
     const uint32_t khalf = 1u << (kbits - 1), vhalf = 1u << (vbits - 1);
@@ -600,64 +536,473 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const float scale = P.scale;
     const float4* qs4 = reinterpret_cast<const float4*>(qs);
 
-    float o[HPW], corr_prev[HPW], m_prev[HPW], lsum[HPW];
-    #pragma unroll
-    for (int i = 0; i < HPW; ++i) { o[i] = 0.f; corr_prev[i] = 0.f; m_prev[i] = -INFINITY; lsum[i] = 0.f; }
     uint32_t ph_r = 0, ph_pv = 0;
-    bool r_pending = true, pv_pending = false;
+    bool r_pending_any = false, pv_pending_any = false;
 
-    for (int it = 0; it < n_tiles; ++it) {
-        const int t0 = t_begin + it * TM;
-        const bool has_next = it + 1 < n_tiles;
-        const int kb = kv_buf(it);
-        const int tok = t0 + t;
-        const bool valid = tok < t_end;
-        const unsigned char* kvrow = kvb + (size_t(kb) * TM + t) * T.kvrow;
-        const uint32_t kv_off = uint32_t(kvrow - base);
-        // the next tile's K/V fields, into the other buffer (read by the tile before this one)
-        if (T.nkv == 2 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }
-        const uint32_t rcol = uint32_t(it & 1) * 128u;                 // this tile's reconstruction columns
-        const float csp = csp_next;
+    while (unit < hi && !timed_out) {
+        // ---- the next segment: the run of this CTA's units that belongs to one (request, KV head)
+        if (r >= P.n_reqs) break;                                   // unreachable: hi <= T
+        const int seq = P.seq_lens[r];
+        const int nt = req_tiles(seq);
+        const int64_t rs = before * nh, re = rs + int64_t(nt) * nh;
+        if (unit >= re) { before += nt; ++r; continue; }        // past this request (or it has no rows)
+        const int hl = int((unit - rs) / nt);
+        const int64_t ps = rs + int64_t(hl) * nt;
+        const int64_t seg_hi = min(hi, ps + nt);
+        const int t_begin = int(unit - ps) * TM;
+        const int t_end = min(seq, int(seg_hi - ps) * TM);
+        const int64_t slot = int64_t(blockIdx.x) + int64_t(r) * nh + hl;
+        unit = seg_hi;
+        const int h = P.head_lo + hl;
 
-        // ---- this token's RoPE row from global memory when it is not staged (used in the epilogue)
-        uint4 cosw[2], sinw[2];
-        if (!T.rope_smem) {
-            const uint16_t* trow = reinterpret_cast<const uint16_t*>(P.table) +
-                                   int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128;
-            #pragma unroll
-            for (int hp = 0; hp < 2; ++hp) {
-                cosw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 16 * wg + 8 * hp));
-                sinw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 64 + 16 * wg + 8 * hp));
+        // ---- the cheap refusals (uniform); the block ids are checked as the set-up loads them
+        const int di = P.dec_index[r];
+        bool bad = false;
+        if (di < 0 || di >= P.n_decoders) { if (tid == 0) report(P.status, TTKV_STATUS_DECODER); bad = true; }
+        const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
+        if (!bad && blocks_needed > P.bt_cols) { if (tid == 0) report(P.status, TTKV_STATUS_ROW_SHORT); bad = true; }
+        const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
+        if (!bad && (t_end - 1) / P.block_size - t_begin / P.block_size + 1 > BT_CAP) {
+            if (tid == 0) report(P.status, TTKV_STATUS_ROW_SHORT);   // the plan keeps a segment within BT_CAP blocks
+            bad = true;
+        }
+        const int n_tiles = (t_end - t_begin + TM - 1) / TM;
+
+        // ---- staging. Per tile, 16-byte cp.async copies laid out chunk-fastest over the tile's tokens
+        // (a warp's copies cover a few consecutive slot fields, not 32 scattered rows), the issue cost
+        // shared by every warp: the coefficient blocks (one buffer, refilled after the softmax
+        // barrier for the tile after next) and this head's K and V fields (T.nkv buffers, refilled at
+        // the top of the tile before), each field exactly the 16-byte blocks covering it, never past
+        // the blob. Every thread arrives once per phase on the unit's mbarrier after its own copies
+        // (cp.async.mbarrier.arrive.noinc). The tile's RoPE rows are consecutive positions of the
+        // table: two TMA boxes (cos, sin) of 128 rows, 128-byte swizzled, from one thread.
+        const int kfield = P.coeff_bytes + 2 + h * P.k_row;
+        const int vfield = P.v_offset + h * P.v_row;
+        const int koff = kfield & 15, voff = vfield & 15;
+        const int cch = T.cb >> 4;
+        const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
+        const int nkvc = kch + vch;
+        // division by the chunk counts and the block size as a multiply-high (operands < 2^32 / divisor)
+        const uint32_t mul_cf = uint32_t((0x100000000ull + cch - 1) / cch);
+        const uint32_t mul_kv = uint32_t((0x100000000ull + nkvc - 1) / nkvc);
+        const uint32_t bsz = uint32_t(P.block_size);
+        const uint64_t mul_bs = (0x100000000ull + bsz - 1) / bsz;
+        const int blk0 = t_begin / P.block_size;
+        const int32_t* bts = reinterpret_cast<const int32_t*>(base + T.off_bt);
+        auto slot_at = [&](int tok) -> int64_t {
+            const uint32_t blk = uint32_t((uint64_t(uint32_t(tok)) * mul_bs) >> 32);
+            return int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
+        };
+        auto ntok = [&](int tile) { return tile < n_tiles ? min(TM, t_end - (t_begin + tile * TM)) : 0; };
+        auto issue_cf = [&](int tile) {
+            const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
+            for (int i = tid; i < n; i += NTHR) {
+                const uint32_t u = __umulhi(uint32_t(i), mul_cf), c = uint32_t(i) - u * uint32_t(cch);
+                cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
+                           P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
+            }
+            cp_async_arrive(&M->mb_cf);
+        };
+        auto issue_kv = [&](int tile) {
+            const int b = kv_buf(tile), t0k = t_begin + tile * TM, n = ntok(tile) * nkvc;
+            unsigned char* dstb = kvb + size_t(b) * TM * T.kvrow;
+            for (int i = tid; i < n; i += NTHR) {
+                const uint32_t u = __umulhi(uint32_t(i), mul_kv), c = uint32_t(i) - u * uint32_t(nkvc);
+                const uint8_t* src = P.cache + slot_at(t0k + int(u)) * P.row_bytes;
+                unsigned char* dst = dstb + u * T.kvrow;
+                if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
+                else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
+            }
+            cp_async_arrive(&M->mb_kv[b]);
+        };
+        auto issue_rp = [&](int tile) {                                // RP_TID only; the buffer is free
+            mbar_expect_tx(&M->mb_rp, uint32_t(2 * RP_BOX));
+            tma_load_2d(rpb, &maps.rope, 0, t_begin + tile * TM, &M->mb_rp);
+            tma_load_2d(rpb + RP_BOX, &maps.rope, 64, t_begin + tile * TM, &M->mb_rp);
+        };
+        // ---- the segment's set-up. Pass 1: its block-table slice (each id checked against the
+        // cache) and its query rows; then the first tile's copies go out at once. Pass 2, under
+        // those copies: the largest |value| of its decoder slice, coalesced rows w + 16 i. After
+        // that barrier thread t converts column t of the 8-row chunks wg, wg + NWG, ...
+        const float* dec = P.decoders + int64_t(bad ? 0 : di) * P.dec_stride + h * 128 + t;
+        const int64_t dstride = int64_t(P.H) * 128;
+        const int nchunk = T.kp16 / 8;
+        int local_bad = 0;
+        if (!bad) {
+            int32_t* btw = reinterpret_cast<int32_t*>(base + T.off_bt);
+            const int nblk = (t_end - 1) / P.block_size - blk0 + 1;        // <= BT_CAP (checked above)
+            const int64_t n_blocks = P.n_slots / P.block_size;
+            for (int i = tid; i < nblk; i += NTHR) {
+                const int32_t blk = brow[blk0 + i];
+                if (blk < 0 || blk >= n_blocks) local_bad = 1;
+                btw[i] = blk;
+            }
+            for (int i = tid; i < G * 128; i += NTHR) {
+                const int g = i >> 7, j = i & 127;
+                const int qi = (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1);
+                qs[qi] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
             }
         }
-
-        // ---- K residual: code windows of the bitmap bytes of lanes [16wg, 16wg+16) and
-        // [64+16wg, 64+16wg+16) (bytes 2wg+hp and 8+2wg+hp); the fields are cut in the epilogue
-        wait_kv(kb);
-        uint32_t kwin[4], kbyte[4];
-        float krs;
+        if (tid < kMaxG) { M->m[tid] = -INFINITY; M->l[tid] = 0.f; }
+        if (__syncthreads_or(local_bad)) {                 // block-table slice cached and checked
+            if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
+            bad = true;
+        }
+        if (bad) {
+            empty_partial(slot);
+            __syncthreads();
+            continue;
+        }
+        issue_cf(0);
+        issue_kv(0);
+        if (tid == RP_TID && T.rope_smem) issue_rp(0);
+        pend_cf = true; pend_kv0 = true;
+        if (T.rope_smem) pend_rp = true;
+        float mx = 0.f;
         {
-            const uint4* kp = reinterpret_cast<const uint4*>(kvrow);
-            uint32_t bw[4];
-            bitmap_words(kp[0], kp[1], koff, bw);
-            if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
-            trim_bitmap(bw, P.res_k);
-            int pre[4];
-            pre[0] = 0;
-            pre[1] = __popc(bw[0]);
-            pre[2] = pre[1] + __popc(bw[1]);
-            pre[3] = pre[2] + __popc(bw[2]);
+            const float4* d4 = reinterpret_cast<const float4*>(dec - t) + lane;
+            const int64_t rs4 = dstride / 4;
             #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int grp = (q & 1 ? 8 : 0) + 2 * wg + (q >> 1);
-                kbyte[q] = bitmap_byte(bw, grp);
-                kwin[q] = window32(base, kv_off + uint32_t(koff + 16), uint32_t(byte_rank(bw, pre, grp) * kbits)) ^ kflip;
+            for (int i = 0; i < MAX_R1 / 16; ++i) {
+                const int rr = w + 16 * i;
+                if (rr < P.r1) {
+                    const float4 v = d4[rr * rs4];
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
             }
-            krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
+        }
+        mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+        if (lane == 0) M->maxabs[w] = mx;
+        __syncthreads();
+        // decoder slice (again, from L2, while the tile's copies fly): power-of-two scale so
+        // max|D| * 2^-e lies in [2^13, 2^14), then fp16 hi + lo
+        mx = 0.f;
+        #pragma unroll
+        for (int i = 0; i < NTHR / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
+        int e = 0;
+        if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
+        e = max(-100, min(100, e));
+        const float s_down = __uint_as_float(uint32_t(127 - e) << 23);   // 2^-e
+        const float s_up = __uint_as_float(uint32_t(127 + e) << 23);     // 2^e
+        #pragma unroll
+        for (int jc = 0; jc < DEC_CHUNKS; ++jc) {
+            const int cidx = wg + NWG * jc;
+            if (cidx < nchunk) {
+                float dv[8];
+                #pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int rr = cidx * 8 + k;
+                    dv[k] = rr < P.r1 ? dec[rr * dstride] : 0.f;
+                }
+                uint32_t hw[4], lw[4];
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t hh[2], ll[2];
+                    #pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const float v = dv[2 * i + k] * s_down;
+                        hh[k] = f16_bits(v);
+                        ll[k] = f16_bits(v - f16_bits_to_f32(hh[k]));
+                    }
+                    hw[i] = hh[0] | (hh[1] << 16);
+                    lw[i] = ll[0] | (ll[1] << 16);
+                }
+                const uint32_t off = uint32_t((cidx >> 3) * ATOM_BYTES) + kmajor_off(t, cidx & 7);
+                *reinterpret_cast<uint4*>(bhi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
         }
 
-        // ---- PV of the previous tile: each warpgroup folds its query heads into o
-        if (pv_pending) {
+        // ---- first tile: its coefficient block, its A, its reconstruction (TMEM columns 0..127)
+        wait_cf();
+        float csp_next = convert_a(t_begin + t < t_end) * s_up;        // coefficient scale x 2^e of the tile
+        fence_async_smem();
+        tc_before();
+        __syncthreads();
+        tc_after();
+        const uint32_t taddr = M->tmem_base;
+        const uint32_t t_row = taddr + (uint32_t(32 * (w & 3)) << 16);    // this warp's TMEM lanes
+        if (tid == MMA_TID) issue_recon(taddr);
+        if (n_tiles > 1) {                                              // every conversion of tile 0 is done
+            issue_cf(1);
+            pend_cf = true;
+        }
+
+        float o[HPW], corr_prev[HPW], m_prev[HPW], lsum[HPW];
+        #pragma unroll
+        for (int i = 0; i < HPW; ++i) { o[i] = 0.f; corr_prev[i] = 0.f; m_prev[i] = -INFINITY; lsum[i] = 0.f; }
+        bool r_pending = true, pv_pending = false;
+
+        for (int it = 0; it < n_tiles; ++it) {
+            const int t0 = t_begin + it * TM;
+            const bool has_next = it + 1 < n_tiles;
+            const int kb = kv_buf(it);
+            const int tok = t0 + t;
+            const bool valid = tok < t_end;
+            const unsigned char* kvrow = kvb + (size_t(kb) * TM + t) * T.kvrow;
+            const uint32_t kv_off = uint32_t(kvrow - base);
+            // the next tile's K/V fields, into the other buffer (read by the tile before this one)
+            if (T.nkv == 2 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }
+            const uint32_t rcol = uint32_t(it & 1) * 128u;                 // this tile's reconstruction columns
+            const float csp = csp_next;
+
+            // ---- this token's RoPE row from global memory when it is not staged (used in the epilogue)
+            uint4 cosw[2], sinw[2];
+            if (!T.rope_smem) {
+                const uint16_t* trow = reinterpret_cast<const uint16_t*>(P.table) +
+                                       int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128;
+                #pragma unroll
+                for (int hp = 0; hp < 2; ++hp) {
+                    cosw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 16 * wg + 8 * hp));
+                    sinw[hp] = __ldg(reinterpret_cast<const uint4*>(trow + 64 + 16 * wg + 8 * hp));
+                }
+            }
+
+            // ---- K residual: code windows of the bitmap bytes of lanes [16wg, 16wg+16) and
+            // [64+16wg, 64+16wg+16) (bytes 2wg+hp and 8+2wg+hp); the fields are cut in the epilogue
+            wait_kv(kb);
+            uint32_t kwin[4], kbyte[4];
+            float krs;
+            {
+                const uint4* kp = reinterpret_cast<const uint4*>(kvrow);
+                uint32_t bw[4];
+                bitmap_words(kp[0], kp[1], koff, bw);
+                if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
+                trim_bitmap(bw, P.res_k);
+                int pre[4];
+                pre[0] = 0;
+                pre[1] = __popc(bw[0]);
+                pre[2] = pre[1] + __popc(bw[1]);
+                pre[3] = pre[2] + __popc(bw[2]);
+                #pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int grp = (q & 1 ? 8 : 0) + 2 * wg + (q >> 1);
+                    kbyte[q] = bitmap_byte(bw, grp);
+                    kwin[q] = window32(base, kv_off + uint32_t(koff + 16), uint32_t(byte_rank(bw, pre, grp) * kbits)) ^ kflip;
+                }
+                krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
+            }
+
+            // ---- PV of the previous tile: each warpgroup folds its query heads into o
+            if (pv_pending) {
+                if (!mbar_wait(&M->mb_pv, ph_pv)) timed_out = true;
+                else { ph_pv ^= 1u; pv_pending = false; }
+                tc_after();
+                if (wg < G && !__any_sync(0xffffffffu, timed_out)) {
+                    #pragma unroll
+                    for (int i = 0; i < HPW; ++i) {
+                        const int g = wg + NWG * i;
+                        if (g < G) {
+                            const float dh = tmem_ld1(t_row + PV_COL + uint32_t(g));
+                            const float dl = tmem_ld1(t_row + PV_COL + uint32_t(G + g));
+                            tmem_wait_ld();
+                            o[i] = fmaf(o[i], corr_prev[i], dh + dl);
+                        }
+                    }
+                }
+            }
+
+            // ---- V^T (MN-major): lanes [32wg, 32wg+32) of this token as exact small integers
+            float vrs;
+            {
+                const unsigned char* vrow = kvrow + T.kr;
+                const uint32_t vfo = kv_off + uint32_t(T.kr + voff);
+                const uint4* vp = reinterpret_cast<const uint4*>(vrow);
+                uint32_t bw[4];
+                bitmap_words(vp[0], vp[1], voff, bw);
+                if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
+                trim_bitmap(bw, P.v_lanes);
+                const uint32_t word = wg == 0 ? bw[0] : wg == 1 ? bw[1] : wg == 2 ? bw[2] : bw[3];
+                int rank = (wg > 0 ? __popc(bw[0]) : 0) + (wg > 1 ? __popc(bw[1]) : 0) + (wg > 2 ? __popc(bw[2]) : 0);
+                #pragma unroll
+                for (int gi = 0; gi < 4; ++gi) {
+                    const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
+                    const uint32_t win = window32(base, vfo + 16u, uint32_t(rank * vbits)) ^ vflip;
+                    rank += __popc(byte);
+                    uint32_t f[8];
+                    group_fields(win, byte, vbits, lutv, f);
+                    uint32_t hv[4];
+                    #pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t x = (__byte_perm(f[2 * k], f[2 * k + 1], 0x5410) & vmask2) ^ vmag2;
+                        const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&x), vbias2);
+                        hv[k] = *reinterpret_cast<const uint32_t*>(&y);
+                    }
+                    const int ch = 4 * wg + gi;                         // lanes 8ch..8ch+7, one 16-byte chunk
+                    const uint32_t off = uint32_t((t >> 3) * 2048 + (ch >> 3) * 1024 + (t & 7) * 128 +
+                                                  (((ch & 7) ^ (t & 7)) << 4));
+                    *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                }
+                vrs = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
+            }
+
+            // ---- MMA 1 of this tile done: A is free for the next tile's coefficients
+            if (r_pending) {
+                if (!mbar_wait(&M->mb_r, ph_r)) timed_out = true;
+                else { ph_r ^= 1u; r_pending = false; }
+            }
+            tc_after();
+            if (has_next) {
+                wait_cf();
+                csp_next = convert_a(t0 + TM + t < t_end) * s_up;
+            }
+
+            // ---- epilogue: rebuild, patch, rotate, partial scores over this warpgroup's lanes
+            if (T.rope_smem) {
+                wait_rp();
+                // row t of each box: 16-byte block c stored at block c ^ (t & 7)
+                const unsigned char* rc = rpb + t * 128;
+                #pragma unroll
+                for (int hp = 0; hp < 2; ++hp) {
+                    const int c = (2 * wg + hp) ^ (t & 7);
+                    cosw[hp] = *reinterpret_cast<const uint4*>(rc + 16 * c);
+                    sinw[hp] = *reinterpret_cast<const uint4*>(rc + RP_BOX + 16 * c);
+                }
+            }
+            float sp[8];
+            #pragma unroll
+            for (int g = 0; g < 8; ++g) sp[g] = 0.f;
+            if (!__any_sync(0xffffffffu, timed_out)) {
+                float2 s2[G];
+                #pragma unroll
+                for (int g = 0; g < G; ++g) s2[g] = make_float2(0.f, 0.f);
+                const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
+                const float2 neg1 = make_float2(-1.f, -1.f);
+                #pragma unroll
+                for (int hp = 0; hp < 2; ++hp) {                        // 8 RoPE pairs at a time
+                    const int j0 = 16 * wg + 8 * hp;
+                    float al[8], ah[8];
+                    tmem_ld8(t_row + rcol + uint32_t(j0), al);
+                    tmem_ld8(t_row + rcol + uint32_t(64 + j0), ah);
+                    float rl[8], rh[8];
+                    {
+                        uint32_t f[8];
+                        group_fields(kwin[2 * hp], kbyte[2 * hp], kbits, lutk, f);
+                        #pragma unroll
+                        for (int k = 0; k < 8; ++k) rl[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
+                        group_fields(kwin[2 * hp + 1], kbyte[2 * hp + 1], kbits, lutk, f);
+                        #pragma unroll
+                        for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
+                    }
+                    tmem_wait_ld();
+                    const uint32_t cwv[4] = {cosw[hp].x, cosw[hp].y, cosw[hp].z, cosw[hp].w};
+                    const uint32_t swv[4] = {sinw[hp].x, sinw[hp].y, sinw[hp].z, sinw[hp].w};
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {                       // lanes j0+2i, j0+2i+1
+                        float2 cz, sz;
+                        if (tbf16) {
+                            cz = make_float2(__uint_as_float(cwv[i] << 16), __uint_as_float(cwv[i] & 0xffff0000u));
+                            sz = make_float2(__uint_as_float(swv[i] << 16), __uint_as_float(swv[i] & 0xffff0000u));
+                        } else {
+                            cz = __half22float2(*reinterpret_cast<const __half2*>(&cwv[i]));
+                            sz = __half22float2(*reinterpret_cast<const __half2*>(&swv[i]));
+                        }
+                        const float2 kl = f2fma(make_float2(rl[2 * i], rl[2 * i + 1]), krs2,
+                                                f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
+                        const float2 kh = f2fma(make_float2(rh[2 * i], rh[2 * i + 1]), krs2,
+                                                f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
+                        const float2 yl = f2fma(f2mul(kh, neg1), sz, f2mul(kl, cz));
+                        const float2 yh = f2fma(kl, sz, f2mul(kh, cz));
+                        #pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            const float4 qq = qs4[g * 32 + (j0 >> 1) + i];
+                            s2[g] = f2fma(make_float2(qq.x, qq.y), yl, f2fma(make_float2(qq.z, qq.w), yh, s2[g]));
+                        }
+                    }
+                }
+                #pragma unroll
+                for (int g = 0; g < G; ++g) sp[g] = s2[g].x + s2[g].y;
+                tmem_st8(t_row + RED_COL + uint32_t(8 * wg), sp);     // partial scores -> TMEM
+                tmem_wait_st();
+            }
+
+            const bool cf_refill = it + 2 < n_tiles;
+            fence_async_smem();                                          // V^T, next A for the MMAs
+            tc_before();
+            if (__syncthreads_or(timed_out)) { timed_out = true; break; }
+            tc_after();
+
+            // ---- MMA 1 of the next tile into the other reconstruction columns (under the softmax
+            // and the next tile's decode), and the refills of the staging units this tile released
+            if (has_next) {
+                if (tid == MMA_TID) issue_recon(taddr + (rcol ^ 128u));
+                r_pending = true;
+            }
+            if (T.nkv == 1 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }   // the buffer is free now
+            if (cf_refill) { issue_cf(it + 2); pend_cf = true; }
+            if (T.rope_smem && has_next) {
+                if (tid == RP_TID) issue_rp(it + 1);
+                pend_rp = true;
+            }
+
+            // ---- online softmax over the tile: warpgroup wg owns query heads wg, wg + NWG, ... The tile
+            // max is one warp reduction and one warpgroup barrier; each thread keeps the running sum
+            // of its own tokens (rescaled with the max), reduced once after the last tile
+            if (wg < G) {
+                float sc[HPW], m_new[HPW], corr[HPW];
+                #pragma unroll
+                for (int i = 0; i < HPW; ++i) {
+                    const int g = wg + NWG * i;
+                    sc[i] = -INFINITY; m_new[i] = -INFINITY; corr[i] = 0.f;
+                    if (g < G) {
+                        float v = 0.f;
+                        #pragma unroll
+                        for (int c = 0; c < NWG; ++c) v += tmem_ld1(t_row + RED_COL + uint32_t(8 * c + g));
+                        tmem_wait_ld();
+                        sc[i] = valid ? v * scale : -INFINITY;
+                        const float mxg = warp_max(sc[i]);
+                        if (lane == 0) M->red_max[w & 3][g] = mxg;
+                    }
+                }
+                wg_sync(wg);
+                #pragma unroll
+                for (int i = 0; i < HPW; ++i) {
+                    const int g = wg + NWG * i;
+                    if (g < G) {
+                        const float tmax = fmaxf(fmaxf(M->red_max[0][g], M->red_max[1][g]),
+                                                 fmaxf(M->red_max[2][g], M->red_max[3][g]));
+                        const float m_old = M->m[g];
+                        m_new[i] = fmaxf(m_old, tmax);
+                        const float pg = (m_new[i] == -INFINITY || sc[i] == -INFINITY) ? 0.f : expf(sc[i] - m_new[i]);
+                        corr[i] = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new[i]);
+                        lsum[i] = fmaf(lsum[i], corr[i], pg);
+                        // P' = p * V ruler as fp16 hi (column g) + lo (column G + g); this token is K index t
+                        const float pv = pg * vrs;
+                        const uint32_t hb = f16_bits(pv);
+                        const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
+                        const int kt = t & 63, atom = t >> 6;
+                        #pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const int n = k == 0 ? g : G + g;
+                            const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
+                                                          (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
+                            *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
+                        }
+                    }
+                }
+                #pragma unroll
+                for (int i = 0; i < HPW; ++i) { corr_prev[i] = corr[i]; m_prev[i] = m_new[i]; }
+            }
+            fence_async_smem();
+            tc_before();
+            __syncthreads();
+            tc_after();
+            // running max of each query head (every thread of its warpgroup has read the old one)
+            if (wg < G && t == 0) {
+                #pragma unroll
+                for (int i = 0; i < HPW; ++i) {
+                    const int g = wg + NWG * i;
+                    if (g < G) M->m[g] = m_prev[i];
+                }
+            }
+
+            // ---- MMA 2 of this tile: O^T = V^T . P', read back during the next tile
+            if (tid == MMA_TID) issue_pv(taddr + PV_COL);
+            pv_pending = true;
+        }
+
+        // ---- the last tile's PV
+        if (!timed_out && pv_pending) {
             if (!mbar_wait(&M->mb_pv, ph_pv)) timed_out = true;
             else { ph_pv ^= 1u; pv_pending = false; }
             tc_after();
@@ -674,245 +1019,58 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 }
             }
         }
-
-        // ---- V^T (MN-major): lanes [32wg, 32wg+32) of this token as exact small integers
-        float vrs;
-        {
-            const unsigned char* vrow = kvrow + T.kr;
-            const uint32_t vfo = kv_off + uint32_t(T.kr + voff);
-            const uint4* vp = reinterpret_cast<const uint4*>(vrow);
-            uint32_t bw[4];
-            bitmap_words(vp[0], vp[1], voff, bw);
-            if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
-            trim_bitmap(bw, P.v_lanes);
-            const uint32_t word = wg == 0 ? bw[0] : wg == 1 ? bw[1] : wg == 2 ? bw[2] : bw[3];
-            int rank = (wg > 0 ? __popc(bw[0]) : 0) + (wg > 1 ? __popc(bw[1]) : 0) + (wg > 2 ? __popc(bw[2]) : 0);
-            #pragma unroll
-            for (int gi = 0; gi < 4; ++gi) {
-                const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
-                const uint32_t win = window32(base, vfo + 16u, uint32_t(rank * vbits)) ^ vflip;
-                rank += __popc(byte);
-                uint32_t f[8];
-                group_fields(win, byte, vbits, lutv, f);
-                uint32_t hv[4];
-                #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t x = (__byte_perm(f[2 * k], f[2 * k + 1], 0x5410) & vmask2) ^ vmag2;
-                    const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&x), vbias2);
-                    hv[k] = *reinterpret_cast<const uint32_t*>(&y);
-                }
-                const int ch = 4 * wg + gi;                         // lanes 8ch..8ch+7, one 16-byte chunk
-                const uint32_t off = uint32_t((t >> 3) * 2048 + (ch >> 3) * 1024 + (t & 7) * 128 +
-                                              (((ch & 7) ^ (t & 7)) << 4));
-                *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            }
-            vrs = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
-        }
-
-        // ---- MMA 1 of this tile done: A is free for the next tile's coefficients
-        if (r_pending) {
-            if (!mbar_wait(&M->mb_r, ph_r)) timed_out = true;
-            else { ph_r ^= 1u; r_pending = false; }
-        }
-        tc_after();
-        if (has_next) {
-            wait_cf();
-            csp_next = convert_a(t0 + TM + t < t_end) * s_up;
-        }
-
-        // ---- epilogue: rebuild, patch, rotate, partial scores over this warpgroup's lanes
-        if (T.rope_smem) {
-            wait_rp();
-            // row t of each box: 16-byte block c stored at block c ^ (t & 7)
-            const unsigned char* rc = rpb + t * 128;
-            #pragma unroll
-            for (int hp = 0; hp < 2; ++hp) {
-                const int c = (2 * wg + hp) ^ (t & 7);
-                cosw[hp] = *reinterpret_cast<const uint4*>(rc + 16 * c);
-                sinw[hp] = *reinterpret_cast<const uint4*>(rc + RP_BOX + 16 * c);
-            }
-        }
-        float sp[8];
-        #pragma unroll
-        for (int g = 0; g < 8; ++g) sp[g] = 0.f;
-        if (!__any_sync(0xffffffffu, timed_out)) {
-            float2 s2[G];
-            #pragma unroll
-            for (int g = 0; g < G; ++g) s2[g] = make_float2(0.f, 0.f);
-            const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
-            const float2 neg1 = make_float2(-1.f, -1.f);
-            #pragma unroll
-            for (int hp = 0; hp < 2; ++hp) {                        // 8 RoPE pairs at a time
-                const int j0 = 16 * wg + 8 * hp;
-                float al[8], ah[8];
-                tmem_ld8(t_row + rcol + uint32_t(j0), al);
-                tmem_ld8(t_row + rcol + uint32_t(64 + j0), ah);
-                float rl[8], rh[8];
-                {
-                    uint32_t f[8];
-                    group_fields(kwin[2 * hp], kbyte[2 * hp], kbits, lutk, f);
-                    #pragma unroll
-                    for (int k = 0; k < 8; ++k) rl[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
-                    group_fields(kwin[2 * hp + 1], kbyte[2 * hp + 1], kbits, lutk, f);
-                    #pragma unroll
-                    for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
-                }
-                tmem_wait_ld();
-                const uint32_t cwv[4] = {cosw[hp].x, cosw[hp].y, cosw[hp].z, cosw[hp].w};
-                const uint32_t swv[4] = {sinw[hp].x, sinw[hp].y, sinw[hp].z, sinw[hp].w};
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) {                       // lanes j0+2i, j0+2i+1
-                    float2 cz, sz;
-                    if (tbf16) {
-                        cz = make_float2(__uint_as_float(cwv[i] << 16), __uint_as_float(cwv[i] & 0xffff0000u));
-                        sz = make_float2(__uint_as_float(swv[i] << 16), __uint_as_float(swv[i] & 0xffff0000u));
-                    } else {
-                        cz = __half22float2(*reinterpret_cast<const __half2*>(&cwv[i]));
-                        sz = __half22float2(*reinterpret_cast<const __half2*>(&swv[i]));
-                    }
-                    const float2 kl = f2fma(make_float2(rl[2 * i], rl[2 * i + 1]), krs2,
-                                            f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
-                    const float2 kh = f2fma(make_float2(rh[2 * i], rh[2 * i + 1]), krs2,
-                                            f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
-                    const float2 yl = f2fma(f2mul(kh, neg1), sz, f2mul(kl, cz));
-                    const float2 yh = f2fma(kl, sz, f2mul(kh, cz));
-                    #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const float4 qq = qs4[g * 32 + (j0 >> 1) + i];
-                        s2[g] = f2fma(make_float2(qq.x, qq.y), yl, f2fma(make_float2(qq.z, qq.w), yh, s2[g]));
-                    }
-                }
-            }
-            #pragma unroll
-            for (int g = 0; g < G; ++g) sp[g] = s2[g].x + s2[g].y;
-            tmem_st8(t_row + RED_COL + uint32_t(8 * wg), sp);     // partial scores -> TMEM
-            tmem_wait_st();
-        }
-
-        const bool cf_refill = it + 2 < n_tiles;
-        fence_async_smem();                                          // V^T, next A for the MMAs
-        tc_before();
-        if (__syncthreads_or(timed_out)) { timed_out = true; break; }
-        tc_after();
-
-        // ---- MMA 1 of the next tile into the other reconstruction columns (under the softmax
-        // and the next tile's decode), and the refills of the staging units this tile released
-        if (has_next) {
-            if (tid == MMA_TID) issue_recon(taddr + (rcol ^ 128u));
-            r_pending = true;
-        }
-        if (T.nkv == 1 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }   // the buffer is free now
-        if (cf_refill) { issue_cf(it + 2); pend_cf = true; }
-        if (T.rope_smem && has_next) {
-            if (tid == RP_TID) issue_rp(it + 1);
-            pend_rp = true;
-        }
-
-        // ---- online softmax over the tile: warpgroup wg owns query heads wg, wg + NWG, ... The tile
-        // max is one warp reduction and one warpgroup barrier; each thread keeps the running sum
-        // of its own tokens (rescaled with the max), reduced once after the last tile
+        // the softmax denominators: each owning warp's token sums, added up across its warpgroup
         if (wg < G) {
-            float sc[HPW], m_new[HPW], corr[HPW];
-            #pragma unroll
-            for (int i = 0; i < HPW; ++i) {
-                const int g = wg + NWG * i;
-                sc[i] = -INFINITY; m_new[i] = -INFINITY; corr[i] = 0.f;
-                if (g < G) {
-                    float v = 0.f;
-                    #pragma unroll
-                    for (int c = 0; c < NWG; ++c) v += tmem_ld1(t_row + RED_COL + uint32_t(8 * c + g));
-                    tmem_wait_ld();
-                    sc[i] = valid ? v * scale : -INFINITY;
-                    const float mxg = warp_max(sc[i]);
-                    if (lane == 0) M->red_max[w & 3][g] = mxg;
-                }
-            }
-            wg_sync(wg);
             #pragma unroll
             for (int i = 0; i < HPW; ++i) {
                 const int g = wg + NWG * i;
                 if (g < G) {
-                    const float tmax = fmaxf(fmaxf(M->red_max[0][g], M->red_max[1][g]),
-                                             fmaxf(M->red_max[2][g], M->red_max[3][g]));
-                    const float m_old = M->m[g];
-                    m_new[i] = fmaxf(m_old, tmax);
-                    const float pg = (m_new[i] == -INFINITY || sc[i] == -INFINITY) ? 0.f : expf(sc[i] - m_new[i]);
-                    corr[i] = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new[i]);
-                    lsum[i] = fmaf(lsum[i], corr[i], pg);
-                    // P' = p * V ruler as fp16 hi (column g) + lo (column G + g); this token is K index t
-                    const float pv = pg * vrs;
-                    const uint32_t hb = f16_bits(pv);
-                    const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
-                    const int kt = t & 63, atom = t >> 6;
+                    float sum = lsum[i];
                     #pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const int n = k == 0 ? g : G + g;
-                        const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
-                                                      (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
-                        *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
-                    }
+                    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                    if (lane == 0) M->red_sum[w & 3][g] = sum;
                 }
             }
-            #pragma unroll
-            for (int i = 0; i < HPW; ++i) { corr_prev[i] = corr[i]; m_prev[i] = m_new[i]; }
         }
-        fence_async_smem();
-        tc_before();
-        __syncthreads();
-        tc_after();
-        // running max of each query head (every thread of its warpgroup has read the old one)
-        if (wg < G && t == 0) {
-            #pragma unroll
-            for (int i = 0; i < HPW; ++i) {
-                const int g = wg + NWG * i;
-                if (g < G) M->m[g] = m_prev[i];
-            }
-        }
+        timed_out = __syncthreads_or(timed_out);
 
-        // ---- MMA 2 of this tile: O^T = V^T . P', read back during the next tile
-        if (tid == MMA_TID) issue_pv(taddr + PV_COL);
-        pv_pending = true;
+        r_pending_any = r_pending;
+        pv_pending_any = pv_pending;
+        // ---- this segment's partials: slot = CTA index + pair index (one slot per (CTA, pair))
+        if (wg < G) {
+            #pragma unroll
+            for (int i = 0; i < HPW; ++i) {
+                const int g = wg + NWG * i;
+                if (g < G) P.part_o[(slot * G + g) * 128 + t] = timed_out ? 0.f : o[i];
+            }
+        }
+        if (tid < G) {
+            P.part_ml[(slot * G + tid) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
+            const float l = M->red_sum[0][tid] + M->red_sum[1][tid] + M->red_sum[2][tid] + M->red_sum[3][tid];
+            P.part_ml[(slot * G + tid) * 2 + 1] = timed_out ? 0.f : l;
+        }
     }
 
-    // ---- the last tile's PV
-    if (!timed_out && pv_pending) {
-        if (!mbar_wait(&M->mb_pv, ph_pv)) timed_out = true;
-        else { ph_pv ^= 1u; pv_pending = false; }
-        tc_after();
-        if (wg < G && !__any_sync(0xffffffffu, timed_out)) {
-            #pragma unroll
-            for (int i = 0; i < HPW; ++i) {
-                const int g = wg + NWG * i;
-                if (g < G) {
-                    const float dh = tmem_ld1(t_row + PV_COL + uint32_t(g));
-                    const float dl = tmem_ld1(t_row + PV_COL + uint32_t(G + g));
-                    tmem_wait_ld();
-                    o[i] = fmaf(o[i], corr_prev[i], dh + dl);
-                }
-            }
+    // ---- a timeout leaves the rest of the CTA's segments empty
+    if (timed_out) {
+        while (unit < hi && r < P.n_reqs) {
+            const int seq = P.seq_lens[r];
+            const int nt = req_tiles(seq);
+            const int64_t rs = before * nh, re = rs + int64_t(nt) * nh;
+            if (unit >= re) { before += nt; ++r; continue; }
+            const int hl = int((unit - rs) / nt);
+            const int64_t ps = rs + int64_t(hl) * nt;
+            empty_partial(int64_t(blockIdx.x) + int64_t(r) * nh + hl);
+            unit = min(hi, ps + nt);
         }
     }
-    // the softmax denominators: each owning warp's token sums, added up across its warpgroup
-    if (wg < G) {
-        #pragma unroll
-        for (int i = 0; i < HPW; ++i) {
-            const int g = wg + NWG * i;
-            if (g < G) {
-                float sum = lsum[i];
-                #pragma unroll
-                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                if (lane == 0) M->red_sum[w & 3][g] = sum;
-            }
-        }
-    }
-    timed_out = __syncthreads_or(timed_out);
 
     // ---- drain and release: anything still in flight gets one more bounded wait before TMEM and
     // the shared memory are released
     if (timed_out) {
         if (tid == 0) report(P.status, TTKV_STATUS_TIMEOUT);
-        if (r_pending) mbar_wait(&M->mb_r, ph_r);
-        if (pv_pending) mbar_wait(&M->mb_pv, ph_pv);
+        if (r_pending_any) mbar_wait(&M->mb_r, ph_r);
+        if (pv_pending_any) mbar_wait(&M->mb_pv, ph_pv);
         if (pend_cf) mbar_wait(&M->mb_cf, par_cf);
         if (pend_rp) mbar_wait(&M->mb_rp, par_rp);
         if (pend_kv0) mbar_wait(&M->mb_kv[0], par_kv0);
@@ -921,19 +1079,58 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     tc_before();
     __syncthreads();
     tc_after();
-    if (w == 0) tmem_dealloc(taddr, TMEM_COLS);
-    if (wg < G) {
-        #pragma unroll
-        for (int i = 0; i < HPW; ++i) {
-            const int g = wg + NWG * i;
-            if (g < G) P.part_o[((row_base + g) * P.n_splits + split) * 128 + t] = timed_out ? 0.f : o[i];
+    if (w == 0) tmem_dealloc(M->tmem_base, TMEM_COLS);
+}
+
+// Combine the segments of one (request, KV head, query head): thread = lane. The segments of
+// pair p are the CTAs whose unit ranges meet p's units [U, U + tiles), written at slots c + p.
+__global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
+    __shared__ long long red[2][4];
+    const int g = blockIdx.x, hl = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
+    const int nh = P.n_heads;
+    long long before = 0, all = 0;
+    for (int i = lane; i < P.n_reqs; i += 128) {
+        const int v = req_tiles(P.seq_lens[i]);
+        all += v;
+        if (i < r) before += v;
+    }
+    #pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        before += __shfl_xor_sync(0xffffffffu, before, off);
+        all += __shfl_xor_sync(0xffffffffu, all, off);
+    }
+    if ((lane & 31) == 0) { red[0][lane >> 5] = before; red[1][lane >> 5] = all; }
+    __syncthreads();
+    before = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+    all = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+    const int nt = req_tiles(P.seq_lens[r]);
+    float v = 0.f;
+    if (nt > 0) {
+        const long long T = all * nh, n = P.n_ctas;
+        const long long U = before * nh + (long long)hl * nt;
+        const long long c0 = ((U + 1) * n - 1) / T, c1 = ((U + nt) * n - 1) / T;
+        const long long p = (long long)r * nh + hl;
+        // a CTA whose share is empty (fewer units than CTAs) wrote nothing
+        auto empty = [&](long long c) { return c * T / n == (c + 1) * T / n; };
+        float M = -INFINITY;
+        for (long long c = c0; c <= c1; ++c)
+            if (!empty(c)) M = fmaxf(M, P.part_ml[((c + p) * P.G + g) * 2]);
+        float acc = 0.f, den = 0.f;
+        if (M != -INFINITY) {
+            for (long long c = c0; c <= c1; ++c) {
+                if (empty(c)) continue;
+                const long long row = (c + p) * P.G + g;
+                const float ms = P.part_ml[row * 2];
+                if (ms == -INFINITY) continue;
+                const float w = expf(ms - M);
+                acc = fmaf(w, P.part_o[row * 128 + lane], acc);
+                den = fmaf(w, P.part_ml[row * 2 + 1], den);
+            }
         }
+        v = den > 0.f ? acc / den : 0.f;
     }
-    if (tid < G) {
-        P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
-        const float l = M->red_sum[0][tid] + M->red_sum[1][tid] + M->red_sum[2][tid] + M->red_sum[3][tid];
-        P.part_ml[((row_base + tid) * P.n_splits + split) * 2 + 1] = timed_out ? 0.f : l;
-    }
+    const int head_q = (P.head_lo + hl) * P.G + g;
+    store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
 }
 
 // ------------------------------------------------------------------ host plan

@@ -61,6 +61,7 @@ struct ReadParams {
     float scale;
     int head_lo, n_heads;     // KV heads [head_lo, head_lo + n_heads)
     int qmax, n_qblk, n_splits, chunk;
+    int n_reqs, n_ctas;       // tensor-core decode: requests, CTAs of the balanced schedule
     float* part_o;            // [req][head][qmax*G][split][128]
     float* part_ml;           // [req][head][qmax*G][split][2]
     void* out;
@@ -478,38 +479,36 @@ int sm_count() {
 bool tc_serves(const ttkv_layout_t* lay, int HQ) {
     const int G = HQ / lay->H;
     // code windows hold 8 codes in 32 bits: widths up to 4 bits
-    return lay->d == 128 && lay->qbits == 8 && G >= 1 && G <= kMaxG && lay->r1 <= 192 &&
+    return lay->d == 128 && lay->qbits == 8 && G >= 1 && G <= kMaxG && lay->r1 <= tc::MAX_R1 &&
            lay->res_bits <= 4 && lay->v_bits <= 4 && lay->res_k <= 128 && lay->v_lanes <= 128 &&
            tc::tc_geom(lay, G).smem > 0;
 }
 
-// Splits for the tensor-core decode: one resident CTA per SM, 128-token tiles; minimise
-// waves x (tiles per CTA + the set-up of a CTA, about 3/4 of a tile). A split spans at most
-// tc::BT_CAP blocks of `block_size` tokens (the block-table slice a CTA caches); block_size 1 gives
-// the most splits, so a workspace sized for it covers every block size.
+// The tensor-core decode's grid: one resident CTA per SM, each taking an equal share of the
+// (request, KV head, tile) units. A CTA's run of tokens must fit the block-table slice it caches
+// (tc::BT_CAP blocks of `block_size` tokens), so when the batch's units (an upper bound from
+// max_seq) would give a CTA more tiles than that, the grid grows in whole waves. block_size 1 gives
+// the most CTAs, so a workspace sized for it covers every block size. Partials: one slot per
+// (CTA, pair) that can meet, CTA index + pair index, so n_ctas + pairs slots.
 Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads, int block_size) {
     Plan pl{};
     const int G = HQ / lay->H;
     pl.qb = 1;
     pl.n_qblk = 1;
-    const int tiles = std::max(1, (max_seq + tc::TM - 1) / tc::TM);
-    const int pairs = std::max(1, n_reqs * n_heads);
-    const int sms = sm_count();
-    double best = 1e30;
-    int best_s = 1;
-    for (int s = 1; s <= tiles; ++s) {
-        const int waves = (pairs * s + sms - 1) / sms;
-        const int per = (tiles + s - 1) / s;
-        if ((per * tc::TM + block_size - 1) / block_size + 1 > tc::BT_CAP) continue;
-        if (s > 64 && best < 1e30) break;
-        const double cost = double(waves) * (per + 0.75);
-        if (cost < best) { best = cost; best_s = s; }
-    }
-    pl.chunk = ((tiles + best_s - 1) / best_s) * tc::TM;
-    pl.n_splits = std::max(1, (max_seq + pl.chunk - 1) / pl.chunk);
-    const size_t rows = size_t(n_reqs) * n_heads * G;
-    pl.part_o_bytes = rows * pl.n_splits * 128 * sizeof(float);
-    pl.part_ml_bytes = rows * pl.n_splits * 2 * sizeof(float);
+    const long long tiles = std::max(1, (max_seq + tc::TM - 1) / tc::TM);
+    const long long pairs = std::max(1LL, (long long)n_reqs * n_heads);
+    const long long units = pairs * tiles;
+    const long long sms = sm_count();
+    const long long cap = std::max(1LL, (long long)(tc::BT_CAP - 1) * block_size / tc::TM);
+    long long n = sms;
+    if (units > cap * sms) n = (units + cap - 1) / cap;
+    n = (n + sms - 1) / sms * sms;
+    n = std::min(n, units);
+    pl.n_splits = int(n);
+    pl.chunk = 0;
+    const size_t slots = size_t(n + pairs);
+    pl.part_o_bytes = slots * G * 128 * sizeof(float);
+    pl.part_ml_bytes = slots * G * 2 * sizeof(float);
     pl.smem = size_t(tc::tc_geom(lay, G).smem);
     return pl;
 }
@@ -585,12 +584,11 @@ int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps
     auto k = tc::decode_tc_kernel<G>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T.smem) != cudaSuccess)
         return fail(TTKV_ERR_CUDA, "shared memory %d bytes refused", T.smem);
-    dim3 grid(pl.n_splits, P.n_heads, n_reqs);
-    k<<<grid, tc::NTHR, T.smem, st>>>(P, T, maps);
+    k<<<P.n_ctas, tc::NTHR, T.smem, st>>>(P, T, maps);
     if (int e = check_launch("decode_tc_kernel")) return e;
     dim3 mg(P.G, P.n_heads, n_reqs);
-    merge_kernel<<<mg, 128, 0, st>>>(P);
-    return check_launch("merge_kernel");
+    tc::merge_sk_kernel<<<mg, 128, 0, st>>>(P);
+    return check_launch("merge_sk_kernel");
 }
 
 int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
@@ -628,16 +626,24 @@ int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
 
 using namespace ttkv;
 
-extern "C" size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
-                                              int32_t max_seq_len, int32_t head_lo, int32_t head_hi) {
+namespace {
+// Scratch of a decode for caches of `block_size` tokens per block (1 covers every block size).
+size_t decode_workspace(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ, int32_t max_seq_len,
+                        int32_t head_lo, int32_t head_hi, int block_size) {
     if (!lay || lay->H < 1 || HQ < lay->H || head_hi <= head_lo) return 0;
     const Plan pl = make_plan(lay, n_reqs, HQ, 1, max_seq_len, head_hi - head_lo, false);
     size_t need = pl.part_o_bytes + pl.part_ml_bytes;
     if (tc_serves(lay, HQ)) {
-        const Plan pt = make_plan_tc(lay, n_reqs, HQ, max_seq_len, head_hi - head_lo, 1);
+        const Plan pt = make_plan_tc(lay, n_reqs, HQ, max_seq_len, head_hi - head_lo, block_size);
         need = std::max(need, pt.part_o_bytes + pt.part_ml_bytes);
     }
     return need;
+}
+}  // namespace
+
+extern "C" size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
+                                              int32_t max_seq_len, int32_t head_lo, int32_t head_hi) {
+    return decode_workspace(lay, n_reqs, HQ, max_seq_len, head_lo, head_hi, 1);
 }
 
 extern "C" size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
@@ -689,6 +695,7 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     P.q_start = multi ? q_start : nullptr; P.q_len = multi ? q_len : nullptr;
     P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
     P.qmax = multi ? max_q_len : 1; P.n_qblk = pl.n_qblk; P.n_splits = pl.n_splits; P.chunk = pl.chunk;
+    P.n_reqs = batch->n_reqs; P.n_ctas = use_tc ? pl.n_splits : 0;
     P.part_o = reinterpret_cast<float*>(workspace);
     P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
     P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
@@ -758,7 +765,7 @@ extern "C" int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_ca
                                          void* out, int32_t out_dtype, int64_t out_stride,
                                          int32_t max_seq_len, int32_t* status, void* stream) {
     if (int e = check_common(lay, cache, batch, rope, HQ, head_lo, head_hi)) return e;
-    const size_t need = ttkv_decode_workspace_bytes(lay, batch->n_reqs, HQ, max_seq_len, head_lo, head_hi);
+    const size_t need = decode_workspace(lay, batch->n_reqs, HQ, max_seq_len, head_lo, head_hi, cache->block_size);
     if (need > size_t(TTKV_NOALLOC_SCRATCH_BYTES))
         return fail(TTKV_ERR_WORKSPACE,
                     "this decode (%d requests, max_seq_len %d, HQ %d) needs %zu bytes of scratch but "

@@ -1,0 +1,70 @@
+"""KV-head sharding of the TT-KV read across ranks (one process per GPU).
+
+The reference has no multi-GPU path; this is the build's. The read shards by KV head: after the
+coefficient block every head's rows are independent. Rank g of N:
+
+* holds a replica of the byte-identical slot cache (the format is unchanged) and reads only its KV
+  heads [g*H/N, (g+1)*H/N) through `head_lo/head_hi` of the read ABI: the coefficient block of
+  every token plus its own heads' rows;
+* writes its query heads [head_lo*G, head_hi*G) of each layer's output, which are all-gathered over
+  the process group and reassembled in head order, so every rank ends with the whole output.
+
+The write stays replicated: every rank encodes the step's tokens into its own replica. Collectives
+go through `torch.distributed` (NCCL on GPUs, gloo in the CPU tests), with the gathered tensor
+concatenated along dim 0, the form both backends accept.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def head_range(rank: int, world: int, H: int) -> tuple[int, int]:
+    """KV heads [lo, hi) of `rank`: contiguous, equal shares in rank order."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if H % world:
+        raise ValueError(f"{world} ranks do not divide the {H} KV heads")
+    n = H // world
+    return rank * n, (rank + 1) * n
+
+
+class HeadShard:
+    """This rank's share of a head-sharded read and the all-gather that reassembles the output."""
+
+    def __init__(self, H: int, HQ: int, world: int | None = None, rank: int | None = None, group=None):
+        if HQ % H:
+            raise ValueError(f"HQ={HQ} is not a multiple of H={H}")
+        self.group = group
+        self.world = dist.get_world_size(group) if world is None else int(world)
+        self.rank = dist.get_rank(group) if rank is None else int(rank)
+        self.H, self.HQ, self.G = H, HQ, HQ // H
+        self.head_lo, self.head_hi = head_range(self.rank, self.world, H)
+        self.q_lo, self.q_hi = self.head_lo * self.G, self.head_hi * self.G
+
+    def buffers(self, B: int, d: int, dtype, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """(send [B, G*n, d], recv [world*B, G*n, d]) for one layer's output."""
+        n = self.q_hi - self.q_lo
+        return (torch.empty(B, n, d, dtype=dtype, device=device),
+                torch.empty(self.world * B, n, d, dtype=dtype, device=device))
+
+    def pack(self, out: torch.Tensor, send: torch.Tensor) -> None:
+        """This rank's query heads of a layer output [B, HQ, d] into the send buffer."""
+        send.copy_(out[:, self.q_lo:self.q_hi])
+
+    def gather(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+
+    def assemble(self, recv: torch.Tensor, out: torch.Tensor) -> None:
+        """The gathered shares [world*B, G*n, d] into `out` [B, HQ, d], rank r's at its heads."""
+        B, _, d = out.shape
+        out.copy_(recv.view(self.world, B, -1, d).permute(1, 0, 2, 3).reshape(B, self.HQ, d))
+
+    def read(self, read_fn, out: torch.Tensor, send: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:
+        """`read_fn(head_lo, head_hi, out)` writes this rank's query heads of `out`; afterwards `out`
+        holds every head on every rank."""
+        read_fn(self.head_lo, self.head_hi, out)
+        self.pack(out, send)
+        self.gather(send, recv)
+        self.assemble(recv, out)
+        return out
