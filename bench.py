@@ -334,6 +334,153 @@ def run_reference(args):
     print(json.dumps(line))
 
 
+# ---------------------------------------------------------------------------- other workloads
+def _event_ms(fn, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_prefill(args):
+    """Config 3, chunked-prefill continuation: `--batch` prompts of `--prompt-len` tokens continued
+    in `--chunk`-token chunks against one layer's compressed store (r1 = 110, `safe`, fp16 store,
+    block 16). One step = every chunk after the first: the frozen write of the chunk's tokens of all
+    prompts, then ONE continuation read (`ttkv_prefill_cont_paged`) of all prompts, causal over the
+    stored rows. The first chunk (SDPA over the model's own keys + the fit) is set-up."""
+    import numpy as np
+    import torch
+
+    from vllm_ttkv import encode, ops, synthetic
+    from vllm_ttkv.layout import layout_for_config
+    device = torch.device("cuda", 0)
+    B, N, Q, H, HQ, bs, r1 = args.batch, args.prompt_len, args.chunk, 8, 24, 16, 110
+    lay = layout_for_config("safe", r1, H=H)
+    bt_np, n_blocks = synthetic.block_table(0, [N] * B, bs)
+    bt = torch.from_numpy(bt_np).to(device)
+    slots_all = torch.from_numpy((bt_np[:, :, None].astype(np.int64) * bs + np.arange(bs)).reshape(B, -1)[:, :N]).to(device)
+    cache = torch.zeros(n_blocks * bs, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    dec = torch.zeros(B, r1, H * 128, device=device)
+    pinvT = torch.zeros_like(dec)
+    Ks, Vs = [], []
+    for r in range(B):
+        K, V = synth_kv_device(gen, H, N, dtype=torch.float16)
+        fk = encode.fit_into_budget(K[:, :Q], lay, "safe")
+        encode.write_fitted(cache, slots_all[r, :Q].contiguous(), fk, K[:, :Q].permute(1, 0, 2).contiguous(),
+                            V[:, :Q].permute(1, 0, 2).contiguous(), lay)
+        dec[r], pinvT[r] = fk.decoder.decoder_f, fk.decoder.pinvT
+        Ks.append(K.permute(1, 0, 2).contiguous())
+        Vs.append(V.permute(1, 0, 2).contiguous())
+    table = torch.from_numpy(synthetic.cos_sin_cache(N + 16, dtype="float32")).to(device).half()
+    q = torch.randn(B * Q, HQ, 128, generator=gen, device=device).half()
+    out = torch.empty_like(q)
+    idx = torch.arange(B, dtype=torch.int32, device=device)
+    chunks = []
+    for s0 in range(Q, N, Q):
+        e = min(N, s0 + Q)
+        ql = e - s0
+        chunks.append(dict(
+            e=e, ql=ql, slots=slots_all[:, s0:e].reshape(-1).contiguous(),
+            k=torch.cat([Ks[r][s0:e] for r in range(B)]), v=torch.cat([Vs[r][s0:e] for r in range(B)]),
+            tok=torch.repeat_interleave(idx, ql), seq=torch.full((B,), e, dtype=torch.int32, device=device),
+            q_start=(idx * ql).contiguous(), q_len=torch.full((B,), ql, dtype=torch.int32, device=device)))
+    def step():
+        for c in chunks:
+            encode.write_frozen(cache, c["slots"], c["k"], c["v"], c["tok"], dec, pinvT, lay)
+            ops.prefill_cont_paged(lay, cache, bs, bt, c["seq"], dec, idx, table, c["q_start"], c["q_len"],
+                                   q, 128 ** -0.5, out, c["ql"], c["e"])
+
+    ms = _event_ms(step, args.steps, args.warmup)
+    # the continuation launches alone, on the launching stream
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in chunks]
+    torch.cuda.synchronize()
+    for (a, b), c in zip(evs, chunks):
+        a.record()
+        ops.prefill_cont_paged(lay, cache, bs, bt, c["seq"], dec, idx, table, c["q_start"], c["q_len"],
+                               q, 128 ** -0.5, out, c["ql"], c["e"])
+        b.record()
+    torch.cuda.synchronize()
+    read_ms = sum(a.elapsed_time(b) for a, b in evs)
+    # algorithmic work of the reads: causal QK + PV over the stored rows, reconstruction once per chunk
+    flops = 0.0
+    for c in chunks:
+        s0 = c["e"] - c["ql"]
+        pairs = c["ql"] * s0 + c["ql"] * (c["ql"] + 1) / 2
+        flops += B * (4 * 128 * HQ * pairs + 2 * r1 * H * 128 * c["e"])
+    hbm, tc, peak_kind = _peaks()
+    tflops = flops / (read_ms * 1e-3) / 1e12
+    line = {"metric": "chunked-prefill continuation tok/s (cfg3)", "value": B * (N - Q) / (ms * 1e-3),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "workload": "prefill", "dtype": "fp16 model tensors, fp32 math, u8 slots",
+            "data": "synthetic",
+            "config": {"workload": f"cfg3: {B} prompts x {N} tokens, chunks of {Q}, 1 layer r1={r1} safe, block {bs}",
+                       "chunks": len(chunks)},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc, "unit": "TFLOP/s",
+                         "frac": tflops / tc, "peak_kind": peak_kind, "read_ms_per_step": read_ms,
+                         "kernel": "attn_split_kernel<3,16,true> + merge_kernel (ttkv_prefill_cont_paged)",
+                         "algorithmic_flop_per_step": flops},
+            "gpu_launches": len(chunks) * 4}
+    print(json.dumps(line))
+
+
+def run_encode(args):
+    """Config 4, the write path at prefill: one request of `--prompt-len` tokens (16384 for config 4),
+    `--layers` layers at the `tight` allocation with r1 = 110: per layer the TT-SVD fit
+    (`torch.linalg.svd`, a library call as in the reference) + the fit tail and the fitted write
+    (this repository's kernels). The config's 8 requests shard one per GPU with no exchange, so a
+    single GPU runs one request."""
+    import numpy as np
+    import torch
+
+    from vllm_ttkv import encode, ops, synthetic
+    from vllm_ttkv.layout import layout_for_config
+    device = torch.device("cuda", 0)
+    n, H, r1, L = args.prompt_len, 8, 110, args.layers
+    lay = layout_for_config("tight", r1, H=H)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    cache = torch.zeros(n, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device)
+    slots = torch.arange(n, dtype=torch.int64, device=device)
+    KV = [synth_kv_device(gen, H, n, dtype=torch.bfloat16) for _ in range(min(L, 4))]
+    toks = [(K.permute(1, 0, 2).contiguous(), V.permute(1, 0, 2).contiguous()) for K, V in KV]
+    fits = {}
+
+    def step():
+        for l in range(L):
+            K, _ = KV[l % len(KV)]
+            kt, vt = toks[l % len(KV)]
+            fk = encode.fit_into_budget(K, lay, "tight")
+            encode.write_fitted(cache, slots, fk, kt, vt, lay)
+            fits[l % len(KV)] = fk
+
+    ms = _event_ms(step, args.steps, args.warmup)
+    # this repository's write launch alone (the select/quantise/pack of every token), per layer
+    fk = fits[0]
+    kt, vt = toks[0]
+    w_ms = _event_ms(lambda: encode.write_fitted(cache, slots, fk, kt, vt, lay), 10, 3)
+    alg = n * H * 128 * 2 * 2 + n * lay.compressed_bytes_per_token()     # K, V bf16 in; slots out
+    hbm, tc, peak_kind = _peaks()
+    gbs = alg / (w_ms * 1e-3) / 1e9
+    line = {"metric": "prefill encode tok/s (cfg4, one request per GPU)", "value": n / (ms * 1e-3),
+            "unit": f"tok/s ({L} layers)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "ms_per_layer": ms / L, "higher_is_better": True, "workload": "encode",
+            "dtype": "bf16 in, fp32 fit, u8 slots", "data": "synthetic",
+            "config": {"workload": f"cfg4: 1 request x {n} tokens, {L} layers, tight r1={r1}"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_kind": peak_kind, "kernel": "encode_pack_kernel (ttkv_write_paged, fit path)",
+                         "write_ms_per_layer": w_ms, "alg_bytes_per_layer": alg}}
+    print(json.dumps(line))
+
+
 # ---------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -348,9 +495,21 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying per-layer CUDA graphs")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "encode"],
+                    help="decode: config 1 (the default line); prefill: config 3; encode: config 4")
+    ap.add_argument("--prompt-len", type=int, default=None,
+                    help="prefill: prompt tokens (7379); encode: tokens per request (16384)")
+    ap.add_argument("--chunk", type=int, default=256, help="prefill: query tokens per chunk")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload != "decode":
+        if args.prompt_len is None:
+            args.prompt_len = 7379 if args.workload == "prefill" else 16384
+        if args.steps == 200:                      # the decode default; these steps take seconds
+            args.steps = 3
+        (run_prefill if args.workload == "prefill" else run_encode)(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
