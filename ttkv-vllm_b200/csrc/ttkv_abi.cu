@@ -2,6 +2,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "ttkv_common.cuh"
 
@@ -27,6 +30,27 @@ int fail(int code, const char* fmt, ...) {
 int check_launch(const char* what) {
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return TTKV_OK;
+}
+
+int raise_smem_limit(const void* kernel, const char* what) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void*>> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return fail(TTKV_ERR_CUDA, "cudaGetDevice"); }
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == dev && d.second == kernel) return TTKV_OK;
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, kernel) != cudaSuccess ||
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - int(fa.sharedSizeBytes)) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        return fail(TTKV_ERR_CUDA, "%s: raising the shared-memory limit: %s", what, cudaGetErrorString(e));
+    }
+    done.emplace_back(dev, kernel);
     return TTKV_OK;
 }
 

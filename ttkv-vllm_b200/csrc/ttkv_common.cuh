@@ -19,6 +19,11 @@ constexpr int kMaxG = 8;          // largest GQA group (HQ / H)
 void set_error(const char* fmt, ...);
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
+// Raise a kernel's dynamic shared-memory limit to the device's opt-in maximum (less its static
+// shared memory), once per kernel and device; a launch then only names its own size. A per-launch
+// limit would be a property of the last launch, not of each launch (a graph node replayed on its
+// own, or two threads, would see another layer's value).
+int raise_smem_limit(const void* kernel, const char* what);
 
 // ------------------------------------------------------------------ device status
 // First error wins: a status word that already holds a code keeps it.

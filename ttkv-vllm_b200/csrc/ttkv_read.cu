@@ -561,8 +561,7 @@ ReadParams base_params(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
 template <int G, int QB, bool MULTI>
 int launch_g(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     auto k = attn_split_kernel<G, QB, MULTI>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) != cudaSuccess)
-        return fail(TTKV_ERR_CUDA, "shared memory %zu bytes refused", pl.smem);
+    if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "attn_split_kernel")) return e;
     dim3 grid(pl.n_splits, P.n_heads * pl.n_qblk, n_reqs);
     k<<<grid, NT, pl.smem, st>>>(P);
     if (int e = check_launch("attn_split_kernel")) return e;
@@ -582,8 +581,7 @@ template <int G>
 int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
                 cudaStream_t st) {
     auto k = tc::decode_tc_kernel<G>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T.smem) != cudaSuccess)
-        return fail(TTKV_ERR_CUDA, "shared memory %d bytes refused", T.smem);
+    if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "decode_tc_kernel")) return e;
     k<<<P.n_ctas, tc::NTHR, T.smem, st>>>(P, T, maps);
     if (int e = check_launch("decode_tc_kernel")) return e;
     dim3 mg(P.G, P.n_heads, n_reqs);

@@ -598,9 +598,8 @@ int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_cache_t* cache, con
         !encode_2d(&maps.dec, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, decoders, cols, rows, cols * 4, kHeadDim,
                    lay->r1, 0))
         return 1;
-    if (cudaFuncSetAttribute(write_frozen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)) !=
-        cudaSuccess) {
-        cudaGetLastError();
+    if (raise_smem_limit(reinterpret_cast<const void*>(write_frozen_kernel), "write_frozen_kernel") != TTKV_OK) {
+        set_error("%s", "");                                 // the two-launch write serves instead
         return 1;
     }
     {   // the H CTAs of a cluster must fit on the GPU at once (asked once per shape)
