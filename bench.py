@@ -127,7 +127,7 @@ class Workload:
         import numpy as np
         import torch
 
-        from vllm_ttkv import encode, synthetic
+        from vllm_ttkv import encode, ops, synthetic
         from vllm_ttkv.layout import layout_for_config
         self.B, self.n, self.HQ, self.H, self.bs = B, n, HQ, H, block_size
         self.r1s = list(r1s)
@@ -145,7 +145,7 @@ class Workload:
         self.new_slots = slots_all[:, n].contiguous()             # [B] slot of the step's token
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
-        self.layouts, self.caches, self.decoders, self.pinvT = [], [], [], []
+        self.layouts, self.caches, self.decoders, self.pinvT, self.images = [], [], [], [], []
         self.k_new, self.v_new, self.q, self.out = [], [], [], []
         self.fit_s = 0.0
         self.dec_index = torch.arange(B, dtype=torch.int32, device=device)
@@ -173,6 +173,7 @@ class Workload:
             self.layouts.append(lay)
             self.caches.append(cache)
             self.decoders.append(dec)
+            self.images.append(ops.decoder_image(lay, dec))       # made once per decoder, as the pool does
             self.pinvT.append(pinvT)
             self.k_new.append(kn)
             self.v_new.append(vn)
@@ -203,7 +204,7 @@ class Workload:
                             self.dec_index, self.decoders[l], self.pinvT[l], lay)
         ops.decode_paged(lay, self.caches[l], self.bs, self.block_table, self.seq_lens,
                          self.decoders[l], self.dec_index, self.table, self.q[l], self.scale,
-                         self.out[l], self.max_seq, head_lo, head_hi)
+                         self.out[l], self.max_seq, head_lo, head_hi, images=self.images[l])
 
     def step(self, head_lo=0, head_hi=8, gather=None):
         for l in range(self.L):
@@ -606,7 +607,7 @@ def main():
             a.record()
             ops.decode_paged(wl.layouts[l], wl.caches[l], wl.bs, wl.block_table, wl.seq_lens,
                              wl.decoders[l], wl.dec_index, wl.table, wl.q[l], wl.scale, wl.out[l],
-                             wl.max_seq, head_lo, head_hi)
+                             wl.max_seq, head_lo, head_hi, images=wl.images[l])
             b.record()
     torch.cuda.synchronize(device)
     dec_ms = [a.elapsed_time(b) for a, b in evs]

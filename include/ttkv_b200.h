@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define TTKV_ABI_VERSION 1
+#define TTKV_ABI_VERSION 2
 
 /* host-side refusals (return values) */
 #define TTKV_OK 0
@@ -94,7 +94,10 @@ typedef struct ttkv_cache {
 /* The batch's paging and decoders. Request r owns block_table[r*bt_stride + 0..], its first
  * seq_lens[r] tokens are stored (position = index), and its decoder is
  * decoders[dec_index[r]*dec_stride .. +r1*H*d] (fp32 [r1, H*d], column m = h*d + j, the
- * reference's decoder_f, vllm_ttkv/encode.py:178-211). */
+ * reference's decoder_f, vllm_ttkv/encode.py:178-211).
+ * Optional (null: the decode converts the decoders itself): dec_image, the same decoders as
+ * ttkv_decoder_image wrote them, decoder i at dec_image + i*image_stride bytes, and dec_scales
+ * [n_decoders * H] from the same call. */
 typedef struct ttkv_batch {
     const int32_t* block_table;
     int64_t bt_stride;
@@ -105,7 +108,26 @@ typedef struct ttkv_batch {
     int64_t dec_stride;
     const int32_t* dec_index;
     int32_t n_decoders;
+    const void* dec_image;
+    int64_t image_stride;
+    const float* dec_scales;
 } ttkv_batch_t;
+
+/* ---------------------------------------------------------------- decoder images
+ * No counterpart in the reference: an addition of this library.
+ * A decoder is fixed for the life of its request, so the operand form the tensor-core decode
+ * stages from it can be made once: per KV head h, the head's [r1, d] slice scaled by 2^-e (the
+ * power of two that brings its largest |value| into [2^13, 2^14)) and split into fp16 hi + lo,
+ * in the byte layout of the decode's shared-memory operand; and 2^e. A decode given the image
+ * stages it with one bulk copy instead of reading and converting the fp32 decoder.
+ *   ttkv_decoder_image_bytes: bytes per decoder (H heads), 0 when the tensor-core decode does not
+ *     serve the layout (then a decode ignores images);
+ *   ttkv_decoder_image: decoders [n, r1, H*d] fp32 (decoder i at decoders + i*dec_stride) ->
+ *     image + i*image_stride (16-byte aligned, image_stride >= ttkv_decoder_image_bytes) and
+ *     scales[i*H + h]. */
+size_t ttkv_decoder_image_bytes(const ttkv_layout_t* lay);
+int ttkv_decoder_image(const ttkv_layout_t* lay, const float* decoders, int64_t dec_stride, int32_t n,
+                       void* image, int64_t image_stride, float* scales, void* stream);
 
 /* The model's RoPE table in vLLM's layout: [rows, d] = cat(cos, sin) in the model dtype
  * (vllm_ttkv/decode.py:54-122). */

@@ -36,7 +36,7 @@ def _dev(st, q=None):
         tdt=tdt)
 
 
-def _decode(st, out_dtype=torch.float32, head_lo=0, head_hi=None, q=None, scale=None):
+def _decode(st, out_dtype=torch.float32, head_lo=0, head_hi=None, q=None, scale=None, images=False):
     from vllm_ttkv import ops
     d = _dev(st, q)
     B, HQ, _ = d["q"].shape
@@ -44,7 +44,8 @@ def _decode(st, out_dtype=torch.float32, head_lo=0, head_hi=None, q=None, scale=
     ops.reset_status()
     ops.decode_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"], d["idx"],
                      d["table"], d["q"], 128 ** -0.5 if scale is None else scale, out,
-                     int(st["seq_lens"].max()), head_lo, head_hi)
+                     int(st["seq_lens"].max()), head_lo, head_hi,
+                     images=ops.decoder_image(d["lay"], d["dec"]) if images else None)
     ops.check_status()
     return out.float().cpu().numpy()
 
@@ -97,6 +98,17 @@ def test_decode_head_shard_writes_only_its_heads():
 def test_decode_long_context_split_merge():
     st = stores.make_store(6, [2100], cfg="safe", r1=48)
     assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_decoder_images_stage_the_same_operand_the_decode_builds():
+    """ttkv_decoder_image converts each decoder once; a decode staging the image must give the
+    same bits as one converting the fp32 decoder itself (one and three K atoms)."""
+    for r1 in (32, 110, 143):
+        st = stores.make_store(12, [300, 77, 129], cfg="safe", r1=r1)
+        a = _decode(st)
+        b = _decode(st, images=True)
+        assert np.array_equal(a, b), r1
+        assert np.abs(b - stores.expected_decode(st)).max() < 1e-4, r1
 
 
 def test_decode_schedule_over_more_requests_than_one_scan_chunk():

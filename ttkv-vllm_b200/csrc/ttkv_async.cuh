@@ -74,6 +74,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global
+// memory into this CTA's shared memory, its bytes counted on `bar`. No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
 // A 2-D TMA map: `rows` rows of `d0` elements of `dt`, `stride` bytes apart; boxes of b0 x b1
 // elements, swizzled by `box_bytes` (the box's inner width when it is 32, 64 or 128 bytes; any
 // other value: no swizzle). False if the driver's encoder is unavailable or refuses the tensor.

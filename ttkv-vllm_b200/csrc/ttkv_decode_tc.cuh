@@ -274,7 +274,7 @@ struct TcMisc {
     int scan[NTHR / 32];
     int sched_r;
     long long sched_before;
-    uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2];
+    uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2], mb_dec;
     uint32_t tmem_base;
 };
 
@@ -433,6 +433,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         mbar_init(&M->mb_rp, 1);
         mbar_init(&M->mb_kv[0], NTHR);
         mbar_init(&M->mb_kv[1], NTHR);
+        mbar_init(&M->mb_dec, 1);
     }
     if (tid < 32) {
         const int n = tid & 15, bits = tid < 16 ? P.res_bits : P.v_bits;
@@ -536,8 +537,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const float scale = P.scale;
     const float4* qs4 = reinterpret_cast<const float4*>(qs);
 
-    uint32_t ph_r = 0, ph_pv = 0;
-    bool r_pending_any = false, pv_pending_any = false;
+    uint32_t ph_r = 0, ph_pv = 0, ph_dec = 0;
+    bool r_pending_any = false, pv_pending_any = false, pend_dec = false;
 
     while (unit < hi && !timed_out) {
         // ---- the next segment: the run of this CTA's units that belongs to one (request, KV head)
@@ -658,59 +659,73 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         if (tid == RP_TID && T.rope_smem) issue_rp(0);
         pend_cf = true; pend_kv0 = true;
         if (T.rope_smem) pend_rp = true;
-        float mx = 0.f;
-        {
-            const float4* d4 = reinterpret_cast<const float4*>(dec - t) + lane;
-            const int64_t rs4 = dstride / 4;
-            #pragma unroll
-            for (int i = 0; i < MAX_R1 / 16; ++i) {
-                const int rr = w + 16 * i;
-                if (rr < P.r1) {
-                    const float4 v = d4[rr * rs4];
-                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                }
+        float s_up;
+        if (P.dec_image) {
+            // the decoder's operand image (ttkv_decoder_image): one bulk copy into bhi || blo, which
+            // the MMA thread waits for before the segment's first reconstruction
+            if (tid == MMA_TID) {
+                const uint32_t bytes = uint32_t(2 * T.natom * ATOM_BYTES);
+                mbar_expect_tx(&M->mb_dec, bytes);
+                bulk_g2s(bhi, P.dec_image + int64_t(di) * P.image_stride + int64_t(h) * bytes, bytes, &M->mb_dec);
+                pend_dec = true;
             }
-        }
-        mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
-        if (lane == 0) M->maxabs[w] = mx;
-        __syncthreads();
-        // decoder slice (again, from L2, while the tile's copies fly): power-of-two scale so
-        // max|D| * 2^-e lies in [2^13, 2^14), then fp16 hi + lo
-        mx = 0.f;
-        #pragma unroll
-        for (int i = 0; i < NTHR / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
-        int e = 0;
-        if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
-        e = max(-100, min(100, e));
-        const float s_down = __uint_as_float(uint32_t(127 - e) << 23);   // 2^-e
-        const float s_up = __uint_as_float(uint32_t(127 + e) << 23);     // 2^e
-        #pragma unroll
-        for (int jc = 0; jc < DEC_CHUNKS; ++jc) {
-            const int cidx = wg + NWG * jc;
-            if (cidx < nchunk) {
-                float dv[8];
+            s_up = P.dec_scales[int64_t(di) * P.H + h];
+        } else {
+            float mx = 0.f;
+            {
+                const float4* d4 = reinterpret_cast<const float4*>(dec - t) + lane;
+                const int64_t rs4 = dstride / 4;
                 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int rr = cidx * 8 + k;
-                    dv[k] = rr < P.r1 ? dec[rr * dstride] : 0.f;
-                }
-                uint32_t hw[4], lw[4];
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint32_t hh[2], ll[2];
-                    #pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const float v = dv[2 * i + k] * s_down;
-                        hh[k] = f16_bits(v);
-                        ll[k] = f16_bits(v - f16_bits_to_f32(hh[k]));
+                for (int i = 0; i < MAX_R1 / 16; ++i) {
+                    const int rr = w + 16 * i;
+                    if (rr < P.r1) {
+                        const float4 v = d4[rr * rs4];
+                        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
                     }
-                    hw[i] = hh[0] | (hh[1] << 16);
-                    lw[i] = ll[0] | (ll[1] << 16);
                 }
-                const uint32_t off = uint32_t((cidx >> 3) * ATOM_BYTES) + kmajor_off(t, cidx & 7);
-                *reinterpret_cast<uint4*>(bhi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
             }
+            mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+            if (lane == 0) M->maxabs[w] = mx;
+            __syncthreads();
+            // decoder slice (again, from L2, while the tile's copies fly): power-of-two scale so
+            // max|D| * 2^-e lies in [2^13, 2^14), then fp16 hi + lo
+            mx = 0.f;
+            #pragma unroll
+            for (int i = 0; i < NTHR / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
+            int e = 0;
+            if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
+            e = max(-100, min(100, e));
+            const float s_down = __uint_as_float(uint32_t(127 - e) << 23);   // 2^-e
+            s_up = __uint_as_float(uint32_t(127 + e) << 23);                 // 2^e
+            #pragma unroll
+            for (int jc = 0; jc < DEC_CHUNKS; ++jc) {
+                const int cidx = wg + NWG * jc;
+                if (cidx < nchunk) {
+                    float dv[8];
+                    #pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int rr = cidx * 8 + k;
+                        dv[k] = rr < P.r1 ? dec[rr * dstride] : 0.f;
+                    }
+                    uint32_t hw[4], lw[4];
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t hh[2], ll[2];
+                        #pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const float v = dv[2 * i + k] * s_down;
+                            hh[k] = f16_bits(v);
+                            ll[k] = f16_bits(v - f16_bits_to_f32(hh[k]));
+                        }
+                        hw[i] = hh[0] | (hh[1] << 16);
+                        lw[i] = ll[0] | (ll[1] << 16);
+                    }
+                    const uint32_t off = uint32_t((cidx >> 3) * ATOM_BYTES) + kmajor_off(t, cidx & 7);
+                    *reinterpret_cast<uint4*>(bhi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+            }
+
         }
 
         // ---- first tile: its coefficient block, its A, its reconstruction (TMEM columns 0..127)
@@ -722,6 +737,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         tc_after();
         const uint32_t taddr = M->tmem_base;
         const uint32_t t_row = taddr + (uint32_t(32 * (w & 3)) << 16);    // this warp's TMEM lanes
+        if (tid == MMA_TID && pend_dec) {
+            if (!mbar_wait(&M->mb_dec, ph_dec)) timed_out = true;
+            else { ph_dec ^= 1u; pend_dec = false; }
+        }
         if (tid == MMA_TID) issue_recon(taddr);
         if (n_tiles > 1) {                                              // every conversion of tile 0 is done
             issue_cf(1);
@@ -1075,6 +1094,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         if (pend_rp) mbar_wait(&M->mb_rp, par_rp);
         if (pend_kv0) mbar_wait(&M->mb_kv[0], par_kv0);
         if (pend_kv1) mbar_wait(&M->mb_kv[1], par_kv1);
+        if (pend_dec) mbar_wait(&M->mb_dec, ph_dec);
     }
     tc_before();
     __syncthreads();
@@ -1133,7 +1153,56 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
 }
 
+// The decoders' operand images (ttkv_decoder_image): grid (decoders, KV heads), thread t = column
+// t of the head's slice. The same scale and split as the decode's own staging, byte for byte, in
+// the layout of its bhi || blo shared-memory region.
+__global__ void __launch_bounds__(128) decoder_image_kernel(const float* dec, int64_t dec_stride, int r1, int H,
+                                                            int kp16, int natom, unsigned char* image,
+                                                            int64_t image_stride, float* scales) {
+    __shared__ float wmax[4];
+    const int n = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    const float* col = dec + int64_t(n) * dec_stride + h * 128 + t;
+    const int64_t rs = int64_t(H) * 128;
+    float mx = 0.f;
+    for (int rr = 0; rr < r1; ++rr) mx = fmaxf(mx, fabsf(col[rr * rs]));
+    mx = warp_max(mx);
+    if ((t & 31) == 0) wmax[t >> 5] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    int e = 0;
+    if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
+    e = max(-100, min(100, e));
+    const float s_down = __uint_as_float(uint32_t(127 - e) << 23);
+    unsigned char* bhi = image + int64_t(n) * image_stride + int64_t(h) * 2 * natom * ATOM_BYTES;
+    unsigned char* blo = bhi + natom * ATOM_BYTES;
+    for (int cidx = 0; cidx < kp16 / 8; ++cidx) {
+        uint32_t hw[4], lw[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t hh[2], ll[2];
+            #pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int rr = cidx * 8 + 2 * i + k;
+                const float v = rr < r1 ? col[rr * rs] * s_down : 0.f;
+                hh[k] = f16_bits(v);
+                ll[k] = f16_bits(v - f16_bits_to_f32(hh[k]));
+            }
+            hw[i] = hh[0] | (hh[1] << 16);
+            lw[i] = ll[0] | (ll[1] << 16);
+        }
+        const uint32_t off = uint32_t((cidx >> 3) * ATOM_BYTES) + kmajor_off(t, cidx & 7);
+        *reinterpret_cast<uint4*>(bhi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(blo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    if (t == 0) scales[int64_t(n) * H + h] = __uint_as_float(uint32_t(127 + e) << 23);
+}
+
 // ------------------------------------------------------------------ host plan
+// Bytes of one decoder's image: per KV head the hi and lo operand atoms.
+inline size_t image_bytes(const ttkv_layout_t* lay) {
+    const int kp16 = (lay->r1 + 15) / 16 * 16;
+    return size_t(lay->H) * 2 * ((kp16 + 63) / 64) * ATOM_BYTES;
+}
 inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
 // The shared-memory plan of decode_tc_kernel for a layout, or smem == 0 if it does not fit.

@@ -49,6 +49,9 @@ struct ReadParams {
     int64_t dec_stride;
     const int32_t* dec_index;
     int n_decoders;
+    const unsigned char* dec_image;   // optional: ttkv_decoder_image's operand images
+    int64_t image_stride;
+    const float* dec_scales;
     const void* table;
     int table_dtype;
     int64_t table_rows;
@@ -535,6 +538,13 @@ int check_common(const ttkv_layout_t* lay, const ttkv_cache_t* cache, const ttkv
         return fail(TTKV_ERR_ARG, "decoder stride %lld < r1*H*d", (long long)batch->dec_stride);
     if ((reinterpret_cast<uintptr_t>(batch->decoders) & 15) || (batch->dec_stride & 3))
         return fail(TTKV_ERR_ALIGN, "decoders must be 16-byte aligned with a stride of 4 floats");
+    if (batch->dec_image) {
+        const size_t img = tc_serves(lay, HQ) ? tc::image_bytes(lay) : 0;
+        if (img && ((reinterpret_cast<uintptr_t>(batch->dec_image) & 15) || (batch->image_stride & 15) ||
+                    batch->image_stride < int64_t(img) || !batch->dec_scales))
+            return fail(TTKV_ERR_ALIGN, "decoder images must be 16-byte aligned, %zu bytes apart at least, "
+                        "with their scales", img);
+    }
     if (!rope->table || rope->rows < 1) return fail(TTKV_ERR_ARG, "RoPE table missing");
     if (rope->dtype < TTKV_F32 || rope->dtype > TTKV_BF16) return fail(TTKV_ERR_ARG, "RoPE dtype");
     return TTKV_OK;
@@ -554,6 +564,8 @@ ReadParams base_params(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
     P.block_table = batch->block_table; P.bt_stride = batch->bt_stride; P.bt_cols = batch->bt_cols;
     P.seq_lens = batch->seq_lens; P.decoders = batch->decoders; P.dec_stride = batch->dec_stride;
     P.dec_index = batch->dec_index; P.n_decoders = batch->n_decoders;
+    P.dec_image = static_cast<const unsigned char*>(batch->dec_image);
+    P.image_stride = batch->image_stride; P.dec_scales = batch->dec_scales;
     P.table = rope->table; P.table_dtype = rope->dtype; P.table_rows = rope->rows;
     return P;
 }
@@ -711,6 +723,28 @@ extern "C" int ttkv_decode_paged(const ttkv_layout_t* lay, const ttkv_cache_t* c
     return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ, scale,
                       head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, workspace,
                       workspace_bytes, status, stream);
+}
+
+extern "C" size_t ttkv_decoder_image_bytes(const ttkv_layout_t* lay) {
+    if (!lay || lay->d != kHeadDim || lay->r1 < 1 || lay->r1 > tc::MAX_R1) return 0;
+    return tc::image_bytes(lay);
+}
+
+extern "C" int ttkv_decoder_image(const ttkv_layout_t* lay, const float* decoders, int64_t dec_stride, int32_t n,
+                                  void* image, int64_t image_stride, float* scales, void* stream) {
+    if (!lay) return fail(TTKV_ERR_ARG, "layout is null");
+    const size_t per = ttkv_decoder_image_bytes(lay);
+    if (!per) return fail(TTKV_ERR_UNSUPPORTED, "the tensor-core decode does not serve r1=%d, d=%d", lay->r1, lay->d);
+    if (n < 0 || (n && (!decoders || !image || !scales))) return fail(TTKV_ERR_ARG, "null decoders/image/scales");
+    if (dec_stride < int64_t(lay->r1) * lay->H * kHeadDim) return fail(TTKV_ERR_ARG, "decoder stride");
+    if ((reinterpret_cast<uintptr_t>(image) & 15) || (image_stride & 15) || image_stride < int64_t(per))
+        return fail(TTKV_ERR_ALIGN, "image must be 16-byte aligned with a stride of at least %zu bytes", per);
+    if (n == 0) return TTKV_OK;
+    const int kp16 = (lay->r1 + 15) / 16 * 16;
+    tc::decoder_image_kernel<<<dim3(n, lay->H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        decoders, dec_stride, lay->r1, lay->H, kp16, (kp16 + 63) / 64, static_cast<unsigned char*>(image),
+        image_stride, scales);
+    return check_launch("decoder_image_kernel");
 }
 
 extern "C" int ttkv_prefill_cont_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,

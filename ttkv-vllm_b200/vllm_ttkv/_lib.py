@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import pathlib
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_PATH = pathlib.Path(__file__).resolve().parents[1] / "libttkv_sm100.so"
 
 # host-side refusal codes (ttkv_b200.h)
@@ -40,7 +40,8 @@ class Cache(C.Structure):
 class Batch(C.Structure):
     _fields_ = [("block_table", C.c_void_p), ("bt_stride", C.c_int64), ("bt_cols", C.c_int32),
                 ("seq_lens", C.c_void_p), ("n_reqs", C.c_int32), ("decoders", C.c_void_p),
-                ("dec_stride", C.c_int64), ("dec_index", C.c_void_p), ("n_decoders", C.c_int32)]
+                ("dec_stride", C.c_int64), ("dec_index", C.c_void_p), ("n_decoders", C.c_int32),
+                ("dec_image", C.c_void_p), ("image_stride", C.c_int64), ("dec_scales", C.c_void_p)]
 
 
 class Rope(C.Structure):
@@ -56,6 +57,8 @@ SIGNATURES = {
     "ttkv_last_error": (C.c_char_p, []),
     "ttkv_abi_version": (I32, []),
     "ttkv_decode_workspace_bytes": (SZ, [LP, I32, I32, I32, I32, I32]),
+    "ttkv_decoder_image_bytes": (SZ, [LP]),
+    "ttkv_decoder_image": (C.c_int, [LP, P, I64, I32, P, I64, P, P]),
     "ttkv_decode_paged": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P, I32, I64,
                                     I32, P, SZ, P, P]),
     "ttkv_decode_paged_noalloc": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P,

@@ -263,7 +263,7 @@ class TTKVAttentionImpl(_ImplBase):
         pool = pool_for_layer(name, lay, query.device)
         ops.decode_paged(lay, cache, plan.block_size, md.block_table[:n], md.seq_lens[:n],
                          pool.decoders, plan.dec_rows(query.device), self._device_table(table, query),
-                         query[:n], self.scale, output[:n], max(plan.seq_lens[:n]))
+                         query[:n], self.scale, output[:n], max(plan.seq_lens[:n]), images=pool.images)
 
     def _prefill(self, name, lay, cache, plan, md, table, query, key, value, output):
         cont = []

@@ -115,7 +115,32 @@ def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int) -> _lib.C
     return _lib.Cache(flat.data_ptr(), flat.shape[0], flat.stride(0), block_size)
 
 
-def _batch_struct(block_table, seq_lens, decoders, dec_index) -> _lib.Batch:
+def decoder_image(lay: TTKLayout, decoders: torch.Tensor, out=None):
+    """The decode's operand images of decoders [n, r1, H*d] fp32: (image [n, bytes] uint8,
+    scales [n, H] fp32), or None when the tensor-core decode does not serve the layout.
+    `out` (image, scales) are written in place when given."""
+    _need_cuda(decoders)
+    if decoders.dtype != torch.float32 or decoders.dim() != 3 or not decoders.is_contiguous():
+        raise TypeError("decoders must be a contiguous float32 [n, r1, H*d] pool")
+    L = _lib.lib()
+    la = lay.abi()
+    per = L.ttkv_decoder_image_bytes(C.byref(la))
+    if per == 0:
+        return None
+    n = decoders.shape[0]
+    if out is None:
+        image = torch.zeros(n, per, dtype=torch.uint8, device=decoders.device)
+        scales = torch.zeros(n, lay.H, dtype=torch.float32, device=decoders.device)
+    else:
+        image, scales = out
+        if image.dtype != torch.uint8 or image.shape[0] < n or image.stride(0) < per or scales.shape[0] < n:
+            raise ValueError("image / scales too small for the decoders")
+    _lib.check(L.ttkv_decoder_image(C.byref(la), decoders.data_ptr(), decoders.stride(0), n,
+                                    image.data_ptr(), image.stride(0), scales.data_ptr(), _stream()))
+    return image, scales
+
+
+def _batch_struct(block_table, seq_lens, decoders, dec_index, images=None) -> _lib.Batch:
     for name, t, dt in (("block_table", block_table, torch.int32), ("seq_lens", seq_lens, torch.int32),
                         ("dec_index", dec_index, torch.int32), ("decoders", decoders, torch.float32)):
         if t.dtype != dt:
@@ -127,9 +152,15 @@ def _batch_struct(block_table, seq_lens, decoders, dec_index) -> _lib.Batch:
     n = block_table.shape[0]
     if seq_lens.numel() < n or dec_index.numel() < n:
         raise ValueError("seq_lens / dec_index shorter than the block table")
+    img, istride, scl = None, 0, None
+    if images is not None:
+        image, scales = images
+        if image.shape[0] < decoders.shape[0] or scales.shape[0] < decoders.shape[0]:
+            raise ValueError("one decoder image and scale row per pool row")
+        img, istride, scl = image.data_ptr(), image.stride(0), scales.data_ptr()
     return _lib.Batch(block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
                       seq_lens.data_ptr(), n, decoders.data_ptr(), decoders.stride(0),
-                      dec_index.data_ptr(), decoders.shape[0])
+                      dec_index.data_ptr(), decoders.shape[0], img, istride, scl)
 
 
 def _rope_struct(table: torch.Tensor) -> _lib.Rope:
@@ -143,9 +174,10 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
                  seq_lens: torch.Tensor, decoders: torch.Tensor, dec_index: torch.Tensor,
                  table: torch.Tensor, q: torch.Tensor, scale: float, out: torch.Tensor,
                  max_seq_len: int, head_lo: int = 0, head_hi: int | None = None,
-                 status: torch.Tensor | None = None) -> torch.Tensor:
+                 status: torch.Tensor | None = None, images=None) -> torch.Tensor:
     """Batched decode read: q [B, HQ, d] (row r = request r) -> out [B, HQ, d] (heads of the KV
-    heads [head_lo, head_hi) written). `cache` is the [n_slots, row_bytes] uint8 view."""
+    heads [head_lo, head_hi) written). `cache` is the [n_slots, row_bytes] uint8 view. `images`:
+    the pool's (image, scales) from `decoder_image`, staged instead of converting the decoders."""
     _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q, out)
     head_hi = lay.H if head_hi is None else head_hi
     B, HQ, d = q.shape
@@ -158,7 +190,7 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
     ws = workspace(ws_n, q.device)
     st = status if status is not None else status_word(q.device)
     c_s = _cache_struct(lay, cache, block_size)
-    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index)
+    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index, images)
     r_s = _rope_struct(table)
     _lib.check(L.ttkv_decode_paged(
         C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),

@@ -21,6 +21,7 @@ import re
 
 import torch
 
+from vllm_ttkv import ops
 from vllm_ttkv.layout import TTKLayout, config, layout_for_config
 
 CONFIG_ENV = "VLLM_TTKV_CONFIG"
@@ -102,12 +103,15 @@ def request_slot(key: int, create: bool = False) -> int | None:
 
 
 class DecoderPool:
-    """One layer's device decoders `[cap, r1, H*d]` fp32 and transposed pseudo-inverses."""
+    """One layer's device decoders `[cap, r1, H*d]` fp32, their transposed pseudo-inverses, and
+    the decode's operand images of them (`ops.decoder_image`, made once per decoder)."""
 
     def __init__(self, lay: TTKLayout, device, capacity: int = 16):
         self.lay, self.device = lay, torch.device(device)
         self.decoders = torch.zeros(capacity, lay.r1, lay.H * lay.d, device=self.device)
         self.pinvT = torch.zeros_like(self.decoders)
+        # None: a host pool, or a layout the tensor-core decode does not serve
+        self.images = ops.decoder_image(lay, self.decoders) if self.device.type == "cuda" else None
 
     @property
     def capacity(self) -> int:
@@ -122,12 +126,18 @@ class DecoderPool:
         dec[:self.capacity] = self.decoders
         pin[:self.capacity] = self.pinvT
         self.decoders, self.pinvT = dec, pin
+        if self.images is not None:
+            self.images = ops.decoder_image(self.lay, self.decoders)
 
     def put(self, slot: int, kdec) -> None:
         if slot >= self.capacity:
             self._grow(slot)
         self.decoders[slot] = kdec.decoder_f
         self.pinvT[slot] = kdec.pinvT
+        if self.images is not None:
+            image, scales = self.images
+            ops.decoder_image(self.lay, self.decoders[slot:slot + 1],
+                              out=(image[slot:slot + 1], scales[slot:slot + 1]))
 
 
 def pool_for_layer(layer_name: str, lay: TTKLayout, device) -> DecoderPool:
