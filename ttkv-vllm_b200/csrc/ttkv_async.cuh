@@ -81,6 +81,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may
+// start while the kernel before it runs: pdl_wait() blocks until that kernel has completed and
+// its memory is visible (it returns at once when there is no such dependency); pdl_trigger()
+// lets the next kernel of the stream launch before this one ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // A 2-D TMA map: `rows` rows of `d0` elements of `dt`, `stride` bytes apart; boxes of b0 x b1
 // elements, swizzled by `box_bytes` (the box's inner width when it is 32, 64 or 128 bytes; any
 // other value: no swizzle). False if the driver's encoder is unavailable or refuses the tensor.

@@ -364,6 +364,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const int wg = tid >> 7, t = tid & 127;
     const int nh = P.n_heads;
+    // launched while the kernel before it may still run: everything this kernel reads (seq_lens,
+    // the block table, q, the decoders, the cache) may come from that kernel
+    pdl_wait();
 
     // ---- the schedule. Units are (request, KV head, 128-token tile) in request-major order;
     // T = n_heads * sum over requests of their tiles, from the device's seq_lens. CTA c takes the
@@ -409,6 +412,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         }
     }
     __syncthreads();
+    pdl_trigger();                                             // the merge may launch
     if (lo >= hi) return;                                      // uniform: nothing for this CTA
     r = M->sched_r;
     before = M->sched_before;
@@ -1108,6 +1112,7 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     __shared__ long long red[2][4];
     const int g = blockIdx.x, hl = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
     const int nh = P.n_heads;
+    pdl_wait();                                                // the decode's partials are written
     long long before = 0, all = 0;
     for (int i = lane; i < P.n_reqs; i += 128) {
         const int v = req_tiles(P.seq_lens[i]);

@@ -594,11 +594,27 @@ int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps
                 cudaStream_t st) {
     auto k = tc::decode_tc_kernel<G>;
     if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "decode_tc_kernel")) return e;
-    k<<<P.n_ctas, tc::NTHR, T.smem, st>>>(P, T, maps);
-    if (int e = check_launch("decode_tc_kernel")) return e;
-    dim3 mg(P.G, P.n_heads, n_reqs);
-    tc::merge_sk_kernel<<<mg, 128, 0, st>>>(P);
-    return check_launch("merge_sk_kernel");
+    // both launches may start while the kernel before them runs (programmatic dependent launch):
+    // the decode waits for the step's write before its first cache read, the merge for the decode
+    // before its first partial
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(P.n_ctas);
+    cfg.blockDim = dim3(tc::NTHR);
+    cfg.dynamicSmemBytes = T.smem;
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, P, T, maps);
+    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "decode_tc_kernel: %s", cudaGetErrorString(e));
+    cfg.gridDim = dim3(P.G, P.n_heads, n_reqs);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    e = cudaLaunchKernelEx(&cfg, tc::merge_sk_kernel, P);
+    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "merge_sk_kernel: %s", cudaGetErrorString(e));
+    return TTKV_OK;
 }
 
 int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,

@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
 
     const int h = blockIdx.x, t = blockIdx.y;
     const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
+    pdl_trigger();                                           // the read of the step may launch
     const int64_t slot = P.slots[t];
     if (slot < 0 || slot >= P.n_slots) {
         if (tid == 0 && h == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
