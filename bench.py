@@ -214,16 +214,21 @@ class Workload:
 
 
 # ---------------------------------------------------------------------------- plugin e2e
-def plugin_e2e(wl, steps, warmup, device):
+def plugin_e2e(wl, steps, warmup, device, graph=False):
     """The step through the reference-facing plugin, `TTKVAttentionImpl.forward`, once per layer:
     the raw key handed over by the rotary capture's stash, q/k/v copied in from pinned host memory
-    and every layer's output copied back, one new metadata object (and step plan) per step.
+    and every layer's output copied back.
+
+    eager: one new metadata object (and host-read step plan) per step, forward per layer.
+    graph: the 28 forward calls captured once in one CUDA graph (the device-planned decode step:
+    pool rows looked up on the device, no readback) and replayed per step, as an engine that
+    captures decode steps does; the copies in and out stay outside the graph, every step.
     Returns (ms per step, h2d bytes, d2h bytes)."""
     from types import SimpleNamespace
 
     import torch
 
-    from vllm_ttkv import encode, metadata, patch, rope_store
+    from vllm_ttkv import encode, metadata, ops, patch, rope_store
     from vllm_ttkv.impl import TTKVAttentionImpl
     impl = TTKVAttentionImpl(wl.HQ, 128, wl.scale, wl.H)
     keys = [int(x) for x in wl.block_table[:, 0].tolist()]
@@ -247,18 +252,50 @@ def plugin_e2e(wl, steps, warmup, device):
     qsl_cpu = torch.arange(wl.B + 1, dtype=torch.int32)
     qsl = qsl_cpu.to(device)
 
-    def step():
-        md = metadata.TTKVAttentionMetadata(
+    def new_md():
+        return metadata.TTKVAttentionMetadata(
             seq_lens=wl.seq_lens, slot_mapping=wl.new_slots, block_table=wl.block_table,
             query_start_loc=qsl, query_start_loc_cpu=qsl_cpu, num_actual_tokens=wl.B,
             max_query_len=1, max_seq_len=wl.max_seq, ttkv_serial=metadata.next_serial())
-        for l, (layer, page) in enumerate(layers):
-            wl.q[l].copy_(pin_q[l], non_blocking=True)
-            wl.k_new[l].copy_(pin_k[l], non_blocking=True)
-            wl.v_new[l].copy_(pin_v[l], non_blocking=True)
-            patch.stash_raw_k(layer.layer_name, wl.k_new[l], None, wl.table)
-            impl.forward(layer, wl.q[l], None, wl.v_new[l], page, md, wl.out[l])
-            pin_o[l].copy_(wl.out[l], non_blocking=True)
+
+    def forward(l, md):
+        layer, page = layers[l]
+        patch.stash_raw_k(layer.layer_name, wl.k_new[l], None, wl.table)
+        impl.forward(layer, wl.q[l], None, wl.v_new[l], page, md, wl.out[l])
+
+    def copy_in(l):
+        wl.q[l].copy_(pin_q[l], non_blocking=True)
+        wl.k_new[l].copy_(pin_k[l], non_blocking=True)
+        wl.v_new[l].copy_(pin_v[l], non_blocking=True)
+
+    if graph:
+        md = new_md()
+        ops.status_word(device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):              # eager warm-up: workspaces, key map, pools
+            for l in range(wl.L):
+                forward(l, md)
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for l in range(wl.L):
+                forward(l, md)
+
+        def step():
+            for l in range(wl.L):
+                copy_in(l)
+            g.replay()
+            for l in range(wl.L):
+                pin_o[l].copy_(wl.out[l], non_blocking=True)
+    else:
+        def step():
+            md = new_md()
+            for l in range(wl.L):
+                copy_in(l)
+                forward(l, md)
+                pin_o[l].copy_(wl.out[l], non_blocking=True)
 
     for _ in range(warmup):
         step()
@@ -269,6 +306,9 @@ def plugin_e2e(wl, steps, warmup, device):
         step()
     e1.record()
     torch.cuda.synchronize(device)
+    ops.check_status(device)
+    if graph:
+        del g
     rope_store.clear_decoders()
     rope_store.clear_stores()
     return e0.elapsed_time(e1) / steps, h2d, d2h
@@ -658,6 +698,11 @@ def main():
         plugin = {"value": args.batch / (p_ms * 1e-3), "unit": "tok/s", "ms_per_step": p_ms,
                   "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
                   "api": "TTKVAttentionImpl.forward per layer (write + decode), new metadata per step"}
+        g_ms, _, _ = plugin_e2e(wl, args.steps, args.warmup, device, graph=True)
+        plugin["graph"] = {"value": args.batch / (g_ms * 1e-3), "unit": "tok/s", "ms_per_step": g_ms,
+                           "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
+                           "api": "TTKVAttentionImpl.forward x 28 captured once in a CUDA graph "
+                                  "(device-planned decode step), replayed per step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

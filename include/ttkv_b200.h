@@ -49,6 +49,7 @@ extern "C" {
 #define TTKV_STATUS_SLOT_RANGE 4   /* a slot id < 0 (PAD_SLOT_ID) or >= n_slots on a write */
 #define TTKV_STATUS_QUERY 5        /* q_len > seq_len, or a query range outside the batch */
 #define TTKV_STATUS_TIMEOUT 6      /* a bounded wait on the tensor-core pipeline ran out */
+#define TTKV_STATUS_SEQ_BOUND 7    /* a seq_len above the call's max_seq_len (the read's bound) */
 
 /* element types */
 #define TTKV_F32 0
@@ -146,6 +147,11 @@ typedef struct ttkv_rope {
  *   out:  request r's output at out + r*out_stride elements, [HQ, d]; only query heads of the
  *         KV heads [head_lo, head_hi) are written (G = HQ/H per KV head).
  *   scale: softmax scale (the model's, e.g. d^-0.5).
+ *   max_seq_len: an upper bound of the batch's seq_lens, read only on the host (it sizes the
+ *         workspace and is checked against the RoPE table). The launch reads nothing from the
+ *         host that varies with the batch, and its grid does not depend on seq_lens, so a stream
+ *         capture made with a bound replays any batch of the same request count within it. A
+ *         request longer than the bound is refused on the device (TTKV_STATUS_SEQ_BOUND).
  */
 size_t ttkv_decode_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
                                    int32_t max_seq_len, int32_t head_lo, int32_t head_hi);

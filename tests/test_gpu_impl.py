@@ -192,3 +192,99 @@ def test_decode_refuses_a_request_with_no_fitted_decoder():
     impl = TTKVAttentionImpl(HQ, D, SCALE, H)
     with pytest.raises(RuntimeError, match="no fitted decoder|first chunk"):
         _forward(impl, w, md, raw_k, value, q)
+
+
+# ---------------------------------------------------------------- the device-planned decode step
+def test_device_planned_decode_step_matches_the_host_planned_one(monkeypatch):
+    from vllm_ttkv import impl as impl_mod
+    w = _world(37, [70, 33, 129, 17])
+    md, raw_k, value, q = _step(w, [1, 1, 1, 1])
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+    before = w["page"].clone()
+    out_host = _forward(impl, w, md, raw_k, value, q)
+    page_host = w["page"].clone()
+    w["page"].copy_(before)
+    monkeypatch.setattr(impl_mod, "_DEVICE_PLAN", True)
+    md2, _, _, _ = _step(w, [1, 1, 1, 1])
+    out_dev = _forward(impl, w, md2, raw_k, value, q)
+    assert isinstance(getattr(md2, impl_mod._PLAN_ATTR), impl_mod.DevicePlan)
+    assert torch.equal(w["page"], page_host)                   # the same bytes written
+    # the read's bound differs (the table's rows), so the shares may split differently
+    assert (out_dev.float() - out_host.float()).abs().max().item() < 1e-3
+    _close(out_dev, stores.expected_decode(_after(w), q=q.float().cpu().numpy()))
+
+
+def test_a_captured_decode_step_replays_for_the_next_steps(monkeypatch):
+    """The forward captured once in a CUDA graph (device plan, no readback) and replayed for two
+    steps whose lengths, slots and tokens differ from the captured one's."""
+    from vllm_ttkv import impl as impl_mod
+    from vllm_ttkv import ops
+    monkeypatch.setattr(impl_mod, "_DEVICE_PLAN", True)
+    w = _world(38, [70, 33, 129, 17])
+    st0, name = w["st"], w["layer"].layer_name
+    steps = []
+    for back, seed in ((2, 0), (1, 1), (0, 2)):                 # seq_lens - 2, - 1, seq_lens
+        ws = dict(w, st=dict(st0, seq_lens=st0["seq_lens"] - back))
+        steps.append((ws, _step(ws, [1, 1, 1, 1], seed=seed)))
+    md0, k0, v0, q0 = steps[0][1]
+    buf = dict(seq=md0.seq_lens.clone(), slots=md0.slot_mapping.clone(), k=k0.clone(),
+               v=v0.clone(), q=q0.clone())
+    md = metadata.TTKVAttentionMetadata(
+        seq_lens=buf["seq"], slot_mapping=buf["slots"], block_table=md0.block_table.clone(),
+        query_start_loc=md0.query_start_loc, query_start_loc_cpu=md0.query_start_loc_cpu,
+        num_actual_tokens=4, ttkv_serial=metadata.next_serial())
+    out = torch.zeros(4, HQ, D, dtype=torch.float16, device="cuda")
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+
+    def fwd():
+        patch.stash_raw_k(name, buf["k"], None, w["table"])
+        impl.forward(w["layer"], buf["q"], None, buf["v"], w["page"], md, out)
+
+    ops.reset_status()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):                              # eager warm-up of the same path
+        fwd()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fwd()
+    for ws, (mds, ks, vs, qs) in steps[1:]:
+        buf["seq"].copy_(mds.seq_lens)
+        buf["slots"].copy_(mds.slot_mapping)
+        buf["k"].copy_(ks)
+        buf["v"].copy_(vs)
+        buf["q"].copy_(qs)
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        _close(out, stores.expected_decode(_after(ws), q=qs.float().cpu().numpy()))
+    ops.check_status()
+    del graph
+
+
+def test_device_plan_refuses_a_request_without_a_decoder_on_the_device(monkeypatch):
+    from vllm_ttkv import impl as impl_mod
+    from vllm_ttkv import ops
+    monkeypatch.setattr(impl_mod, "_DEVICE_PLAN", True)
+    w = _world(39, [30, 12], fresh=(1,))
+    md, raw_k, value, q = _step(w, [1, 1])
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+    ops.reset_status()
+    out = _forward(impl, w, md, raw_k, value, q)
+    with pytest.raises(RuntimeError, match="decoder"):
+        ops.check_status()
+    st = _after(w)
+    sub = dict(st, block_table=st["block_table"][:1], seq_lens=st["seq_lens"][:1],
+               decoders=st["decoders"][:1])
+    _close(out[:1], stores.expected_decode(sub, q=q[:1].float().cpu().numpy()))
+
+
+def test_a_pinned_pool_refuses_to_grow():
+    from vllm_ttkv import ops
+    w = _world(40, [20])
+    pool = rope_store.pool_for_layer(w["layer"].layer_name, w["lay"], "cuda")
+    pool.pin()
+    with pytest.raises(RuntimeError, match="reserve_rows"):
+        pool._grow(pool.capacity + 1)
+    ops._PINNED.pop(pool.decoders.data_ptr())

@@ -119,9 +119,9 @@ def test_decode_schedule_over_more_requests_than_one_scan_chunk():
     assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
 
 
-def test_decode_block_size_one_grows_the_grid_in_waves():
+def test_decode_block_size_one_cuts_shares_into_virtual_shares():
     """With one token per block a CTA's cached block-table slice covers only 3 tiles, so 4 x 2100
-    tokens x 8 heads (544 tiles) need more CTAs than SMs."""
+    tokens x 8 heads (544 tiles) cut each CTA's share in two."""
     st = stores.make_store(9, [2100, 2100, 1900, 2050], cfg="safe", r1=32, block_size=1)
     assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
 
@@ -219,3 +219,42 @@ def test_decoder_index_outside_pool_is_refused_on_device():
                      0.1, out, 20)
     with pytest.raises(RuntimeError, match="decoder"):
         ops.check_status()
+
+
+def test_decode_refuses_a_request_longer_than_the_bound_on_device():
+    from vllm_ttkv import ops
+    st = stores.make_store(13, [300, 40], cfg="safe", r1=32)
+    d = _dev(st)
+    out = torch.zeros(2, 24, 128, device="cuda")
+    ops.reset_status()
+    ops.decode_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"], d["idx"],
+                     d["table"], d["q"], 128 ** -0.5, out, 100)
+    with pytest.raises(RuntimeError, match="bound"):
+        ops.check_status()
+    want = stores.expected_decode(st)
+    assert np.abs(out[1].cpu().numpy() - want[1]).max() < 1e-4            # within the bound: read
+
+
+def test_decode_bound_far_above_the_batch_gives_the_same_result():
+    """A graph captured with a large bound (the RoPE table's rows) replays shorter batches: the
+    grid is one CTA per SM either way and only the workspace grows."""
+    st = stores.make_store(14, [300, 77, 129], cfg="safe", r1=32)
+    from vllm_ttkv import ops
+    d = _dev(st)
+    outs = []
+    for bound in (300, int(st["table"].shape[0])):
+        out = torch.zeros(3, 24, 128, device="cuda")
+        ops.reset_status()
+        ops.decode_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"],
+                         d["idx"], d["table"], d["q"], 128 ** -0.5, out, bound)
+        ops.check_status()
+        outs.append(out.cpu().numpy())
+    assert np.abs(outs[0] - outs[1]).max() < 1e-5
+    assert np.abs(outs[1] - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_decode_three_virtual_shares_per_cta():
+    """One token per block: a segment may span 3 tiles, so 7 x 2100 tokens x 8 heads (952 tiles)
+    cut each CTA's share into 3 virtual shares."""
+    st = stores.make_store(15, [2100] * 7, cfg="safe", r1=24, block_size=1)
+    assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4

@@ -5,7 +5,8 @@ import torch
 from torch import nn
 
 from vllm_ttkv import metadata, patch
-from vllm_ttkv.impl import StepPlan, TTKVAttentionImpl, plan_for, validate_slot_ids
+from vllm_ttkv.impl import (DevicePlan, StepPlan, TTKVAttentionImpl, decode_only, plan_for,
+                            validate_slot_ids)
 from vllm_ttkv.layout import TTKLayout
 
 
@@ -82,6 +83,50 @@ def test_plan_is_reused_within_a_step_and_rebuilt_for_the_next():
     assert plan_for(md, 16, 1024) is not p1
     md.ttkv_serial = 0                                     # not built here: never cached
     assert plan_for(md, 16, 1024) is not plan_for(md, 16, 1024)
+
+
+def test_decode_only_reads_the_host_copy_of_the_query_starts():
+    assert decode_only(_md([1, 1, 1], [3, 4, 5])) == 3
+    assert decode_only(_md([1, 2], [3, 4])) == 0
+    assert decode_only(_md([0, 2], [3, 4])) == 0                  # the same total, not all ones
+    md = _md([1, 1], [3, 4])
+    md.query_start_loc_cpu = None
+    assert decode_only(md) == 0
+
+
+def test_a_device_plan_reads_nothing_back_and_defers_the_refusals():
+    # a PAD_SLOT_ID slot is refused by the host plan before any launch ...
+    md = _md([1, 1], [3, 3], slots=[5, -1], serial=metadata.next_serial())
+    with pytest.raises(RuntimeError, match="PAD_SLOT_ID"):
+        plan_for(md, 16, 1024)
+    # ... and left to the kernels' status word by the device plan
+    p = plan_for(md, 16, 1024, device_plan=True)
+    assert isinstance(p, DevicePlan) and p.n == 2
+    assert plan_for(md, 16, 1024, device_plan=True) is p
+    assert plan_for(md, 16, 1024, device_plan=True, capturing=True) is not p   # captured anew
+    # a step with a prefill keeps the host plan
+    assert isinstance(plan_for(_md([1, 3], [3, 9]), 16, 1024, device_plan=True), StepPlan)
+
+
+def test_the_device_key_map_follows_the_registry():
+    from vllm_ttkv import ops, rope_store
+    rope_store.clear_decoders()
+    try:
+        rope_store._REQ_SLOT.update({7: 0, 40: 3})
+        lut = rope_store.key_rows("cpu", 64)
+        assert lut.numel() >= 64 and int(lut[7]) == 0 and int(lut[40]) == 3 and int(lut[8]) == -1
+        rope_store._set_key_row(1500, 5)                         # past the map: it grows
+        rows = rope_store.rows_for_keys(torch.tensor([40, 7, 1500, 9, -1, 10 ** 7], dtype=torch.int32))
+        assert rows.tolist() == [3, 0, 5, -1, -1, -1] and rows.dtype == torch.int32
+        lut = rope_store.key_rows("cpu")
+        ops.pin(lut)
+        with pytest.raises(RuntimeError, match="reserve_keys"):
+            rope_store.key_rows("cpu", lut.numel() + 1)
+        rope_store.clear_decoders()                              # a pinned map is emptied, kept
+        assert rope_store.key_rows("cpu") is lut and int(lut[40]) == -1
+    finally:
+        ops._PINNED.clear()
+        rope_store.clear_decoders()
 
 
 def test_metadata_build_copies_the_step_and_stamps_a_new_serial():

@@ -2,11 +2,13 @@
 //
 // Included by ttkv_read.cu inside its anonymous namespace (shares ReadParams and the merge).
 //
-// The launch is one CTA per SM (more only when a block-table slice would overflow), four warpgroups
-// (512 threads) each. The work is the list of (request, KV head, 128-token tile) units, request-
-// major; CTA c takes the c-th equal share of it, computed on the device from seq_lens, and walks
-// it as segments, one per (request, KV head) it touches, each leaving a partial (o, max, sum) that
-// merge_sk_kernel combines. Within a segment, token t of the current tile is TMEM lane t;
+// The launch is one CTA per SM, four warpgroups (512 threads) each, whatever the batch's lengths.
+// The work is the list of (request, KV head, 128-token tile) units, request-major; CTA c takes the
+// c-th equal share of it, computed on the device from seq_lens, and walks it as segments, one per
+// (request, KV head) it touches, each leaving a partial (o, max, sum) that merge_sk_kernel
+// combines. A segment's tokens must fit the block-table slice a CTA caches (BT_CAP blocks), so when
+// the shares would be longer than that the device cuts every share into k equal virtual shares
+// (k from the batch's total), and a segment also ends at a virtual boundary. Within a segment, token t of the current tile is TMEM lane t;
 // warpgroup c handles a quarter of that token's 128 head lanes (the RoPE pairs j, j+64 for j in
 // [16c, 16c+16) of K, the V lanes [32c, 32c+32)). Per tile:
 //
@@ -274,6 +276,8 @@ struct TcMisc {
     int scan[NTHR / 32];
     int sched_r;
     long long sched_before;
+    long long sched_T, sched_nv, sched_hi;   // the batch's units, virtual shares, this CTA's end
+    long long seg_slot;                      // the current segment's partial slot
     uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2], mb_dec;
     uint32_t tmem_base;
 };
@@ -317,6 +321,20 @@ __device__ __forceinline__ void tmem_wait_st() {
 
 // Tiles of a request (a request with no rows has none).
 __device__ __forceinline__ int req_tiles(int seq) { return seq > 0 ? (seq + TM - 1) / TM : 0; }
+
+// Tiles a segment may span so that its tokens stay within BT_CAP blocks of `block_size` (a run of
+// s tiles starting at a tile boundary touches at most s*TM/block_size + 1 blocks).
+__host__ __device__ __forceinline__ int64_t share_cap(int block_size) {
+    const int64_t c = int64_t(BT_CAP - 1) * block_size / TM;
+    return c > 0 ? c : 1;
+}
+
+// k: the virtual shares per CTA, the least that keeps every share of T units over n CTAs within
+// share_cap tiles (a share of T / (n k) units holds at most ceil of that).
+__host__ __device__ __forceinline__ int64_t virtual_shares(int64_t T, int64_t n, int block_size) {
+    const int64_t per = n * share_cap(block_size);
+    return T > per ? (T + per - 1) / per : 1;
+}
 
 // Exclusive prefix sum of v over the CTA's threads in thread order, and the CTA's total. Every
 // thread of the CTA calls it; `wsum` is NTHR / 32 ints of shared memory.
@@ -411,12 +429,27 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             acc += tot;                                        // uniform: the CTA's sum
         }
     }
+    // virtual shares: nv = gridDim.x * k equal shares of T, k the least that keeps a share within
+    // `cap` tiles; CTA c walks shares c*k .. c*k + k - 1 (its range [lo, hi) is their union). Kept
+    // in shared memory and read per segment, which saves their registers for the tile loop.
+    const int64_t nv = int64_t(gridDim.x) * virtual_shares(T_units, gridDim.x, P.block_size);
+    if (tid == 0) { M->sched_T = T_units; M->sched_nv = nv; M->sched_hi = hi; }
     __syncthreads();
     pdl_trigger();                                             // the merge may launch
+    if (nv + int64_t(P.n_reqs) * nh > P.n_part_slots) {       // uniform: seq_lens above the bound
+        if (blockIdx.x == 0 && tid == 0) report(P.status, TTKV_STATUS_SEQ_BOUND);
+        return;
+    }
     if (lo >= hi) return;                                      // uniform: nothing for this CTA
     r = M->sched_r;
     before = M->sched_before;
     int64_t unit = lo;
+    // the virtual share holding unit u: v = ceil((u + 1) nv / T) - 1; it ends at (v + 1) T / nv
+    auto share_of = [&](int64_t u, int64_t& v, int64_t& v_end) {
+        const int64_t Tn = M->sched_T, n = M->sched_nv;
+        v = ((u + 1) * n - 1) / Tn;
+        v_end = (v + 1) * Tn / n;
+    };
 
     auto empty_partial = [&](int64_t slot) {
         if (tid < G) {
@@ -544,26 +577,30 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     uint32_t ph_r = 0, ph_pv = 0, ph_dec = 0;
     bool r_pending_any = false, pv_pending_any = false, pend_dec = false;
 
-    while (unit < hi && !timed_out) {
+    while (unit < M->sched_hi && !timed_out) {
         // ---- the next segment: the run of this CTA's units that belongs to one (request, KV head)
         if (r >= P.n_reqs) break;                                   // unreachable: hi <= T
         const int seq = P.seq_lens[r];
         const int nt = req_tiles(seq);
         const int64_t rs = before * nh, re = rs + int64_t(nt) * nh;
         if (unit >= re) { before += nt; ++r; continue; }        // past this request (or it has no rows)
+        int64_t vs, vs_end;
+        share_of(unit, vs, vs_end);
         const int hl = int((unit - rs) / nt);
         const int64_t ps = rs + int64_t(hl) * nt;
-        const int64_t seg_hi = min(hi, ps + nt);
+        const int64_t seg_hi = min(vs_end, ps + nt);                // vs_end <= the CTA's end
         const int t_begin = int(unit - ps) * TM;
         const int t_end = min(seq, int(seg_hi - ps) * TM);
-        const int64_t slot = int64_t(blockIdx.x) + int64_t(r) * nh + hl;
+        const int64_t slot = vs + int64_t(r) * nh + hl;
+        if (tid == 0) M->seg_slot = slot;       // read again at the segment's end (registers)
         unit = seg_hi;
         const int h = P.head_lo + hl;
 
         // ---- the cheap refusals (uniform); the block ids are checked as the set-up loads them
         const int di = P.dec_index[r];
         bool bad = false;
-        if (di < 0 || di >= P.n_decoders) { if (tid == 0) report(P.status, TTKV_STATUS_DECODER); bad = true; }
+        if (seq > P.max_seq) { if (tid == 0) report(P.status, TTKV_STATUS_SEQ_BOUND); bad = true; }
+        if (!bad && (di < 0 || di >= P.n_decoders)) { if (tid == 0) report(P.status, TTKV_STATUS_DECODER); bad = true; }
         const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
         if (!bad && blocks_needed > P.bt_cols) { if (tid == 0) report(P.status, TTKV_STATUS_ROW_SHORT); bad = true; }
         const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
@@ -1055,36 +1092,41 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 }
             }
         }
+        // written before the set-up's barriers; read before this barrier, after which thread 0 may
+        // start the next segment
+        const int64_t slot_e = M->seg_slot;
         timed_out = __syncthreads_or(timed_out);
 
         r_pending_any = r_pending;
         pv_pending_any = pv_pending;
-        // ---- this segment's partials: slot = CTA index + pair index (one slot per (CTA, pair))
+        // ---- this segment's partials: slot = virtual share + pair index (one per (share, pair))
         if (wg < G) {
             #pragma unroll
             for (int i = 0; i < HPW; ++i) {
                 const int g = wg + NWG * i;
-                if (g < G) P.part_o[(slot * G + g) * 128 + t] = timed_out ? 0.f : o[i];
+                if (g < G) P.part_o[(slot_e * G + g) * 128 + t] = timed_out ? 0.f : o[i];
             }
         }
         if (tid < G) {
-            P.part_ml[(slot * G + tid) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
+            P.part_ml[(slot_e * G + tid) * 2 + 0] = timed_out ? -INFINITY : M->m[tid];
             const float l = M->red_sum[0][tid] + M->red_sum[1][tid] + M->red_sum[2][tid] + M->red_sum[3][tid];
-            P.part_ml[(slot * G + tid) * 2 + 1] = timed_out ? 0.f : l;
+            P.part_ml[(slot_e * G + tid) * 2 + 1] = timed_out ? 0.f : l;
         }
     }
 
     // ---- a timeout leaves the rest of the CTA's segments empty
     if (timed_out) {
-        while (unit < hi && r < P.n_reqs) {
+        while (unit < M->sched_hi && r < P.n_reqs) {
             const int seq = P.seq_lens[r];
             const int nt = req_tiles(seq);
             const int64_t rs = before * nh, re = rs + int64_t(nt) * nh;
             if (unit >= re) { before += nt; ++r; continue; }
+            int64_t vs, vs_end;
+            share_of(unit, vs, vs_end);
             const int hl = int((unit - rs) / nt);
             const int64_t ps = rs + int64_t(hl) * nt;
-            empty_partial(int64_t(blockIdx.x) + int64_t(r) * nh + hl);
-            unit = min(hi, ps + nt);
+            empty_partial(vs + int64_t(r) * nh + hl);
+            unit = min(vs_end, ps + nt);
         }
     }
 
@@ -1107,7 +1149,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
 }
 
 // Combine the segments of one (request, KV head, query head): thread = lane. The segments of
-// pair p are the CTAs whose unit ranges meet p's units [U, U + tiles), written at slots c + p.
+// pair p are the virtual shares whose unit ranges meet p's units [U, U + tiles), written at
+// slots c + p.
 __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     __shared__ long long red[2][4];
     const int g = blockIdx.x, hl = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
@@ -1130,8 +1173,10 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     all = red[1][0] + red[1][1] + red[1][2] + red[1][3];
     const int nt = req_tiles(P.seq_lens[r]);
     float v = 0.f;
-    if (nt > 0) {
-        const long long T = all * nh, n = P.n_ctas;
+    const long long n = (long long)P.n_ctas * virtual_shares(all * nh, P.n_ctas, P.block_size);
+    // seq_lens above the bound the workspace was sized for: the decode wrote nothing
+    if (nt > 0 && n + (long long)P.n_reqs * nh <= P.n_part_slots) {
+        const long long T = all * nh;
         const long long U = before * nh + (long long)hl * nt;
         const long long c0 = ((U + 1) * n - 1) / T, c1 = ((U + nt) * n - 1) / T;
         const long long p = (long long)r * nh + hl;

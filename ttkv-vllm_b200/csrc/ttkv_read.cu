@@ -65,6 +65,8 @@ struct ReadParams {
     int head_lo, n_heads;     // KV heads [head_lo, head_lo + n_heads)
     int qmax, n_qblk, n_splits, chunk;
     int n_reqs, n_ctas;       // tensor-core decode: requests, CTAs of the balanced schedule
+    int max_seq;              // the call's max_seq_len: a longer request is refused on the device
+    int64_t n_part_slots;     // tensor-core decode: partial slots the workspace holds
     float* part_o;            // [req][head][qmax*G][split][128]
     float* part_ml;           // [req][head][qmax*G][split][2]
     void* out;
@@ -201,6 +203,7 @@ __global__ void __launch_bounds__(NT) attn_split_kernel(const ReadParams P) {
     const int di = P.dec_index[r];
     bool bad = false;
     if (nq <= 0) bad = true;                              // an empty query block: nothing to do
+    if (!bad && seq > P.max_seq) { report(P.status, TTKV_STATUS_SEQ_BOUND); bad = true; }
     if (!bad && (MULTI && (qlen > seq || qlen < 0))) { report(P.status, TTKV_STATUS_QUERY); bad = true; }
     if (!bad && (di < 0 || di >= P.n_decoders)) { report(P.status, TTKV_STATUS_DECODER); bad = true; }
     const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
@@ -443,6 +446,7 @@ int qblock_for(int G, bool multi) {
 struct Plan {
     int qb, n_qblk, n_splits, chunk;
     size_t part_o_bytes, part_ml_bytes, smem;
+    long long n_part_slots;
 };
 
 Plan make_plan(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_q, int max_seq,
@@ -487,12 +491,13 @@ bool tc_serves(const ttkv_layout_t* lay, int HQ) {
            tc::tc_geom(lay, G).smem > 0;
 }
 
-// The tensor-core decode's grid: one resident CTA per SM, each taking an equal share of the
-// (request, KV head, tile) units. A CTA's run of tokens must fit the block-table slice it caches
-// (tc::BT_CAP blocks of `block_size` tokens), so when the batch's units (an upper bound from
-// max_seq) would give a CTA more tiles than that, the grid grows in whole waves. block_size 1 gives
-// the most CTAs, so a workspace sized for it covers every block size. Partials: one slot per
-// (CTA, pair) that can meet, CTA index + pair index, so n_ctas + pairs slots.
+// The tensor-core decode's grid: one resident CTA per SM (fewer only when the batch has fewer
+// units), each taking an equal share of the (request, KV head, tile) units; the grid does not
+// depend on max_seq beyond that, so a graph captured with a bound replays any batch within it. The
+// device cuts the shares into virtual shares when a segment would outgrow the cached block-table
+// slice. Partials: one slot per (virtual share, pair) that can meet, share index + pair index, so
+// the workspace holds (CTAs x the most virtual shares max_seq allows) + pairs slots. block_size 1
+// needs the most shares, so a workspace sized for it covers every block size.
 Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int n_heads, int block_size) {
     Plan pl{};
     const int G = HQ / lay->H;
@@ -501,15 +506,11 @@ Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int
     const long long tiles = std::max(1, (max_seq + tc::TM - 1) / tc::TM);
     const long long pairs = std::max(1LL, (long long)n_reqs * n_heads);
     const long long units = pairs * tiles;
-    const long long sms = sm_count();
-    const long long cap = std::max(1LL, (long long)(tc::BT_CAP - 1) * block_size / tc::TM);
-    long long n = sms;
-    if (units > cap * sms) n = (units + cap - 1) / cap;
-    n = (n + sms - 1) / sms * sms;
-    n = std::min(n, units);
+    const long long n = std::min<long long>(sm_count(), units);
     pl.n_splits = int(n);
     pl.chunk = 0;
-    const size_t slots = size_t(n + pairs);
+    const size_t slots = size_t(n * tc::virtual_shares(units, n, block_size) + pairs);
+    pl.n_part_slots = (long long)slots;
     pl.part_o_bytes = slots * G * 128 * sizeof(float);
     pl.part_ml_bytes = slots * G * 2 * sizeof(float);
     pl.smem = size_t(tc::tc_geom(lay, G).smem);
@@ -722,6 +723,7 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
     P.qmax = multi ? max_q_len : 1; P.n_qblk = pl.n_qblk; P.n_splits = pl.n_splits; P.chunk = pl.chunk;
     P.n_reqs = batch->n_reqs; P.n_ctas = use_tc ? pl.n_splits : 0;
+    P.max_seq = max_seq_len; P.n_part_slots = pl.n_part_slots;
     P.part_o = reinterpret_cast<float*>(workspace);
     P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
     P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;

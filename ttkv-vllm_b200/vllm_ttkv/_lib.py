@@ -19,7 +19,8 @@ ERR_ARG, ERR_LAYOUT, ERR_UNSUPPORTED, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA = -1, -
 STATUS = {0: "ok", 1: "block index outside the cache", 2: "block-table row too short for seq_len",
           3: "decoder index outside the pool", 4: "slot id is PAD_SLOT_ID or outside the cache",
           5: "query range inconsistent with seq_len",
-          6: "a bounded wait on the tensor-core pipeline ran out"}
+          6: "a bounded wait on the tensor-core pipeline ran out",
+          7: "a seq_len above the max_seq_len the read was given (its bound)"}
 
 F32, F16, BF16 = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024   # TTKV_NOALLOC_SCRATCH_BYTES

@@ -21,6 +21,15 @@ The step's layer-independent facts (batch split, request keys, bounds of the slo
 back once per step and cached on the metadata under its serial (impl.py:82-214). Device-side
 refusals (a block id outside the cache, a decoder row outside the pool) land in `ops.status_word`;
 with VLLM_TTKV_CHECK=1 every layer reads it back and raises.
+
+A pure-decode step (every query length 1, seen in the host copy of query_start_loc) can instead be
+planned on the device (`DevicePlan`): each request's pool row comes from the device key map, the
+read's bound is the RoPE table's length, and nothing is read back, so the forward can be captured
+in a CUDA graph and replayed for later steps of the same request count. That is the plan while a
+graph is being captured, and always with VLLM_TTKV_DEVICE_PLAN=1. The host-side refusals of the
+other plan (PAD_SLOT_ID or out-of-range slots, a request without a decoder) then become device
+refusals in the status word, read by `ops.check_status()`. The reference's backend cannot be
+captured at all (vllm_ttkv/metadata.py:95-101).
 """
 from __future__ import annotations
 
@@ -32,8 +41,9 @@ from vllm_ttkv import decode as dc
 from vllm_ttkv import encode, ops
 from vllm_ttkv.layout import TTKLayout
 from vllm_ttkv.patch import take_raw_k
-from vllm_ttkv.rope_store import (decoder_for_request, ensure_store, layout_for_layer,
-                                  pool_for_layer, register_decoder, request_key_host, request_slot)
+from vllm_ttkv.rope_store import (decoder_for_request, ensure_store, key_rows, layout_for_layer,
+                                  pool_for_layer, register_decoder, request_key_host, request_slot,
+                                  rows_for_keys)
 
 try:                                   # vLLM's base class when vLLM is installed
     from vllm.v1.attention.backend import AttentionImpl as _ImplBase
@@ -46,6 +56,7 @@ except Exception:                      # pragma: no cover
     _AttentionType = None
 
 _CHECK = os.environ.get("VLLM_TTKV_CHECK", "") not in ("", "0")
+_DEVICE_PLAN = os.environ.get("VLLM_TTKV_DEVICE_PLAN", "") not in ("", "0")
 _PLAN_ATTR = "_ttkv_plan"
 
 
@@ -136,13 +147,62 @@ class StepPlan:
         return self._dec_rows
 
 
-def plan_for(md, block_size: int, n_slots: int) -> StepPlan:
+def decode_only(md) -> int:
+    """The request count of a pure-decode step (every query length 1), from the HOST copy of
+    query_start_loc; 0 when the step is anything else or there is no host copy."""
+    qc = getattr(md, "query_start_loc_cpu", None)
+    if qc is None or qc.is_cuda or qc.dim() != 1 or qc.numel() < 2:
+        return 0
+    n = qc.numel() - 1
+    return n if torch.equal(qc, torch.arange(n + 1, dtype=qc.dtype)) else 0
+
+
+class DevicePlan:
+    """A pure-decode step planned without a readback: request r is token r, its pool row is
+    looked up on the device from its key (`block_table[r, 0]`), and the read is bounded by the
+    RoPE table rather than by the batch's longest request."""
+
+    __slots__ = ("serial", "n", "block_size", "n_slots", "captured", "_rows")
+
+    def __init__(self, md, n: int, block_size: int, n_slots: int, serial: int, captured: bool):
+        if md.seq_lens is None or md.block_table is None or md.slot_mapping is None:
+            raise RuntimeError(
+                "the attention metadata is missing seq_lens / block_table / slot_mapping, so the "
+                "batch cannot be addressed")
+        if md.seq_lens.shape[0] < n or md.block_table.shape[0] < n or md.slot_mapping.shape[0] < n:
+            raise RuntimeError(
+                f"a decode step of {n} requests needs {n} seq_lens, block-table rows and slots "
+                f"(got {md.seq_lens.shape[0]}, {md.block_table.shape[0]}, {md.slot_mapping.shape[0]})")
+        if md.block_table.shape[1] < 1:
+            raise ValueError("the block table has no columns, so no request has an identity to key "
+                             "a decoder by")
+        self.serial, self.n, self.block_size, self.n_slots = serial, n, block_size, n_slots
+        # made under a capture: its row lookup is a node of the graph, redone at every replay
+        self.captured = captured
+        self._rows = None
+
+    def rows(self, md, device) -> torch.Tensor:
+        """Pool row of each request (-1: no decoder, refused on the device), made once per step."""
+        if self._rows is None:
+            key_rows(device, self.n_slots // self.block_size)
+            self._rows = rows_for_keys(md.block_table[:self.n, 0])
+        return self._rows
+
+
+def plan_for(md, block_size: int, n_slots: int, device_plan: bool = False, capturing: bool = False):
+    """The step's plan, cached on the metadata under its serial. A device plan made outside a
+    capture is not reused inside one (its row lookup must be captured too), nor the other way."""
+    n_dec = decode_only(md) if device_plan else 0
     serial = int(getattr(md, "ttkv_serial", 0) or 0)
-    if not serial:
-        return StepPlan(md, block_size, n_slots, 0)
-    plan = getattr(md, _PLAN_ATTR, None)
-    if plan is None or plan.serial != serial:
-        plan = StepPlan(md, block_size, n_slots, serial)
+    plan = getattr(md, _PLAN_ATTR, None) if serial else None
+    if plan is not None and plan.serial == serial:
+        if isinstance(plan, DevicePlan) and n_dec and plan.captured == capturing:
+            return plan
+        if isinstance(plan, StepPlan) and not n_dec:
+            return plan
+    plan = (DevicePlan(md, n_dec, block_size, n_slots, serial, capturing) if n_dec
+            else StepPlan(md, block_size, n_slots, serial))
+    if serial:
         setattr(md, _PLAN_ATTR, plan)
     return plan
 
@@ -192,7 +252,17 @@ class TTKVAttentionImpl(_ImplBase):
         page = self._cache_tensor(kv_cache)
         block_size = self._block_size(page)
         cache = dc.byte_rows(page, lay.compressed_bytes_per_token())
-        plan = plan_for(attn_metadata, block_size, cache.shape[0])
+        capturing = ops.capturing()
+        if query.is_cuda and not capturing:          # any eager step readies a later capture
+            key_rows(query.device, cache.shape[0] // block_size)
+        plan = plan_for(attn_metadata, block_size, cache.shape[0], _DEVICE_PLAN or capturing, capturing)
+        if isinstance(plan, DevicePlan):
+            if plan.n > n_tokens:
+                raise RuntimeError(f"metadata describes {plan.n} query tokens but the query holds {n_tokens}")
+            self._decode_step(layer, lay, cache, plan, attn_metadata, query, value, output, capturing)
+            if _CHECK and not capturing:
+                ops.check_status(query.device)
+            return output
         N = plan.qsl[-1]
         actual = getattr(attn_metadata, "num_actual_tokens", None)
         if actual and int(actual) != N:
@@ -211,6 +281,37 @@ class TTKVAttentionImpl(_ImplBase):
         if _CHECK:
             ops.check_status(query.device)
         return output
+
+    # ------------------------------------------------------------------ a device-planned decode step
+    def _decode_step(self, layer, lay, cache, plan, md, query, value, output, capturing):
+        """Write token r of every request r and read every request, with no host readback: the
+        frozen write and the decode, each request's pool row from the device key map."""
+        name = getattr(layer, "layer_name", None)
+        stash = take_raw_k(name)
+        if value is None:
+            raise RuntimeError(f"layer {name!r} got no value tensor, so V cannot be stored")
+        if lay.H != self.num_kv_heads:
+            raise RuntimeError(
+                f"the layout was built for H={lay.H} KV heads but this layer has {self.num_kv_heads}")
+        n, dev = plan.n, query.device
+        K = encode.as_kv_heads(stash["raw_k"], self.num_kv_heads, self.head_size, "the captured raw key")[:n]
+        V = encode.as_kv_heads(value, self.num_kv_heads, self.head_size, "value")[:n]
+        table = self._device_table(self._cos_sin_cache(layer, stash), query)
+        ensure_store(name, table, self.num_heads, self.num_kv_heads, self.head_size, lay)
+        pool = pool_for_layer(name, lay, dev)
+        rows = plan.rows(md, dev)
+        if capturing:                       # the graph holds these addresses from now on
+            pool.pin()
+            ops.pin(key_rows(dev), rows)
+        encode.write_frozen(cache, md.slot_mapping[:n], K, V, rows, pool.decoders, pool.pinvT, lay)
+        # the read's bound: the RoPE table (any position the model can reach) under a capture, so
+        # the replays of other lengths stay within it; else the step's own max_seq_len
+        bound = int(table.shape[0])
+        if not capturing and 0 < int(getattr(md, "max_seq_len", 0) or 0) <= bound:
+            bound = int(md.max_seq_len)
+        ops.decode_paged(lay, cache, plan.block_size, md.block_table[:n], md.seq_lens[:n],
+                         pool.decoders, rows, table, query[:n], self.scale, output[:n], bound,
+                         images=pool.images)
 
     # ------------------------------------------------------------------ the write
     def _write(self, layer, name, lay, cache, value, plan, md, device):

@@ -17,6 +17,7 @@ from vllm_ttkv.layout import TTKLayout
 _DTYPE = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 
 _STATUS: dict = {}
+_PINNED: dict = {}                       # data_ptr -> tensor a captured graph reads
 _WORKSPACE: dict = {}
 
 
@@ -38,6 +39,22 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def capturing() -> bool:
+    """Whether the current stream is capturing a CUDA graph."""
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
+def pin(*tensors: torch.Tensor) -> None:
+    """Keep `tensors` alive for the rest of the process: a captured CUDA graph holds their raw
+    addresses (passed through the C ABI), which torch does not know about."""
+    for t in tensors:
+        _PINNED[t.data_ptr()] = t
+
+
+def is_pinned(t: torch.Tensor) -> bool:
+    return _PINNED.get(t.data_ptr()) is t
+
+
 def status_word(device=None) -> torch.Tensor:
     """The per-device int32 status the kernels report device-side refusals into."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -45,6 +62,9 @@ def status_word(device=None) -> torch.Tensor:
         dev = torch.device("cuda", torch.cuda.current_device())
     t = _STATUS.get(dev)
     if t is None:
+        if capturing():
+            raise RuntimeError("the status word must exist before a CUDA graph capture (its zero "
+                               "fill would rerun at every replay): run one eager step first")
         t = torch.zeros(1, dtype=torch.int32, device=dev)
         _STATUS[dev] = t
     return t
@@ -72,6 +92,8 @@ def workspace(nbytes: int, device, key="read") -> torch.Tensor:
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
         _WORKSPACE[(dev, key)] = buf
+    if capturing():                        # a graph keeps the scratch it launched with
+        pin(buf)
     return buf
 
 

@@ -6,6 +6,12 @@ Same surface as the reference's `vllm_ttkv/rope_store.py`:
   * the per-(layer, request) decoder registry keyed by the request's first block
     (register_decoder, decoder_for_request, release_decoder, clear_decoders).
 
+Graph capture. A decode step can be planned without reading anything back (`rows_for_keys` maps
+each request's key to its pool row on the device). A CUDA graph captured over it holds the raw
+addresses of the pools and of the key map, so those are `pin`ned by the capture: they stay alive
+for the process, and a pinned pool or key map refuses to grow (size them first with
+`reserve_rows` / `reserve_keys`).
+
 What changes is where decoders live. The reference keeps a host dict of fp32 tensors, one lookup
 per request per layer (rope_store.py:169-237), which a batched kernel cannot read. Here every
 registered decoder also occupies a row of a per-layer DEVICE pool (`DecoderPool`), and a request
@@ -35,6 +41,8 @@ _POOLS: dict[str, "DecoderPool"] = {}
 _REQ_SLOT: dict[int, int] = {}                         # request key -> pool row (all layers)
 _FREE_SLOTS: list[int] = []
 _NEXT_SLOT = [0]
+_KEY_ROWS: dict[torch.device, torch.Tensor] = {}       # device copy of _REQ_SLOT: key -> row, -1
+_RESERVE = [16]                                        # pool rows a new pool starts with
 
 
 def _layer_index(layer_name: str) -> int | None:
@@ -102,12 +110,75 @@ def request_slot(key: int, create: bool = False) -> int | None:
     return s
 
 
+# ------------------------------------------------------------------ the device key map
+def key_rows(device, n_keys: int = 0) -> torch.Tensor:
+    """The device's key -> pool row map (int32, -1 where a key has no row), holding at least
+    `n_keys` keys (a request's key is a block id, so the cache's block count covers every key)."""
+    dev = torch.device(device)
+    lut = _KEY_ROWS.get(dev)
+    if lut is None or lut.numel() < n_keys:
+        if ops.capturing():
+            # made inside a capture, its initialisation would be a node that every replay reruns
+            raise RuntimeError(
+                f"the decoder key map on {dev} must hold {n_keys} keys before a CUDA graph capture: "
+                f"run one eager step first or call rope_store.reserve_keys")
+        if lut is not None and ops.is_pinned(lut):
+            raise RuntimeError(
+                f"the decoder key map on {dev} holds {lut.numel()} keys and a captured CUDA graph "
+                f"reads it, so it cannot grow to {n_keys}; call rope_store.reserve_keys before the "
+                f"capture")
+        n = max(1024, n_keys, 0 if lut is None else lut.numel(), max(_REQ_SLOT, default=-1) + 1)
+        new = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        if lut is not None:
+            new[:lut.numel()] = lut
+        else:
+            for key, row in _REQ_SLOT.items():
+                if key < n:
+                    new[key] = row
+        lut = new
+        _KEY_ROWS[dev] = lut
+    return lut
+
+
+def reserve_keys(n_keys: int, device) -> torch.Tensor:
+    """Size the device key map for block ids below `n_keys` (before a graph capture)."""
+    return key_rows(device, n_keys)
+
+
+def rows_for_keys(keys: torch.Tensor) -> torch.Tensor:
+    """Pool rows (int32, -1 for a key without a decoder) of device request keys, on the device:
+    no readback, so a decode step planned with it can be captured in a CUDA graph. A key outside
+    the map reads -1 (the kernels then refuse the request on the device)."""
+    lut = key_rows(keys.device)
+    k = keys.to(torch.int64)
+    ok = (k >= 0) & (k < lut.numel())
+    rows = lut.index_select(0, k.clamp(0, lut.numel() - 1))
+    return torch.where(ok, rows, torch.full_like(rows, -1))
+
+
+def _set_key_row(key: int, row: int) -> None:
+    for dev, lut in _KEY_ROWS.items():
+        if key >= lut.numel():
+            lut = key_rows(dev, max(key + 1, 2 * lut.numel()))
+        lut[key] = row
+
+
+def reserve_rows(n_rows: int) -> None:
+    """Give every decoder pool (existing and later) at least `n_rows` rows, e.g. the engine's
+    maximum number of live requests, so that no pool has to grow after a graph capture."""
+    _RESERVE[0] = max(_RESERVE[0], int(n_rows))
+    for pool in _POOLS.values():
+        if pool.capacity < n_rows:
+            pool._grow(n_rows - 1)
+
+
 class DecoderPool:
     """One layer's device decoders `[cap, r1, H*d]` fp32, their transposed pseudo-inverses, and
     the decode's operand images of them (`ops.decoder_image`, made once per decoder)."""
 
-    def __init__(self, lay: TTKLayout, device, capacity: int = 16):
+    def __init__(self, lay: TTKLayout, device, capacity: int | None = None):
         self.lay, self.device = lay, torch.device(device)
+        capacity = _RESERVE[0] if capacity is None else capacity
         self.decoders = torch.zeros(capacity, lay.r1, lay.H * lay.d, device=self.device)
         self.pinvT = torch.zeros_like(self.decoders)
         # None: a host pool, or a layout the tensor-core decode does not serve
@@ -117,7 +188,15 @@ class DecoderPool:
     def capacity(self) -> int:
         return self.decoders.shape[0]
 
+    def pin(self) -> None:
+        """Keep this pool's tensors alive and fixed: a captured CUDA graph reads them."""
+        ops.pin(self.decoders, self.pinvT, *(self.images or ()))
+
     def _grow(self, need: int):
+        if ops.is_pinned(self.decoders):
+            raise RuntimeError(
+                f"the decoder pool holds {self.capacity} rows and a captured CUDA graph reads it, so "
+                f"it cannot grow to row {need}; call rope_store.reserve_rows before the capture")
         cap = self.capacity
         while cap <= need:
             cap *= 2
@@ -143,6 +222,11 @@ class DecoderPool:
 def pool_for_layer(layer_name: str, lay: TTKLayout, device) -> DecoderPool:
     pool = _POOLS.get(layer_name)
     if pool is None or pool.lay.r1 != lay.r1 or pool.device != torch.device(device):
+        if ops.capturing():
+            raise RuntimeError(
+                f"layer {layer_name!r} has no decoder pool and one cannot be made inside a CUDA "
+                f"graph capture (its zero fill would rerun at every replay): run one eager step "
+                f"first")
         pool = DecoderPool(lay, device)
         _POOLS[layer_name] = pool
     return pool
@@ -154,8 +238,12 @@ def register_decoder(layer_name: str, key: int, decoder, lay: TTKLayout | None =
     _DECODERS[(layer_name, key)] = decoder
     lay = lay if lay is not None else layout_for_layer(layer_name)
     if lay is not None and decoder.decoder_f.is_cuda:
+        fresh = key not in _REQ_SLOT
         slot = request_slot(key, create=True)
         pool_for_layer(layer_name, lay, decoder.decoder_f.device).put(slot, decoder)
+        if fresh:
+            key_rows(decoder.decoder_f.device, key + 1)
+            _set_key_row(key, slot)
 
 
 def decoder_for_request(layer_name: str | None, key: int):
@@ -172,6 +260,7 @@ def release_decoder(layer_name: str, key: int) -> None:
         s = _REQ_SLOT.pop(key, None)
         if s is not None:
             _FREE_SLOTS.append(s)
+            _set_key_row(key, -1)
 
 
 def release_request(key: int) -> None:
@@ -180,11 +269,18 @@ def release_request(key: int) -> None:
 
 
 def clear_decoders() -> None:
+    """Forget every decoder. A pinned key map is kept (emptied), so a graph that reads it sees no
+    request; a pinned pool stays alive but is no longer the layer's pool."""
     _DECODERS.clear()
     _POOLS.clear()
     _REQ_SLOT.clear()
     _FREE_SLOTS.clear()
     _NEXT_SLOT[0] = 0
+    for dev in list(_KEY_ROWS):
+        if ops.is_pinned(_KEY_ROWS[dev]):
+            _KEY_ROWS[dev].fill_(-1)
+        else:
+            del _KEY_ROWS[dev]
 
 
 def decoder_for_layer(layer_name: str | None):
