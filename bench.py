@@ -41,7 +41,7 @@ METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs pe
 # profiles/decode_tc_cfg1.md: layer 9 (r1 = 110) of this workload, 8 requests x 4323 rows.
 # The per-launch `traffic` of the roofline scales it by algorithmic bytes (the kernel reads each
 # slot byte once, so traffic grows in proportion to the rows and widths a launch reads).
-CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 36.4e6 + 0.004e6}
+CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 37.01e6 + 0.005e6}
 
 
 def _peaks():

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define TTKV_ABI_VERSION 2
+#define TTKV_ABI_VERSION 3
 
 /* host-side refusals (return values) */
 #define TTKV_OK 0
@@ -90,7 +90,14 @@ typedef struct ttkv_cache {
     int64_t n_slots;
     int64_t row_bytes;
     int32_t block_size;
+    int32_t flags;         /* TTKV_CACHE_*; 0 keeps the reference's refusals */
 } ttkv_cache_t;
+
+/* Writes skip a token whose slot id is negative (vLLM's PAD_SLOT_ID, which an engine gives the
+ * padding tokens of a batch padded to a captured CUDA graph's size) instead of refusing it with
+ * TTKV_STATUS_SLOT_RANGE. Slots at or past n_slots are still refused. Without the flag a negative
+ * slot is refused, as the reference's write refuses PAD_SLOT_ID (vllm_ttkv/impl.py:217-238). */
+#define TTKV_CACHE_SKIP_PAD 1
 
 /* The batch's paging and decoders. Request r owns block_table[r*bt_stride + 0..], its first
  * seq_lens[r] tokens are stored (position = index), and its decoder is

@@ -280,6 +280,33 @@ def test_device_plan_refuses_a_request_without_a_decoder_on_the_device(monkeypat
     _close(out[:1], stores.expected_decode(sub, q=q[:1].float().cpu().numpy()))
 
 
+def test_a_device_planned_step_skips_the_padding_of_a_padded_batch(monkeypatch):
+    """A decode batch padded to a captured size: the padding request has seq_len 0, slot
+    PAD_SLOT_ID and no decoder. It writes and reads nothing and refuses nothing."""
+    from vllm_ttkv import impl as impl_mod
+    from vllm_ttkv import ops
+    monkeypatch.setattr(impl_mod, "_DEVICE_PLAN", True)
+    w = _world(41, [50, 23])
+    md, raw_k, value, q = _step(w, [1, 1])
+    pad = lambda t, v: torch.cat([t, torch.full_like(t[:1], v)])
+    qsl = torch.arange(4, dtype=torch.int32)
+    mdp = metadata.TTKVAttentionMetadata(
+        seq_lens=pad(md.seq_lens, 0), slot_mapping=pad(md.slot_mapping, -1),
+        block_table=pad(md.block_table, 0), query_start_loc=qsl.cuda(), query_start_loc_cpu=qsl,
+        num_actual_tokens=3, ttkv_serial=metadata.next_serial())
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+    rows = w["page"].view(-1, w["page"].shape[-1])             # [slots, blob]
+    rows[md.slot_mapping] = 0xAB                               # the real tokens' slots, marked
+    before = rows.clone()
+    ops.reset_status()
+    out = _forward(impl, w, mdp, pad(raw_k, 0), pad(value, 0), pad(q, 0))
+    ops.check_status()
+    assert torch.all(out[2] == 0)
+    changed = (rows != before).any(1).nonzero().flatten().tolist()
+    assert sorted(changed) == sorted(md.slot_mapping.tolist())  # the two real tokens' slots only
+    _close(out[:2], stores.expected_decode(_after(w), q=q.float().cpu().numpy()))
+
+
 def test_a_pinned_pool_refuses_to_grow():
     from vllm_ttkv import ops
     w = _world(40, [20])

@@ -206,6 +206,32 @@ def test_write_refuses_pad_slot_on_device():
         ops.check_status()
 
 
+@pytest.mark.parametrize("r1", [32, 208])
+def test_write_skips_pad_slots_when_asked(r1):
+    """TTKV_CACHE_SKIP_PAD (the padding of a batch padded to a captured graph): the padding tokens
+    write nothing, even with a decoder row of -1, and the others write what they write alone
+    (r1 32: the fused cluster write; 208: the two-launch write)."""
+    from vllm_ttkv import ops
+    st, g, K, V, tok_dec = _frozen_case(seed=3, n_tok=4, r1=r1)
+    k = torch.from_numpy(K.transpose(1, 0, 2).copy()).cuda().half()
+    v = torch.from_numpy(V.transpose(1, 0, 2).copy()).cuda().half()
+    dec, pinv = torch.from_numpy(st["decoders"]).cuda(), torch.from_numpy(st["pinvT"]).cuda()
+    rows = torch.from_numpy(tok_dec).cuda()
+    rows_pad = rows.clone()
+    rows_pad[1] = -1
+    outs = []
+    for slots, tdec, skip in (([0, 1, 2, 3], rows, False), ([0, -1, 2, -1], rows_pad, True)):
+        cache = torch.full((8, g.blob_bytes), 7, dtype=torch.uint8, device="cuda")
+        ops.reset_status()
+        ops.write_paged(_lay(g), cache, torch.tensor(slots, dtype=torch.int64, device="cuda"), k, v,
+                        tdec, dec, pinvs=pinv, skip_pad=skip)
+        ops.check_status()
+        outs.append(cache.cpu().numpy())
+    full, padded = outs
+    assert np.array_equal(padded[[0, 2]], full[[0, 2]])
+    assert np.all(padded[[1, 3]] == 7) and np.all(padded[4:] == 7)
+
+
 def test_write_then_read_round_trip():
     """A store written by the CUDA writer reads back (CUDA reader) like the oracle reads it."""
     from vllm_ttkv import ops

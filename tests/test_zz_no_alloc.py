@@ -46,7 +46,7 @@ def _noalloc(d, out, max_seq, status):
     """One call of ttkv_decode_paged_noalloc with plain pointers (no workspace argument)."""
     lib = _lib.lib()
     la = d["lay"].abi()
-    cache = _lib.Cache(d["cache"].data_ptr(), d["cache"].shape[0], d["cache"].stride(0), 16)
+    cache = _lib.Cache(d["cache"].data_ptr(), d["cache"].shape[0], d["cache"].stride(0), 16, 0)
     batch = _lib.Batch(d["bt"].data_ptr(), d["bt"].stride(0), d["bt"].shape[1], d["seq"].data_ptr(),
                        d["bt"].shape[0], d["dec"].data_ptr(), d["dec"].stride(0), d["idx"].data_ptr(),
                        d["dec"].shape[0])

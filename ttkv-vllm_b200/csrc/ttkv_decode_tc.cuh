@@ -873,12 +873,13 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
                 trim_bitmap(bw, P.v_lanes);
                 const uint32_t word = wg == 0 ? bw[0] : wg == 1 ? bw[1] : wg == 2 ? bw[2] : bw[3];
-                int rank = (wg > 0 ? __popc(bw[0]) : 0) + (wg > 1 ? __popc(bw[1]) : 0) + (wg > 2 ? __popc(bw[2]) : 0);
+                const int rank0 = (wg > 0 ? __popc(bw[0]) : 0) + (wg > 1 ? __popc(bw[1]) : 0) + (wg > 2 ? __popc(bw[2]) : 0);
                 #pragma unroll
                 for (int gi = 0; gi < 4; ++gi) {
                     const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
+                    // each group's rank from the word directly: the four groups do not wait on each other
+                    const int rank = rank0 + (gi ? __popc(word >> (32 - 8 * gi)) : 0);
                     const uint32_t win = window32(base, vfo + 16u, uint32_t(rank * vbits)) ^ vflip;
-                    rank += __popc(byte);
                     uint32_t f[8];
                     group_fields(win, byte, vbits, lutv, f);
                     uint32_t hv[4];
@@ -923,9 +924,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             #pragma unroll
             for (int g = 0; g < 8; ++g) sp[g] = 0.f;
             if (!__any_sync(0xffffffffu, timed_out)) {
-                float2 s2[G];
+                // two accumulators per query head (the yl and the yh terms): chains half as long
+                float2 s2[G], s2h[G];
                 #pragma unroll
-                for (int g = 0; g < G; ++g) s2[g] = make_float2(0.f, 0.f);
+                for (int g = 0; g < G; ++g) { s2[g] = make_float2(0.f, 0.f); s2h[g] = s2[g]; }
                 const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
                 const float2 neg1 = make_float2(-1.f, -1.f);
                 #pragma unroll
@@ -966,12 +968,13 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                         #pragma unroll
                         for (int g = 0; g < G; ++g) {
                             const float4 qq = qs4[g * 32 + (j0 >> 1) + i];
-                            s2[g] = f2fma(make_float2(qq.x, qq.y), yl, f2fma(make_float2(qq.z, qq.w), yh, s2[g]));
+                            s2[g] = f2fma(make_float2(qq.x, qq.y), yl, s2[g]);
+                            s2h[g] = f2fma(make_float2(qq.z, qq.w), yh, s2h[g]);
                         }
                     }
                 }
                 #pragma unroll
-                for (int g = 0; g < G; ++g) sp[g] = s2[g].x + s2[g].y;
+                for (int g = 0; g < G; ++g) sp[g] = (s2[g].x + s2h[g].x) + (s2[g].y + s2h[g].y);
                 tmem_st8(t_row + RED_COL + uint32_t(8 * wg), sp);     // partial scores -> TMEM
                 tmem_wait_st();
             }

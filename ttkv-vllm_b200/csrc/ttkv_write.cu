@@ -120,6 +120,8 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
 // (the two-launch frozen write, for pools the fused kernel cannot map)
 struct ProjParams {
     int H, r1;
+    const int64_t* slots;     // skip_pad: a token with a negative slot is not projected
+    int skip_pad;
     const void* k;
     int k_dtype;
     int64_t k_stride;
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(PROJ_WARPS * 32) project_kernel(const ProjPara
     for (int i = threadIdx.x; i < HD; i += blockDim.x)
         m_s[i] = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + i);
     __syncthreads();
+    if (P.skip_pad && P.slots[t] < 0) return;                 // a padding token: nothing to write
     const int di = P.tok_dec[t];
     if (di < 0 || di >= P.n_decoders) {
         if (threadIdx.x == 0) report(P.status, TTKV_STATUS_DECODER);
@@ -170,6 +173,7 @@ struct EncParams {
     int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
     uint8_t* cache;
     int64_t n_slots, row_bytes;
+    int skip_pad;             // TTKV_CACHE_SKIP_PAD: a negative slot is skipped, not refused
     const int64_t* slots;
     const void* k;
     int k_dtype;
@@ -199,6 +203,7 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
     __shared__ float cs_s;
 
     const int64_t slot = P.slots[t];
+    if (slot < 0 && P.skip_pad) return;
     if (slot < 0 || slot >= P.n_slots) {
         if (tid == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
         return;
@@ -303,6 +308,7 @@ struct FrozenParams {
     int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
     uint8_t* cache;
     int64_t n_slots, row_bytes;
+    int skip_pad;             // TTKV_CACHE_SKIP_PAD: a negative slot is skipped, not refused
     const int64_t* slots;
     const void* k;
     int k_dtype;
@@ -360,6 +366,7 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
     const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
     pdl_trigger();                                           // the read of the step may launch
     const int64_t slot = P.slots[t];
+    if (slot < 0 && P.skip_pad) return;                      // the cluster's token: uniform
     if (slot < 0 || slot >= P.n_slots) {
         if (tid == 0 && h == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
         return;
@@ -467,6 +474,7 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
 struct RowsParams {
     uint8_t* cache;
     int64_t n_slots, row_bytes;
+    int skip_pad;             // TTKV_CACHE_SKIP_PAD: a negative slot is skipped, not refused
     const int64_t* slots;
     int n_tok, heads, field_off, row_stride, lanes, bits;
     const void* x;
@@ -482,6 +490,7 @@ __global__ void __launch_bounds__(128) select_rows_kernel(const RowsParams P) {
     if (i >= int64_t(P.n_tok) * P.heads) return;
     const int t = int(i % P.n_tok), h = int(i / P.n_tok);
     const int64_t slot = P.slots[t];
+    if (slot < 0 && P.skip_pad) return;
     if (slot < 0 || slot >= P.n_slots) {
         if (L == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
         return;
@@ -632,6 +641,7 @@ int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_cache_t* cache, con
     P.v_lanes = lay->v_lanes; P.v_bits = lay->v_bits; P.coeff_bytes = lay->coeff_bytes;
     P.k_row = lay->k_row_bytes; P.v_row = lay->v_row_bytes; P.v_offset = lay->v_offset;
     P.cache = cache->base; P.n_slots = cache->n_slots; P.row_bytes = cache->row_bytes;
+    P.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
     P.k_dtype = k_dtype; P.k_stride = k_stride; P.v_dtype = v_dtype; P.v_stride = v_stride;
     P.n_decoders = n_decoders; P.status = status;
     const int esz_k = k_dtype == TTKV_F32 ? 4 : 2, esz_v = v_dtype == TTKV_F32 ? 4 : 2;
@@ -711,7 +721,8 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
     float* c = nullptr;
     if (frozen) {
         ProjParams pp{};
-        pp.H = lay->H; pp.r1 = lay->r1; pp.k = k; pp.k_dtype = k_dtype; pp.k_stride = k_stride;
+        pp.H = lay->H; pp.r1 = lay->r1; pp.slots = slot_mapping; pp.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
+        pp.k = k; pp.k_dtype = k_dtype; pp.k_stride = k_stride;
         pp.tok_dec = tok_dec; pp.pinvs = pinvs; pp.pinv_stride = pinv_stride; pp.n_decoders = n_decoders;
         c = reinterpret_cast<float*>(workspace);
         pp.c = c; pp.status = status;
@@ -724,6 +735,7 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
     ep.v_lanes = lay->v_lanes; ep.v_bits = lay->v_bits; ep.coeff_bytes = lay->coeff_bytes;
     ep.k_row = lay->k_row_bytes; ep.v_row = lay->v_row_bytes; ep.v_offset = lay->v_offset;
     ep.cache = cache->base; ep.n_slots = cache->n_slots; ep.row_bytes = cache->row_bytes;
+    ep.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
     ep.slots = slot_mapping; ep.k = k; ep.k_dtype = k_dtype; ep.k_stride = k_stride;
     ep.v = v; ep.v_dtype = v_dtype; ep.v_stride = v_stride; ep.tok_dec = tok_dec;
     ep.decoders = decoders; ep.dec_stride = dec_stride; ep.n_decoders = n_decoders;
@@ -748,6 +760,7 @@ extern "C" int ttkv_select_pack_rows(const ttkv_cache_t* cache, const int64_t* s
     if (x_dtype < TTKV_F32 || x_dtype > TTKV_BF16) return fail(TTKV_ERR_ARG, "x dtype");
     RowsParams p{};
     p.cache = cache->base; p.n_slots = cache->n_slots; p.row_bytes = cache->row_bytes;
+    p.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
     p.slots = slots; p.n_tok = n_tok; p.heads = heads; p.field_off = field_off;
     p.row_stride = row_stride; p.lanes = lanes; p.bits = bits; p.x = x; p.x_dtype = x_dtype;
     p.status = status;

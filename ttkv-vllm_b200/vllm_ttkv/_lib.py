@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import pathlib
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 LIB_PATH = pathlib.Path(__file__).resolve().parents[1] / "libttkv_sm100.so"
 
 # host-side refusal codes (ttkv_b200.h)
@@ -23,6 +23,7 @@ STATUS = {0: "ok", 1: "block index outside the cache", 2: "block-table row too s
           7: "a seq_len above the max_seq_len the read was given (its bound)"}
 
 F32, F16, BF16 = 0, 1, 2
+CACHE_SKIP_PAD = 1                          # TTKV_CACHE_SKIP_PAD
 NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024   # TTKV_NOALLOC_SCRATCH_BYTES
 
 
@@ -35,7 +36,7 @@ class Layout(C.Structure):
 
 class Cache(C.Structure):
     _fields_ = [("base", C.c_void_p), ("n_slots", C.c_int64), ("row_bytes", C.c_int64),
-                ("block_size", C.c_int32)]
+                ("block_size", C.c_int32), ("flags", C.c_int32)]
 
 
 class Batch(C.Structure):

@@ -147,7 +147,9 @@ def write_fitted(cache_u8: torch.Tensor, slot_mapping: torch.Tensor, fk: FittedK
 
 def write_frozen(cache_u8: torch.Tensor, slot_mapping: torch.Tensor, K_tok, V_tok,
                  tok_dec: torch.Tensor, decoders: torch.Tensor, pinvT: torch.Tensor,
-                 lay: TTKLayout) -> None:
-    """Project every token onto its request's frozen decoder and write it (one launch pair for
-    the whole layer): K_tok / V_tok [n, H, d]; tok_dec [n] index into the decoder pool."""
-    ops.write_paged(lay, cache_u8, slot_mapping, K_tok, V_tok, tok_dec, decoders, pinvs=pinvT)
+                 lay: TTKLayout, skip_pad: bool = False) -> None:
+    """Project every token onto its request's frozen decoder and write it (one launch for the
+    whole layer): K_tok / V_tok [n, H, d]; tok_dec [n] index into the decoder pool. skip_pad:
+    padding tokens (PAD_SLOT_ID) are skipped rather than refused."""
+    ops.write_paged(lay, cache_u8, slot_mapping, K_tok, V_tok, tok_dec, decoders, pinvs=pinvT,
+                    skip_pad=skip_pad)

@@ -28,8 +28,10 @@ read's bound is the RoPE table's length, and nothing is read back, so the forwar
 in a CUDA graph and replayed for later steps of the same request count. That is the plan while a
 graph is being captured, and always with VLLM_TTKV_DEVICE_PLAN=1. The host-side refusals of the
 other plan (PAD_SLOT_ID or out-of-range slots, a request without a decoder) then become device
-refusals in the status word, read by `ops.check_status()`. The reference's backend cannot be
-captured at all (vllm_ttkv/metadata.py:95-101).
+refusals in the status word, read by `ops.check_status()`, except that a PAD_SLOT_ID slot is
+skipped: an engine padding a decode batch to a captured size gives its padding tokens that slot
+(and seq_len 0, which the read skips). The reference's backend cannot be captured at all
+(vllm_ttkv/metadata.py:95-101).
 """
 from __future__ import annotations
 
@@ -303,7 +305,9 @@ class TTKVAttentionImpl(_ImplBase):
         if capturing:                       # the graph holds these addresses from now on
             pool.pin()
             ops.pin(key_rows(dev), rows)
-        encode.write_frozen(cache, md.slot_mapping[:n], K, V, rows, pool.decoders, pool.pinvT, lay)
+        # a batch padded to a captured size carries PAD_SLOT_ID for its padding tokens: skipped
+        encode.write_frozen(cache, md.slot_mapping[:n], K, V, rows, pool.decoders, pool.pinvT, lay,
+                            skip_pad=True)
         # the read's bound: the RoPE table (any position the model can reach) under a capture, so
         # the replays of other lengths stay within it; else the step's own max_seq_len
         bound = int(table.shape[0])

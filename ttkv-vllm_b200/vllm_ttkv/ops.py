@@ -128,13 +128,13 @@ def _row_stride(t: torch.Tensor, name: str) -> int:
     return t.stride(0) if t.shape[0] > 1 else t.shape[1] * 128
 
 
-def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int) -> _lib.Cache:
+def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int, flags: int = 0) -> _lib.Cache:
     if flat.dtype != torch.uint8 or flat.dim() != 2:
         raise ValueError("cache must be a [n_slots, row_bytes] uint8 view")
     if flat.shape[1] < lay.compressed_bytes_per_token():
         raise ValueError(f"cache rows are {flat.shape[1]} bytes, the layout needs "
                          f"{lay.compressed_bytes_per_token()}")
-    return _lib.Cache(flat.data_ptr(), flat.shape[0], flat.stride(0), block_size)
+    return _lib.Cache(flat.data_ptr(), flat.shape[0], flat.stride(0), block_size, flags)
 
 
 def decoder_image(lay: TTKLayout, decoders: torch.Tensor, out=None):
@@ -256,11 +256,14 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
 def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor, k: torch.Tensor,
                 v: torch.Tensor, tok_dec: torch.Tensor, decoders: torch.Tensor,
                 pinvs: torch.Tensor | None = None, coeff_q: torch.Tensor | None = None,
-                coeff_scale: torch.Tensor | None = None, status: torch.Tensor | None = None):
+                coeff_scale: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                skip_pad: bool = False):
     """Encode tokens k/v [n, H, d] (raw pre-RoPE K; V) into their slots.
 
     Frozen path: `pinvs` [n_dec, r1, H*d] (pinv transposed) given -> project + quantise.
-    Fit path: `coeff_q` [n, r1] int8 and `coeff_scale` [n] float32 given."""
+    Fit path: `coeff_q` [n, r1] int8 and `coeff_scale` [n] float32 given.
+    skip_pad: a negative slot (PAD_SLOT_ID, the padding of a batch padded to a captured graph's
+    size) is skipped instead of refused."""
     _need_cuda(cache, slot_mapping, k, v, tok_dec, decoders)
     n = slot_mapping.numel()
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
@@ -278,7 +281,7 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
     L = _lib.lib()
     la = lay.abi()
     st = status if status is not None else status_word(k.device)
-    c_s = _cache_struct(lay, cache, 1)
+    c_s = _cache_struct(lay, cache, 1, _lib.CACHE_SKIP_PAD if skip_pad else 0)
     ws_n = L.ttkv_write_workspace_bytes(C.byref(la), n)
     ws = workspace(ws_n, k.device, key="write")
     if pinvs is not None:
@@ -312,7 +315,7 @@ def select_pack_rows(cache: torch.Tensor, slots: torch.Tensor, x: torch.Tensor, 
         raise ValueError(f"{x.shape[0]} rows for {n_tok} tokens and {heads} heads")
     sl = slots.to(torch.int64).contiguous()
     st = status if status is not None else status_word(x.device)
-    c_s = _lib.Cache(cache.data_ptr(), cache.shape[0], cache.stride(0), 1)
+    c_s = _lib.Cache(cache.data_ptr(), cache.shape[0], cache.stride(0), 1, 0)
     _lib.check(_lib.lib().ttkv_select_pack_rows(
         C.byref(c_s), sl.data_ptr(), n_tok, x.data_ptr(), dtype_code(x), heads, d, field_off,
         row_stride, lanes, bits, st.data_ptr(), _stream()))
