@@ -522,6 +522,105 @@ def run_encode(args):
     print(json.dumps(line))
 
 
+def run_sweep(args):
+    """Config 2, the long-context decode sweep: 1082 / 4322 / 8642 / 14402 cached tokens at batch
+    1, 8, 32 and 64, the 28 calibrated layers at `--cfg` (campaign4x: 4-bit residual and V codes),
+    block 16. One step = per layer the write of every request's new token, then the read of every
+    request; the 28 layers of a step are one CUDA graph per point. Set-up fits ONE request per layer
+    at the longest context (the device TT-SVD + this repository's writer) and copies its rows into
+    every request's own blocks, so all requests read the same bytes from different slots (the read's
+    cost depends on the layout and the lengths, not on the values). Reports each point's step time,
+    and per batch the slope of step time over context (us per cached token per step)."""
+    import numpy as np
+    import torch
+
+    from vllm_ttkv import encode, ops, synthetic
+    from vllm_ttkv.layout import layout_for_config
+    device = torch.device("cuda", 0)
+    ctxs = [int(x) for x in args.sweep_ctx.split(",")]
+    batches = [int(x) for x in args.sweep_batch.split(",")]
+    r1s = (synthetic.LLAMA32_3B_R1 * ((args.layers + 27) // 28))[:args.layers]
+    H, HQ, bs = 8, 24, 16
+    Bmax, nmax = max(batches), max(ctxs) + 1
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    bt_np, n_blocks = synthetic.block_table(0, [nmax] * Bmax, bs)
+    bt = torch.from_numpy(bt_np).to(device)
+    slots_all = torch.from_numpy((bt_np[:, :, None].astype(np.int64) * bs + np.arange(bs))
+                                 .reshape(Bmax, -1)[:, :nmax]).to(device)
+    t0 = time.perf_counter()
+    layers = []
+    for l, r1 in enumerate(r1s):
+        lay = layout_for_config(args.cfg, r1, H=H)
+        cache = torch.zeros(n_blocks * bs, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device)
+        K, V = synth_kv_device(gen, H, nmax, dtype=torch.bfloat16)
+        fk = encode.fit_into_budget(K, lay, args.cfg)
+        encode.write_fitted(cache, slots_all[0].contiguous(), fk, K.permute(1, 0, 2).contiguous(),
+                            V.permute(1, 0, 2).contiguous(), lay)
+        rows0 = cache[slots_all[0]]
+        for r in range(1, Bmax):
+            cache[slots_all[r]] = rows0
+        del rows0
+        dec = fk.decoder.decoder_f.unsqueeze(0).expand(Bmax, -1, -1).contiguous()
+        pinvT = fk.decoder.pinvT.unsqueeze(0).expand(Bmax, -1, -1).contiguous()
+        layers.append(dict(lay=lay, cache=cache, dec=dec, pinvT=pinvT, images=ops.decoder_image(lay, dec),
+                           k=torch.randn(Bmax, H, 128, generator=gen, device=device).to(torch.bfloat16),
+                           v=torch.randn(Bmax, H, 128, generator=gen, device=device).to(torch.bfloat16),
+                           q=torch.randn(Bmax, HQ, 128, generator=gen, device=device).to(torch.bfloat16),
+                           out=torch.empty(Bmax, HQ, 128, dtype=torch.bfloat16, device=device)))
+    torch.cuda.synchronize(device)
+    setup_s = time.perf_counter() - t0
+    table = torch.from_numpy(synthetic.cos_sin_cache(nmax + 16, dtype="float32")).to(device).to(torch.bfloat16)
+    dec_index = torch.arange(Bmax, dtype=torch.int32, device=device)
+    hbm, tc, peak_kind = _peaks()
+    ops.status_word(device)
+    points = []
+    for B in batches:
+        for n in ctxs:
+            seq = torch.full((B,), n + 1, dtype=torch.int32, device=device)
+            new_slots = slots_all[:B, n].contiguous()
+
+            def step():
+                for L in layers:
+                    encode.write_frozen(L["cache"], new_slots, L["k"][:B], L["v"][:B], dec_index[:B],
+                                        L["dec"], L["pinvT"], L["lay"])
+                    ops.decode_paged(L["lay"], L["cache"], bs, bt[:B], seq, L["dec"], dec_index[:B], table,
+                                     L["q"][:B], 128 ** -0.5, L["out"][:B], n + 1, images=L["images"])
+
+            step()                                     # eager once: workspaces, then one graph
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            ms = _event_ms(g.replay, args.steps, args.warmup)
+            del g
+            alg = sum(B * (n + 1) * L["lay"].compressed_bytes_per_token()
+                      + B * L["lay"].r1 * H * 128 * 4 + 2 * B * HQ * 128 * 2 for L in layers)
+            points.append({"batch": B, "ctx": n, "ms_per_step": ms, "tok_s": B / (ms * 1e-3),
+                           "read_gbs": alg / (ms * 1e-3) / 1e9})
+    ops.check_status(device)
+    slopes = {}
+    for B in batches:
+        pts = [p for p in points if p["batch"] == B]
+        if len(pts) > 1:
+            x = np.array([p["ctx"] for p in pts], float)
+            y = np.array([p["ms_per_step"] for p in pts], float)
+            slopes[str(B)] = float(np.polyfit(x, y, 1)[0] * 1e3)          # us per cached token
+    top = max(points, key=lambda p: p["read_gbs"])
+    line = {"metric": "decode step ms vs context and batch (cfg2 sweep)", "value": top["tok_s"],
+            "unit": "tok/s (best point)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "workload": "sweep", "dtype": "bf16 model tensors, fp32 math, u8 slots",
+            "data": "synthetic",
+            "config": {"workload": f"cfg2: ctx {ctxs} x batch {batches}, {len(layers)} calibrated layers, "
+                                   f"{args.cfg}, block {bs}, one CUDA graph per step",
+                       "setup_s": round(setup_s, 1)},
+            "points": points, "us_per_cached_token_per_step": slopes,
+            "roofline": {"bound": "hbm", "achieved": top["read_gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": top["read_gbs"] / hbm, "peak_kind": peak_kind,
+                         "note": "whole step (writes + reads) at the best point, algorithmic read bytes"}}
+    print(json.dumps(line))
+
+
 # ---------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -536,14 +635,24 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying per-layer CUDA graphs")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "encode"],
-                    help="decode: config 1 (the default line); prefill: config 3; encode: config 4")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "encode", "sweep"],
+                    help="decode: config 1 (the default line); sweep: config 2; prefill: config 3; "
+                         "encode: config 4")
+    ap.add_argument("--sweep-ctx", default="1082,4322,8642,14402", help="sweep: cached tokens")
+    ap.add_argument("--sweep-batch", default="1,8,32,64", help="sweep: batch sizes")
     ap.add_argument("--prompt-len", type=int, default=None,
                     help="prefill: prompt tokens (7379); encode: tokens per request (16384)")
     ap.add_argument("--chunk", type=int, default=256, help="prefill: query tokens per chunk")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "sweep":
+        if args.cfg == "safe" and "--cfg" not in sys.argv:
+            args.cfg = "campaign4x"                 # config 2 is quoted at 4-bit storage
+        if args.steps == 200:
+            args.steps = 20
+        run_sweep(args)
+        return
     if args.workload != "decode":
         if args.prompt_len is None:
             args.prompt_len = 7379 if args.workload == "prefill" else 16384
