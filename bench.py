@@ -179,38 +179,61 @@ class Workload:
             self.v_new.append(vn)
             self.q.append(torch.randn(B, HQ, 128, generator=gen, device=device).to(dtype))
             self.out.append(torch.empty(B, HQ, 128, dtype=dtype, device=device))
+        self.heads = (0, H)
+        self.read_layouts = list(self.layouts)
+        self.read_dec = list(self.decoders)
         self.table = torch.from_numpy(synthetic.cos_sin_cache(seq + 16, dtype="float32")).to(device).to(dtype)
         self.scale = 128 ** -0.5
 
-    def slot_bytes(self, l):
-        return self.B * self.max_seq * self.layouts[l].compressed_bytes_per_token()
-
-    def read_bytes(self, l, n_heads=8):
-        """Algorithmic bytes of one decode launch: the slots' coefficient blocks and the read
-        heads' K/V rows, the decoders (fp32, the heads read), the queries and outputs."""
-        lay = self.layouts[l]
-        per_tok = lay.coeff_bytes + 2 + n_heads * (lay.k_row_bytes + lay.v_row_bytes)
-        if n_heads == self.H:
-            per_tok = lay.compressed_bytes_per_token()
-        dec = self.B * lay.r1 * n_heads * 128 * 4
-        io = 2 * self.B * (self.HQ * n_heads // self.H) * 128 * 2
-        return self.B * self.max_seq * per_tok + dec + io
-
-    def layer_step(self, l, head_lo=0, head_hi=8):
-        """One layer: write the step's token of every request, then read every request's store."""
-        from vllm_ttkv import encode, ops
-        lay = self.layouts[l]
-        encode.write_frozen(self.caches[l], self.new_slots, self.k_new[l], self.v_new[l],
-                            self.dec_index, self.decoders[l], self.pinvT[l], lay)
-        ops.decode_paged(lay, self.caches[l], self.bs, self.block_table, self.seq_lens,
-                         self.decoders[l], self.dec_index, self.table, self.q[l], self.scale,
-                         self.out[l], self.max_seq, head_lo, head_hi, images=self.images[l])
-
-    def step(self, head_lo=0, head_hi=8, gather=None):
+    def shard(self, lo, hi):
+        """Keep only KV heads [lo, hi) in storage, the storage-sharded format of tensor
+        parallelism: each layer's cache becomes the blobs of `lay.shard(lo, hi)` (the coefficient
+        block and these heads' rows), the read's decoders these heads' columns. The write still
+        projects every head (the pinv and K of all heads), and packs these heads only."""
+        from vllm_ttkv import ops
+        from vllm_ttkv.layout import shard_slots
+        self.heads = (lo, hi)
         for l in range(self.L):
-            self.layer_step(l, head_lo, head_hi)
-            if gather is not None:
-                gather(l)
+            lay = self.layouts[l]
+            self.caches[l] = shard_slots(self.caches[l], lay, lo, hi)
+            self.read_layouts[l] = lay.shard(lo, hi)
+            self.read_dec[l] = self.decoders[l][:, :, lo * 128:hi * 128].contiguous()
+            self.images[l] = ops.decoder_image(self.read_layouts[l], self.read_dec[l])
+        import torch
+        torch.cuda.empty_cache()
+
+    def slot_bytes(self, l):
+        return self.B * self.max_seq * self.read_layouts[l].compressed_bytes_per_token()
+
+    def read_bytes(self, l):
+        """Algorithmic bytes of one decode launch: the slots (this rank's storage: the coefficient
+        block and its heads' rows), the decoders (fp32, the heads read), the queries and outputs."""
+        lay = self.read_layouts[l]
+        dec = self.B * lay.r1 * lay.H * 128 * 4
+        io = 2 * self.B * (self.HQ * lay.H // self.H) * 128 * 2
+        return self.B * self.max_seq * lay.compressed_bytes_per_token() + dec + io
+
+    def write(self, l):
+        """The write of the step's token of every request (every head projected; this rank's
+        heads packed)."""
+        from vllm_ttkv import encode
+        encode.write_frozen(self.caches[l], self.new_slots, self.k_new[l], self.v_new[l],
+                            self.dec_index, self.decoders[l], self.pinvT[l], self.layouts[l],
+                            heads=self.heads)
+
+    def read(self, l):
+        """The read of every request's store: this rank's query heads of out[l]."""
+        from vllm_ttkv import ops
+        lo, hi = self.heads
+        G = self.HQ // self.H
+        ops.decode_paged(self.read_layouts[l], self.caches[l], self.bs, self.block_table, self.seq_lens,
+                         self.read_dec[l], self.dec_index, self.table, self.q[l][:, lo * G:hi * G],
+                         self.scale, self.out[l][:, lo * G:hi * G], self.max_seq, images=self.images[l])
+
+    def layer_step(self, l):
+        """One layer: write the step's token of every request, then read every request's store."""
+        self.write(l)
+        self.read(l)
 
 
 # ---------------------------------------------------------------------------- plugin e2e
@@ -684,6 +707,8 @@ def main():
     r1s = (S.LLAMA32_3B_R1 * ((args.layers + 27) // 28))[:args.layers]
     t0 = time.perf_counter()
     wl = Workload(args.batch, args.ctx, r1s, args.cfg, device, torch.bfloat16, seed=0)
+    if sh is not None:
+        wl.shard(head_lo, head_hi)                 # each rank stores only its heads' rows
     setup_s = time.perf_counter() - t0
 
     bufs = [sh.buffers(wl.B, 128, wl.dtype, device) for _ in range(wl.L)] if sh else None
@@ -691,7 +716,7 @@ def main():
     def layer_work(l):
         """The layer's launches on this rank (what a layer graph holds): write, read, and the copy
         of this rank's query heads into the all-gather's send buffer."""
-        wl.layer_step(l, head_lo, head_hi)
+        wl.layer_step(l)
         if sh is not None:
             sh.pack(wl.out[l], bufs[l][0])
 
@@ -754,14 +779,12 @@ def main():
         for l in range(wl.L):
             a, b = evs[rep * wl.L + l]
             a.record()
-            ops.decode_paged(wl.layouts[l], wl.caches[l], wl.bs, wl.block_table, wl.seq_lens,
-                             wl.decoders[l], wl.dec_index, wl.table, wl.q[l], wl.scale, wl.out[l],
-                             wl.max_seq, head_lo, head_hi, images=wl.images[l])
+            wl.read(l)
             b.record()
     torch.cuda.synchronize(device)
     dec_ms = [a.elapsed_time(b) for a, b in evs]
     dec_total_ms = sum(dec_ms) / reps                          # all layers' decode launches, per step
-    alg_bytes = sum(wl.read_bytes(l, n_heads) for l in range(wl.L))
+    alg_bytes = sum(wl.read_bytes(l) for l in range(wl.L))
     achieved = alg_bytes / (dec_total_ms * 1e-3) / 1e9
     # algorithmic reconstruction FLOPs, (cq*cs) @ D over the heads read (the fp16 hi/lo split of
     # D doubles the tensor-core work actually issued; that is not counted)
@@ -827,7 +850,7 @@ def main():
     cap = CAPTURED_LAUNCH["layer"]
     traffic = None
     if cap < wl.L and n_heads == H:
-        traffic = CAPTURED_LAUNCH["dram_bytes"] * (alg_bytes / wl.L) / wl.read_bytes(cap, n_heads)
+        traffic = CAPTURED_LAUNCH["dram_bytes"] * (alg_bytes / wl.L) / wl.read_bytes(cap)
     if rank == 0:
         line = {"metric": METRIC, "value": args.batch / (ms * 1e-3), "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -841,6 +864,10 @@ def main():
                            "l2": "inputs larger than L2 (slots %.0f MB/step)" % (
                                sum(wl.slot_bytes(l) for l in range(wl.L)) / 1e6),
                            "parallelism": f"kv-head shard x{world}" if world > 1 else "single",
+                           "storage_bytes_per_token": sum(wl.read_layouts[l].compressed_bytes_per_token()
+                                                          for l in range(wl.L)),
+                           "storage": ("storage-sharded: coefficient block + this rank's heads' rows"
+                                       if world > 1 else "full blobs"),
                            "launch": "one CUDA graph per layer (write + read)" if graphs else "eager"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define TTKV_ABI_VERSION 3
+#define TTKV_ABI_VERSION 4
 
 /* host-side refusals (return values) */
 #define TTKV_OK 0
@@ -244,6 +244,28 @@ int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
                      const int8_t* coeff_q, const float* coeff_scale,
                      void* workspace, size_t workspace_bytes,
                      int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------- write, storage-sharded
+ * No counterpart in the reference (it has no multi-GPU path): an addition of this library.
+ * The storage-sharded slot format for KV-head tensor parallelism: a GPU holding KV heads
+ * [h_lo, h_hi) stores per token the blob of the layout with H' = h_hi - h_lo heads and the same
+ * widths: [coefficient block + ruler][its heads' K rows] padded to 16 B, [its heads' V rows]
+ * padded to 16 B. Reassembled (coefficient block from any shard, head rows in head order, zero
+ * padding) the shards are byte-identical to the full blob ttkv_write_paged writes.
+ * `lay` is the FULL layout: k/v, the decoders and the pinv pool cover all H heads, because the
+ * coefficients project every head's K (c = M @ pinv); only heads [h_lo, h_hi) are packed, into
+ * `cache`, whose rows have the held heads' layout (ttkv_layout_init with H' heads).
+ * A read of a shard is ttkv_decode_paged with that layout, the decoders' columns of the held
+ * heads ([r1, H'*d] per decoder) and the held heads' query rows.
+ * ttkv_write_paged(lay, ...) is ttkv_write_paged_shard(lay, 0, lay->H, ...). */
+int ttkv_write_paged_shard(const ttkv_layout_t* lay, int32_t h_lo, int32_t h_hi,
+                           const ttkv_cache_t* cache, const int64_t* slot_mapping, int32_t n_tok,
+                           const void* k, int32_t k_dtype, int64_t k_stride,
+                           const void* v, int32_t v_dtype, int64_t v_stride,
+                           const int32_t* tok_dec, const float* decoders, int64_t dec_stride,
+                           const float* pinvs, int64_t pinv_stride, int32_t n_decoders,
+                           const int8_t* coeff_q, const float* coeff_scale,
+                           void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /* Lane select + quantise + bit-pack of `rows` (head, token)-ordered rows x [rows, d] into the
  * slots: row i = h*n_tok + t lands at slots[t], field_off + h*row_stride. The standalone form

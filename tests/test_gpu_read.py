@@ -258,3 +258,27 @@ def test_decode_three_virtual_shares_per_cta():
     cut each CTA's share into 3 virtual shares."""
     st = stores.make_store(15, [2100] * 7, cfg="safe", r1=24, block_size=1)
     assert np.abs(_decode(st) - stores.expected_decode(st)).max() < 1e-4
+
+
+def test_decode_of_a_storage_shard_matches_the_full_decode_on_its_heads():
+    """A shard's cache (its heads' rows), its decoders' columns and its heads' queries: the same
+    outputs as the full store's decode on those heads (the schedules split differently, so to
+    float rounding of the merge)."""
+    from vllm_ttkv import ops
+    from vllm_ttkv.layout import shard_slots
+    st = stores.make_store(16, [300, 77, 129], cfg="safe", r1=110)
+    d = _dev(st)
+    full = _decode(st)
+    G = 3
+    for lo, hi in ((0, 4), (4, 8), (6, 8)):
+        lay = d["lay"].shard(lo, hi)
+        cache = shard_slots(d["cache"], d["lay"], lo, hi)
+        dec = d["dec"][:, :, lo * 128:hi * 128].contiguous()
+        q = d["q"][:, lo * G:hi * G]
+        out = torch.zeros(3, (hi - lo) * G, 128, device="cuda")
+        ops.reset_status()
+        ops.decode_paged(lay, cache, st["block_size"], d["bt"], d["seq"], dec, d["idx"], d["table"],
+                         q, 128 ** -0.5, out, int(st["seq_lens"].max()),
+                         images=ops.decoder_image(lay, dec))
+        ops.check_status()
+        assert np.abs(out.cpu().numpy() - full[:, lo * G:hi * G]).max() < 1e-5, (lo, hi)

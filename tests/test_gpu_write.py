@@ -101,24 +101,27 @@ def _frozen_case(seed=0, n_tok=7, cfg="safe", r1=32, kv_dtype="float16"):
     return st, g, K, V, tok_dec
 
 
-def _write_gpu(g, K, V, tok_dec, decoders, pinvT=None, cq=None, cs=None, kv_dtype=torch.float16):
+def _write_gpu(g, K, V, tok_dec, decoders, pinvT=None, cq=None, cs=None, kv_dtype=torch.float16,
+               heads=None):
     from vllm_ttkv import ops
     n = K.shape[1]
-    cache = torch.zeros(n + 3, g.blob_bytes + 16, dtype=torch.uint8, device="cuda")
+    lay = _lay(g)
+    blob = lay.shard(*heads).compressed_bytes_per_token() if heads else g.blob_bytes
+    cache = torch.zeros(n + 3, blob + 16, dtype=torch.uint8, device="cuda")
     slots = torch.arange(n, dtype=torch.int64, device="cuda") + 2           # not starting at 0
     k = torch.from_numpy(K.transpose(1, 0, 2).copy()).cuda().to(kv_dtype)
     v = torch.from_numpy(V.transpose(1, 0, 2).copy()).cuda().to(kv_dtype)
     ops.reset_status()
-    ops.write_paged(_lay(g), cache, slots, k, v, torch.from_numpy(tok_dec).cuda(),
+    ops.write_paged(lay, cache, slots, k, v, torch.from_numpy(tok_dec).cuda(),
                     torch.from_numpy(decoders).cuda(),
                     pinvs=None if pinvT is None else torch.from_numpy(pinvT).cuda(),
                     coeff_q=None if cq is None else torch.from_numpy(cq).cuda(),
-                    coeff_scale=None if cs is None else torch.from_numpy(cs).cuda())
+                    coeff_scale=None if cs is None else torch.from_numpy(cs).cuda(), heads=heads)
     ops.check_status()
     c = cache.cpu().numpy()
     assert not c[:2].any() and not c[n + 2:].any(), "wrote outside the named slots"
-    assert not c[:, g.blob_bytes:].any(), "wrote past the blob"
-    return c[2:n + 2, :g.blob_bytes]
+    assert not c[:, blob:].any(), "wrote past the blob"
+    return c[2:n + 2, :blob]
 
 
 def test_write_given_coefficients_is_bit_exact():
@@ -230,6 +233,30 @@ def test_write_skips_pad_slots_when_asked(r1):
     full, padded = outs
     assert np.array_equal(padded[[0, 2]], full[[0, 2]])
     assert np.all(padded[[1, 3]] == 7) and np.all(padded[4:] == 7)
+
+
+@pytest.mark.parametrize("r1", [32, 110, 208])
+def test_storage_sharded_writes_reassemble_to_the_full_write(r1):
+    """Each of 2, 4 and 8 shards written on its own (only its heads' rows, every head projected)
+    reassembles to the bytes of the full write, bit for bit: the fused cluster write (r1 32, 110)
+    and the two-launch write (208), frozen path; and the fit path with given coefficients."""
+    import torch as _t
+    from vllm_ttkv.layout import unshard_slots
+    from vllm_ttkv.shard import head_range
+    st, g, K, V, tok_dec = _frozen_case(seed=5, n_tok=6, r1=r1)
+    lay = _lay(g)
+    cases = {"frozen": dict(pinvT=st["pinvT"])}
+    if r1 == 32:
+        cq = np.random.default_rng(1).integers(-128, 128, (K.shape[1], r1)).astype(np.int8)
+        cases["fit"] = dict(cq=cq, cs=np.full(K.shape[1], 0.013, np.float32))
+    for name, kw in cases.items():
+        full = _write_gpu(g, K, V, tok_dec, st["decoders"], **kw)
+        for world in (2, 4, 8):
+            ranges = [head_range(r, world, g.H) for r in range(world)]
+            shards = [_t.from_numpy(_write_gpu(g, K, V, tok_dec, st["decoders"], heads=hr, **kw))
+                      for hr in ranges]
+            got = unshard_slots(shards, lay, ranges).numpy()
+            assert np.array_equal(got, full), (name, world)
 
 
 def test_write_then_read_round_trip():

@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(PROJ_WARPS * 32) project_kernel(const ProjPara
 // ------------------------------------------------------------------ encode + pack
 struct EncParams {
     int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
+    int h_lo;                 // the cache holds heads [h_lo, h_lo + gridDim.x): head h's rows are
+                              // written at h - h_lo (v_offset is the cache layout's)
     uint8_t* cache;
     int64_t n_slots, row_bytes;
     int skip_pad;             // TTKV_CACHE_SKIP_PAD: a negative slot is skipped, not refused
@@ -191,9 +193,9 @@ struct EncParams {
     int32_t* status;
 };
 
-// grid (H, n_tok), 128 threads.
+// grid (heads written, n_tok), 128 threads: CTA x = KV head h_lo + x.
 __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
-    const int h = blockIdx.x, t = blockIdx.y;
+    const int h = P.h_lo + int(blockIdx.x), t = blockIdx.y, hs = int(blockIdx.x);
     const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
     __shared__ float g_s[kMaxRank];          // cq * cs
     __shared__ int8_t cq_s[kMaxRank];
@@ -275,14 +277,14 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
         float x[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i) x[i] = r_s[4 * L + i];
-        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + h * P.k_row, codes_s[0]);
+        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + hs * P.k_row, codes_s[0]);
     } else if (w == 1) {
         float x[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i)
             x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
-        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + h * P.v_row, codes_s[1]);
-    } else if (w == 2 && h == 0) {
+        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + hs * P.v_row, codes_s[1]);
+    } else if (w == 2 && hs == 0) {
         // the coefficient block and its fp16 ruler, once per token (encode.py:570-573)
         for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
         if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs_s);
@@ -302,10 +304,16 @@ __global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
 //   residual  R = K - (cq*cs) @ decoder[:, h]                                  (encode.py:335-336)
 //   pack      the K residual row; CTA 0 also writes the coefficient block and its ruler
 //
+// A head-sharded cache holds heads [h_lo, h_hi) only (the storage-sharded format): every CTA of
+// the cluster still projects (c needs every head), but only the held heads load their decoder
+// slice and write rows, at h - h_lo, and CTA h_lo writes the coefficient block.
+//
 // Every CTA of a cluster handles the same token, so the early exits (a bad slot or decoder index)
 // are taken by all of them together, before the first cluster barrier.
 struct FrozenParams {
     int H, r1, res_k, res_bits, v_lanes, v_bits, coeff_bytes, k_row, v_row, v_offset;
+    int h_lo, h_hi;           // heads the cache holds: every CTA projects, these write their rows
+                              // at h - h_lo (v_offset is the cache layout's)
     uint8_t* cache;
     int64_t n_slots, row_bytes;
     int skip_pad;             // TTKV_CACHE_SKIP_PAD: a negative slot is skipped, not refused
@@ -377,21 +385,23 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
         return;
     }
     uint8_t* row = P.cache + slot * P.row_bytes;
+    const bool held = h >= P.h_lo && h < P.h_hi;             // this head's rows are written here
+    const int hs = h - P.h_lo;
 
     if (tid == 0) mbar_init(&bar, 1);
     __syncthreads();
     if (tid == 0) {
-        mbar_expect_tx(&bar, uint32_t(2 * P.r1 * kHeadDim * sizeof(float)));
+        mbar_expect_tx(&bar, uint32_t((held ? 2 : 1) * P.r1 * kHeadDim * sizeof(float)));
         tma_load_2d(pinv_s, &M.pinv, h * kHeadDim, di * P.r1, &bar);
-        tma_load_2d(dec_s, &M.dec, h * kHeadDim, di * P.r1, &bar);
+        if (held) tma_load_2d(dec_s, &M.dec, h * kHeadDim, di * P.r1, &bar);
     }
     if (tid < kHeadDim) k_s[tid] = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + h * kHeadDim + tid);
-    if (w == 7) {                                            // V needs nothing from the projection
+    if (w == 7 && held) {                                    // V needs nothing from the projection
         float x[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i)
             x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
-        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + h * P.v_row, codes_s[1]);
+        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + hs * P.v_row, codes_s[1]);
     }
     const bool landed = mbar_wait(&bar, 0);
     const bool bad = __syncthreads_or(!landed);              // also publishes k_s
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
     __syncthreads();
 
     // ---- (cq*cs) @ decoder[:, h]: the two thread halves take the two halves of the rows
-    if (!bad) {
+    if (!bad && held) {
         const int half = tid >> 7, j = tid & 127;
         const int mid = (P.r1 + 1) >> 1;
         const int i0 = half ? mid : 0, i1 = half ? P.r1 : mid;
@@ -457,12 +467,12 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
     }
     __syncthreads();
 
-    if (!bad && w == 0) {
+    if (!bad && held && w == 0) {
         float x[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i) x[i] = k_s[4 * L + i] - (kd_s[0][4 * L + i] + kd_s[1][4 * L + i]);
-        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + h * P.k_row, codes_s[0]);
-    } else if (!bad && w == 1 && h == 0) {
+        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + hs * P.k_row, codes_s[0]);
+    } else if (!bad && w == 1 && h == P.h_lo) {
         for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
         if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs);
     }
@@ -590,7 +600,8 @@ int check_cache(const ttkv_cache_t* cache, int need) {
 
 // The fused frozen write when the pools map as 2-D TMA tensors and the slices fit in shared
 // memory: returns 0 when launched, a negative error code, or 1 to take the two-launch path.
-int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_cache_t* cache, const int64_t* slots,
+int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_layout_t* out, int h_lo,
+                        const ttkv_cache_t* cache, const int64_t* slots,
                         int32_t n_tok, const void* k, int32_t k_dtype, int64_t k_stride, const void* v,
                         int32_t v_dtype, int64_t v_stride, const int32_t* tok_dec, const float* decoders,
                         int64_t dec_stride, const float* pinvs, int64_t pinv_stride, int32_t n_decoders,
@@ -639,7 +650,8 @@ int launch_frozen_fused(const ttkv_layout_t* lay, const ttkv_cache_t* cache, con
     FrozenParams P{};
     P.H = lay->H; P.r1 = lay->r1; P.res_k = lay->res_k; P.res_bits = lay->res_bits;
     P.v_lanes = lay->v_lanes; P.v_bits = lay->v_bits; P.coeff_bytes = lay->coeff_bytes;
-    P.k_row = lay->k_row_bytes; P.v_row = lay->v_row_bytes; P.v_offset = lay->v_offset;
+    P.k_row = lay->k_row_bytes; P.v_row = lay->v_row_bytes; P.v_offset = out->v_offset;
+    P.h_lo = h_lo; P.h_hi = h_lo + out->H;
     P.cache = cache->base; P.n_slots = cache->n_slots; P.row_bytes = cache->row_bytes;
     P.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
     P.k_dtype = k_dtype; P.k_stride = k_stride; P.v_dtype = v_dtype; P.v_stride = v_stride;
@@ -679,14 +691,14 @@ extern "C" size_t ttkv_write_workspace_bytes(const ttkv_layout_t* lay, int32_t n
     return size_t(n_tok) * lay->r1 * sizeof(float);
 }
 
-extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
-                                const int64_t* slot_mapping, int32_t n_tok, const void* k,
-                                int32_t k_dtype, int64_t k_stride, const void* v, int32_t v_dtype,
-                                int64_t v_stride, const int32_t* tok_dec, const float* decoders,
-                                int64_t dec_stride, const float* pinvs, int64_t pinv_stride,
-                                int32_t n_decoders, const int8_t* coeff_q, const float* coeff_scale,
-                                void* workspace, size_t workspace_bytes, int32_t* status,
-                                void* stream) {
+extern "C" int ttkv_write_paged_shard(const ttkv_layout_t* lay, int32_t h_lo, int32_t h_hi,
+                                      const ttkv_cache_t* cache, const int64_t* slot_mapping,
+                                      int32_t n_tok, const void* k, int32_t k_dtype, int64_t k_stride,
+                                      const void* v, int32_t v_dtype, int64_t v_stride,
+                                      const int32_t* tok_dec, const float* decoders, int64_t dec_stride,
+                                      const float* pinvs, int64_t pinv_stride, int32_t n_decoders,
+                                      const int8_t* coeff_q, const float* coeff_scale, void* workspace,
+                                      size_t workspace_bytes, int32_t* status, void* stream) {
     if (!lay) return fail(TTKV_ERR_ARG, "layout is null");
     if (lay->d != kHeadDim) return fail(TTKV_ERR_UNSUPPORTED, "head dim %d: d=128 only", lay->d);
     if (lay->qbits != 8) return fail(TTKV_ERR_UNSUPPORTED, "qbits=%d: coefficients are int8", lay->qbits);
@@ -695,7 +707,14 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
     if (lay->res_k < 1 || lay->res_bits < 2 || lay->v_bits < 2 || lay->res_bits > 8 || lay->v_bits > 8)
         return fail(TTKV_ERR_UNSUPPORTED, "lane widths res_k=%d res_bits=%d v_bits=%d", lay->res_k,
                     lay->res_bits, lay->v_bits);
-    if (int e = check_cache(cache, lay->blob_bytes)) return e;
+    if (h_lo < 0 || h_hi > lay->H || h_lo >= h_hi)
+        return fail(TTKV_ERR_ARG, "held heads [%d, %d) outside the layout's %d", h_lo, h_hi, lay->H);
+    // the cache's rows: the layout of the held heads (the same widths, H = h_hi - h_lo)
+    ttkv_layout_t out{};
+    if (int e = ttkv_layout_init(&out, h_hi - h_lo, lay->d, lay->r1, lay->qbits, lay->res_k,
+                                 lay->res_bits, lay->v_lanes, lay->v_bits, lay->align))
+        return e;
+    if (int e = check_cache(cache, out.blob_bytes)) return e;
     if (n_tok < 0) return fail(TTKV_ERR_ARG, "n_tok < 0");
     if (n_tok == 0) return TTKV_OK;
     if (!slot_mapping || !k || !v) return fail(TTKV_ERR_ARG, "slot_mapping/k/v null");
@@ -713,9 +732,9 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
                     ttkv_write_workspace_bytes(lay, n_tok));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (frozen) {
-        const int r = launch_frozen_fused(lay, cache, slot_mapping, n_tok, k, k_dtype, k_stride, v, v_dtype,
-                                          v_stride, tok_dec, decoders, dec_stride, pinvs, pinv_stride,
-                                          n_decoders, status, st);
+        const int r = launch_frozen_fused(lay, &out, h_lo, cache, slot_mapping, n_tok, k, k_dtype, k_stride,
+                                          v, v_dtype, v_stride, tok_dec, decoders, dec_stride, pinvs,
+                                          pinv_stride, n_decoders, status, st);
         if (r <= 0) return r;                                // launched (0) or failed (< 0)
     }
     float* c = nullptr;
@@ -733,7 +752,8 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
     EncParams ep{};
     ep.H = lay->H; ep.r1 = lay->r1; ep.res_k = lay->res_k; ep.res_bits = lay->res_bits;
     ep.v_lanes = lay->v_lanes; ep.v_bits = lay->v_bits; ep.coeff_bytes = lay->coeff_bytes;
-    ep.k_row = lay->k_row_bytes; ep.v_row = lay->v_row_bytes; ep.v_offset = lay->v_offset;
+    ep.k_row = lay->k_row_bytes; ep.v_row = lay->v_row_bytes; ep.v_offset = out.v_offset;
+    ep.h_lo = h_lo;
     ep.cache = cache->base; ep.n_slots = cache->n_slots; ep.row_bytes = cache->row_bytes;
     ep.skip_pad = cache->flags & TTKV_CACHE_SKIP_PAD;
     ep.slots = slot_mapping; ep.k = k; ep.k_dtype = k_dtype; ep.k_stride = k_stride;
@@ -741,8 +761,23 @@ extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* ca
     ep.decoders = decoders; ep.dec_stride = dec_stride; ep.n_decoders = n_decoders;
     ep.c = c; ep.coeff_q = frozen ? nullptr : coeff_q; ep.coeff_scale = frozen ? nullptr : coeff_scale;
     ep.status = status;
-    encode_pack_kernel<<<dim3(lay->H, n_tok), 128, 0, st>>>(ep);
+    encode_pack_kernel<<<dim3(h_hi - h_lo, n_tok), 128, 0, st>>>(ep);
     return check_launch("encode_pack_kernel");
+}
+
+extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                const int64_t* slot_mapping, int32_t n_tok, const void* k,
+                                int32_t k_dtype, int64_t k_stride, const void* v, int32_t v_dtype,
+                                int64_t v_stride, const int32_t* tok_dec, const float* decoders,
+                                int64_t dec_stride, const float* pinvs, int64_t pinv_stride,
+                                int32_t n_decoders, const int8_t* coeff_q, const float* coeff_scale,
+                                void* workspace, size_t workspace_bytes, int32_t* status,
+                                void* stream) {
+    if (!lay) return fail(TTKV_ERR_ARG, "layout is null");
+    return ttkv_write_paged_shard(lay, 0, lay->H, cache, slot_mapping, n_tok, k, k_dtype, k_stride, v,
+                                  v_dtype, v_stride, tok_dec, decoders, dec_stride, pinvs, pinv_stride,
+                                  n_decoders, coeff_q, coeff_scale, workspace, workspace_bytes, status,
+                                  stream);
 }
 
 extern "C" int ttkv_select_pack_rows(const ttkv_cache_t* cache, const int64_t* slots, int32_t n_tok,

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import pathlib
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 LIB_PATH = pathlib.Path(__file__).resolve().parents[1] / "libttkv_sm100.so"
 
 # host-side refusal codes (ttkv_b200.h)
@@ -71,6 +71,8 @@ SIGNATURES = {
     "ttkv_write_workspace_bytes": (SZ, [LP, I32]),
     "ttkv_write_paged": (C.c_int, [LP, CP, P, I32, P, I32, I64, P, I32, I64, P, P, I64, P, I64,
                                    I32, P, P, P, SZ, P, P]),
+    "ttkv_write_paged_shard": (C.c_int, [LP, I32, I32, CP, P, I32, P, I32, I64, P, I32, I64, P, P,
+                                         I64, P, I64, I32, P, P, P, SZ, P, P]),
     "ttkv_select_pack_rows": (C.c_int, [CP, P, I32, P, I32, I32, I32, I32, I32, I32, I32, P, P]),
     "ttkv_fit_tail_scratch_bytes": (SZ, [I32, I32, I32, I32]),
     "ttkv_fit_tail": (C.c_int, [P, P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P, P, P, P, SZ,

@@ -136,20 +136,23 @@ def fit_into_budget(K: torch.Tensor, lay: TTKLayout, cfg: dict | str) -> FittedK
 
 
 def write_fitted(cache_u8: torch.Tensor, slot_mapping: torch.Tensor, fk: FittedK, K_tok, V_tok,
-                 lay: TTKLayout, pool_index: torch.Tensor | None = None) -> None:
-    """Write a fitted chunk: K_tok / V_tok [n, H, d], slot ids [n] int64."""
+                 lay: TTKLayout, pool_index: torch.Tensor | None = None,
+                 heads: tuple[int, int] | None = None) -> None:
+    """Write a fitted chunk: K_tok / V_tok [n, H, d], slot ids [n] int64. heads: the KV heads a
+    storage-sharded cache holds (rows of `lay.shard(*heads)`)."""
     n = slot_mapping.numel()
     dec = fk.decoder.decoder_f.unsqueeze(0)
     tok_dec = torch.zeros(n, dtype=torch.int32, device=K_tok.device) if pool_index is None else pool_index
     ops.write_paged(lay, cache_u8, slot_mapping, K_tok, V_tok, tok_dec, dec,
-                    coeff_q=fk.coeff_q, coeff_scale=fk.coeff_scale)
+                    coeff_q=fk.coeff_q, coeff_scale=fk.coeff_scale, heads=heads)
 
 
 def write_frozen(cache_u8: torch.Tensor, slot_mapping: torch.Tensor, K_tok, V_tok,
                  tok_dec: torch.Tensor, decoders: torch.Tensor, pinvT: torch.Tensor,
-                 lay: TTKLayout, skip_pad: bool = False) -> None:
+                 lay: TTKLayout, skip_pad: bool = False, heads: tuple[int, int] | None = None) -> None:
     """Project every token onto its request's frozen decoder and write it (one launch for the
     whole layer): K_tok / V_tok [n, H, d]; tok_dec [n] index into the decoder pool. skip_pad:
-    padding tokens (PAD_SLOT_ID) are skipped rather than refused."""
+    padding tokens (PAD_SLOT_ID) are skipped rather than refused. heads: the KV heads a
+    storage-sharded cache holds (rows of `lay.shard(*heads)`)."""
     ops.write_paged(lay, cache_u8, slot_mapping, K_tok, V_tok, tok_dec, decoders, pinvs=pinvT,
-                    skip_pad=skip_pad)
+                    skip_pad=skip_pad, heads=heads)

@@ -13,6 +13,7 @@ each padded to `align` bytes (vllm_ttkv/layout.py:56-157). Residual and V rows a
 from __future__ import annotations
 
 import ctypes
+import dataclasses
 import math
 from dataclasses import dataclass
 
@@ -110,6 +111,18 @@ class TTKLayout:
     def ratio(self) -> float:
         return self.dense_bytes_per_token() / self.compressed_bytes_per_token()
 
+    def shard(self, h_lo: int, h_hi: int) -> "TTKLayout":
+        """The layout of a storage-sharded cache that holds only KV heads [h_lo, h_hi): the same
+        widths with H = h_hi - h_lo, i.e. the coefficient block and its ruler, then the held heads'
+        K rows (padded to `align`), then their V rows (padded). No counterpart in the reference,
+        which has no multi-GPU path; the reassembled shards are the reference's slot bytes
+        (`shard_slots` / `unshard_slots`)."""
+        if not 0 <= h_lo < h_hi <= self.H:
+            raise ValueError(f"heads [{h_lo}, {h_hi}) outside the layout's {self.H}")
+        if (h_lo, h_hi) == (0, self.H):
+            return self
+        return dataclasses.replace(self, H=h_hi - h_lo)
+
     def abi(self):
         """The `ttkv_layout_t` of this layout, validated by the library."""
         from vllm_ttkv import _lib
@@ -133,6 +146,41 @@ def layout_for_config(cfg, r1: int, H: int = 8, d: int = 128) -> TTKLayout:
     return TTKLayout(H=H, d=d, r1=r1, qbits=cfg["qbits"],
                      res_k=max(int(d * cfg["res_frac"]), 1), res_bits=cfg["res_bits"],
                      v_lanes=cfg["k_lanes"], v_bits=cfg["vbits"])
+
+
+# ---------------------------------------------------------------- the storage-sharded format
+def shard_slots(rows: torch.Tensor, lay: TTKLayout, h_lo: int, h_hi: int) -> torch.Tensor:
+    """The shard of full blobs `rows` [n, >= blob_bytes] uint8 that holds KV heads [h_lo, h_hi):
+    [n, lay.shard(h_lo, h_hi).blob_bytes], padding zero."""
+    sl = lay.shard(h_lo, h_hi)
+    head = lay.coeff_bytes + 2
+    out = torch.zeros(rows.shape[0], sl.compressed_bytes_per_token(), dtype=torch.uint8, device=rows.device)
+    out[:, :head] = rows[:, :head]
+    nk, nv = (h_hi - h_lo) * lay.k_row_bytes, (h_hi - h_lo) * lay.v_row_bytes
+    out[:, head:head + nk] = rows[:, head + h_lo * lay.k_row_bytes:head + h_hi * lay.k_row_bytes]
+    out[:, sl.v_offset:sl.v_offset + nv] = rows[:, lay.v_offset + h_lo * lay.v_row_bytes:
+                                                lay.v_offset + h_hi * lay.v_row_bytes]
+    return out
+
+
+def unshard_slots(shards, lay: TTKLayout, ranges) -> torch.Tensor:
+    """Full blobs [n, lay.blob_bytes] from shards [n, >= shard blob] holding the KV head ranges
+    `ranges` (together every head once): the coefficient block of the first shard, each head's
+    rows from the shard holding it, padding zero."""
+    covered = sorted(h for lo, hi in ranges for h in range(lo, hi))
+    if covered != list(range(lay.H)):
+        raise ValueError(f"the head ranges {list(ranges)} do not cover the {lay.H} heads exactly once")
+    head = lay.coeff_bytes + 2
+    n = shards[0].shape[0]
+    out = torch.zeros(n, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=shards[0].device)
+    out[:, :head] = shards[0][:, :head]
+    for rows, (lo, hi) in zip(shards, ranges):
+        sl = lay.shard(lo, hi)
+        nk, nv = (hi - lo) * lay.k_row_bytes, (hi - lo) * lay.v_row_bytes
+        out[:, head + lo * lay.k_row_bytes:head + hi * lay.k_row_bytes] = rows[:, head:head + nk]
+        out[:, lay.v_offset + lo * lay.v_row_bytes:lay.v_offset + hi * lay.v_row_bytes] = \
+            rows[:, sl.v_offset:sl.v_offset + nv]
+    return out
 
 
 # ---------------------------------------------------------------- the codec's row container

@@ -257,13 +257,15 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
                 v: torch.Tensor, tok_dec: torch.Tensor, decoders: torch.Tensor,
                 pinvs: torch.Tensor | None = None, coeff_q: torch.Tensor | None = None,
                 coeff_scale: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                skip_pad: bool = False):
+                skip_pad: bool = False, heads: tuple[int, int] | None = None):
     """Encode tokens k/v [n, H, d] (raw pre-RoPE K; V) into their slots.
 
     Frozen path: `pinvs` [n_dec, r1, H*d] (pinv transposed) given -> project + quantise.
     Fit path: `coeff_q` [n, r1] int8 and `coeff_scale` [n] float32 given.
     skip_pad: a negative slot (PAD_SLOT_ID, the padding of a batch padded to a captured graph's
-    size) is skipped instead of refused."""
+    size) is skipped instead of refused.
+    heads: (h_lo, h_hi) for a storage-sharded cache holding only those KV heads (rows of
+    `lay.shard(h_lo, h_hi)`); k, v, the decoders and pinvs still cover every head of `lay`."""
     _need_cuda(cache, slot_mapping, k, v, tok_dec, decoders)
     n = slot_mapping.numel()
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
@@ -281,7 +283,8 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
     L = _lib.lib()
     la = lay.abi()
     st = status if status is not None else status_word(k.device)
-    c_s = _cache_struct(lay, cache, 1, _lib.CACHE_SKIP_PAD if skip_pad else 0)
+    h_lo, h_hi = (0, lay.H) if heads is None else (int(heads[0]), int(heads[1]))
+    c_s = _cache_struct(lay.shard(h_lo, h_hi), cache, 1, _lib.CACHE_SKIP_PAD if skip_pad else 0)
     ws_n = L.ttkv_write_workspace_bytes(C.byref(la), n)
     ws = workspace(ws_n, k.device, key="write")
     if pinvs is not None:
@@ -296,8 +299,8 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
         if coeff_scale.dtype != torch.float32 or coeff_scale.numel() != n:
             raise ValueError("coeff_scale must be float32 [n]")
         pv, pv_stride, cq, cs = None, 0, coeff_q.data_ptr(), coeff_scale.contiguous().data_ptr()
-    _lib.check(L.ttkv_write_paged(
-        C.byref(la), C.byref(c_s), slot_mapping.data_ptr(), n, k.data_ptr(), dtype_code(k),
+    _lib.check(L.ttkv_write_paged_shard(
+        C.byref(la), h_lo, h_hi, C.byref(c_s), slot_mapping.data_ptr(), n, k.data_ptr(), dtype_code(k),
         _row_stride(k, "k"), v.data_ptr(), dtype_code(v), _row_stride(v, "v"), tok_dec.data_ptr(),
         decoders.data_ptr(), decoders.stride(0), pv, pv_stride, decoders.shape[0], cq, cs,
         ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))

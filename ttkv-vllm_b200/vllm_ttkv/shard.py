@@ -1,17 +1,20 @@
 """KV-head sharding of the TT-KV read across ranks (one process per GPU).
 
 The reference has no multi-GPU path; this is the build's. The read shards by KV head: after the
-coefficient block every head's rows are independent. Rank g of N:
+coefficient block every head's rows are independent. Rank g of N owns KV heads
+[g*H/N, (g+1)*H/N) and either
+* stores the storage-sharded format (`TTKLayout.shard`, `layout.shard_slots`): per token the
+  coefficient block and its own heads' rows only, written by `ttkv_write_paged_shard` and read as
+  a layout of H/N heads; or
+* holds a replica of the full blobs and reads its heads through `head_lo/head_hi` of the read ABI.
+Either way it writes its query heads [head_lo*G, head_hi*G) of each layer's output, which are
+all-gathered over the process group and reassembled in head order, so every rank ends with the
+whole output.
 
-* holds a replica of the byte-identical slot cache (the format is unchanged) and reads only its KV
-  heads [g*H/N, (g+1)*H/N) through `head_lo/head_hi` of the read ABI: the coefficient block of
-  every token plus its own heads' rows;
-* writes its query heads [head_lo*G, head_hi*G) of each layer's output, which are all-gathered over
-  the process group and reassembled in head order, so every rank ends with the whole output.
-
-The write stays replicated: every rank encodes the step's tokens into its own replica. Collectives
-go through `torch.distributed` (NCCL on GPUs, gloo in the CPU tests), with the gathered tensor
-concatenated along dim 0, the form both backends accept.
+The write's projection needs every head's K (c = M @ pinv), so every rank projects the step's
+tokens; with the sharded format it packs only its heads. Collectives go through
+`torch.distributed` (NCCL on GPUs, gloo in the CPU tests), with the gathered tensor concatenated
+along dim 0, the form both backends accept.
 """
 from __future__ import annotations
 
