@@ -4,15 +4,18 @@ Same two phases as the reference (vllm_ttkv/encode.py):
 
   * a request's FIRST chunk is fitted: TT-SVD of the [n, d, H] key block (tokens first), rank
     capped at the layer's budget and zero-padded to it (`fit_into_budget`, encode.py:257-298).
-    The two SVDs stay library calls (`torch.linalg.svd`, cuSOLVER) exactly as in the reference;
-    everything after them -- coefficient/core quantisation, the decoder contraction, the decoder's
-    own quantisation -- is `ops.fit_tail`, and the residual + V packing into the slots is
-    `ops.write_paged` (fit path).
+    The two decompositions stay library calls: `torch.linalg.svd` as in the reference, or, for a
+    long chunk, the same subspaces from the eigendecomposition of the unfolding's Gram matrix
+    (cuBLAS + cuSOLVER `eigh`, 7x faster at 16k tokens; `VLLM_TTKV_FIT`). Everything after them --
+    coefficient/core quantisation, the decoder contraction, the decoder's own quantisation -- is
+    `ops.fit_tail`, and the residual + V packing into the slots is `ops.write_paged` (fit path).
   * every later token is PROJECTED onto the request's frozen decoder (`encode_frozen`,
     encode.py:301-351): one `ops.write_paged` launch pair per layer for all requests, instead of
     ~20 torch launches per request.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -105,18 +108,58 @@ def _rank_from_spectrum(S: torch.Tensor, tol: float, cap: int | None) -> int:
     return r if cap is None else max(1, min(r, cap))
 
 
-def tt_svd_cores(K: torch.Tensor, tol: float, max_rank: int | None):
+FIT_ENV = "VLLM_TTKV_FIT"                 # "svd" | "gram" | "auto" (default)
+
+
+def _svd_tall(X: torch.Tensor, method: str):
+    """(S, Vh, U_of(r)) of a tall X [m, c]: the thin SVD's singular values (descending), right
+    singular vectors, and a function giving the first r left singular vectors.
+
+    "svd": torch.linalg.svd, as the reference (codec/ttkv_codec.py:96).
+    "gram": the eigendecomposition of X^T X [c, c] (one GEMM and a c x c eigh): S = sqrt(lambda),
+    Vh = the eigenvectors, U_r = X V_r / S_r. The same subspaces and singular values to fp32
+    rounding of the Gram matrix; for the first unfolding of a 16384-token fit ([16384, 1024]) it
+    took 12 ms on a B200 against 87 ms for the SVD. A direction with S = 0 gets a zero column."""
+    if method == "svd":
+        U, S, Vh = torch.linalg.svd(X, full_matrices=False)
+        return S, Vh, lambda r: U[:, :r]
+    lam, V = torch.linalg.eigh(X.T @ X)
+    lam, V = lam.flip(0).clamp_min(0), V.flip(1)
+    S = lam.sqrt()
+    tiny = S.max() * 1e-7 if S.numel() else 0.0
+
+    def left(r):
+        inv = torch.where(S[:r] > tiny, 1.0 / S[:r].clamp_min(1e-30), torch.zeros_like(S[:r]))
+        return (X @ V[:, :r]) * inv
+    return S, V.T, left
+
+
+def fit_method(n: int, width: int) -> str:
+    """The first unfolding's decomposition: VLLM_TTKV_FIT, else "gram" once the unfolding has at
+    least twice as many rows (tokens) as columns, where the Gram matrix is the cheaper route."""
+    m = os.environ.get(FIT_ENV, "auto")
+    if m not in ("svd", "gram", "auto"):
+        raise ValueError(f"{FIT_ENV}={m!r}: expected svd, gram or auto")
+    if m == "auto":
+        return "gram" if n >= 2 * width else "svd"
+    return m
+
+
+def tt_svd_cores(K: torch.Tensor, tol: float, max_rank: int | None, method: str | None = None):
     """TT-SVD of K [H, n, d] with tokens first ([n, d, H]): returns G1 [n, r], G2 [r, d, r2],
-    G3 [r2, H] (codec/ttkv_codec.py:78-109 with the cores squeezed)."""
+    G3 [r2, H] (codec/ttkv_codec.py:78-109 with the cores squeezed). `method` ("svd" or "gram",
+    default `fit_method`) decomposes the first unfolding; the second, [r*d, H], always by Gram
+    (H columns) unless "svd" is asked for."""
     H, n, d = K.shape
     X = K.permute(1, 2, 0).reshape(n, d * H).float()
-    U, S, Vh = torch.linalg.svd(X, full_matrices=False)
+    method = fit_method(n, d * H) if method is None else method
+    S, Vh, left = _svd_tall(X, method)
     r = _rank_from_spectrum(S, tol, max_rank)
-    G1 = U[:, :r].contiguous()
+    G1 = left(r).contiguous()
     rest = (S[:r].unsqueeze(1) * Vh[:r, :]).reshape(r * d, H)
-    U2, S2, Vh2 = torch.linalg.svd(rest, full_matrices=False)
+    S2, Vh2, left2 = _svd_tall(rest, "svd" if method == "svd" or r * d < 2 * H else "gram")
     r2 = _rank_from_spectrum(S2, tol, None)
-    G2 = U2[:, :r2].reshape(r, d, r2).contiguous()
+    G2 = left2(r2).reshape(r, d, r2).contiguous()
     G3 = (S2[:r2].unsqueeze(1) * Vh2[:r2, :]).contiguous()
     return G1, G2, G3
 
