@@ -149,14 +149,21 @@ class Workload:
         self.k_new, self.v_new, self.q, self.out = [], [], [], []
         self.fit_s = 0.0
         self.dec_index = torch.arange(B, dtype=torch.int32, device=device)
+        # every layer's step inputs (q, the new token's K and V) in one device buffer and every
+        # layer's output in another, so a step's host transfers are one copy each way
+        per_in = B * (HQ + 2 * H) * 128
+        self.inbuf = torch.empty(self.L * per_in, dtype=dtype, device=device)
+        self.outbuf = torch.empty(self.L * B * HQ * 128, dtype=dtype, device=device)
         for l, r1 in enumerate(self.r1s):
             lay = layout_for_config(cfg, r1, H=H)
             cache = torch.zeros(self.n_slots, lay.compressed_bytes_per_token(), dtype=torch.uint8,
                                 device=device)
             dec = torch.zeros(B, r1, H * 128, device=device)
             pinvT = torch.zeros(B, r1, H * 128, device=device)
-            kn = torch.empty(B, H, 128, dtype=dtype, device=device)
-            vn = torch.empty(B, H, 128, dtype=dtype, device=device)
+            base = l * per_in
+            qv = self.inbuf[base:base + B * HQ * 128].view(B, HQ, 128)
+            kn = self.inbuf[base + B * HQ * 128:base + B * (HQ + H) * 128].view(B, H, 128)
+            vn = self.inbuf[base + B * (HQ + H) * 128:base + per_in].view(B, H, 128)
             for r in range(B):
                 K, V = synth_kv_device(gen, H, seq, dtype=dtype)
                 t0 = time.perf_counter()
@@ -177,8 +184,9 @@ class Workload:
             self.pinvT.append(pinvT)
             self.k_new.append(kn)
             self.v_new.append(vn)
-            self.q.append(torch.randn(B, HQ, 128, generator=gen, device=device).to(dtype))
-            self.out.append(torch.empty(B, HQ, 128, dtype=dtype, device=device))
+            qv.copy_(torch.randn(B, HQ, 128, generator=gen, device=device))
+            self.q.append(qv)
+            self.out.append(self.outbuf[l * B * HQ * 128:(l + 1) * B * HQ * 128].view(B, HQ, 128))
         self.heads = (0, H)
         self.read_layouts = list(self.layouts)
         self.read_dec = list(self.decoders)
@@ -239,8 +247,8 @@ class Workload:
 # ---------------------------------------------------------------------------- plugin e2e
 def plugin_e2e(wl, steps, warmup, device, graph=False):
     """The step through the reference-facing plugin, `TTKVAttentionImpl.forward`, once per layer:
-    the raw key handed over by the rotary capture's stash, q/k/v copied in from pinned host memory
-    and every layer's output copied back.
+    the raw key handed over by the rotary capture's stash; every layer's q/k/v copied in from
+    pinned host memory (one copy) and every layer's output copied back (one copy).
 
     eager: one new metadata object (and host-read step plan) per step, forward per layer.
     graph: the 28 forward calls captured once in one CUDA graph (the device-planned decode step:
@@ -266,12 +274,10 @@ def plugin_e2e(wl, steps, warmup, device, graph=False):
             rope_store.register_decoder(layer.layer_name, keys[r], kd, lay=lay)
         page = wl.caches[l].view(-1, 1, wl.bs, wl.caches[l].shape[1])
         layers.append((layer, page))
-    pin_q = [x.cpu().pin_memory() for x in wl.q]
-    pin_k = [x.cpu().pin_memory() for x in wl.k_new]
-    pin_v = [x.cpu().pin_memory() for x in wl.v_new]
-    pin_o = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in wl.out]
-    h2d = sum(x.numel() * x.element_size() for x in pin_q + pin_k + pin_v)
-    d2h = sum(x.numel() * x.element_size() for x in pin_o)
+    pin_in = wl.inbuf.cpu().pin_memory()                 # every layer's q, K, V of the step
+    pin_o = torch.empty(wl.outbuf.shape, dtype=wl.outbuf.dtype).pin_memory()
+    h2d = pin_in.numel() * pin_in.element_size()
+    d2h = pin_o.numel() * pin_o.element_size()
     qsl_cpu = torch.arange(wl.B + 1, dtype=torch.int32)
     qsl = qsl_cpu.to(device)
 
@@ -285,11 +291,6 @@ def plugin_e2e(wl, steps, warmup, device, graph=False):
         layer, page = layers[l]
         patch.stash_raw_k(layer.layer_name, wl.k_new[l], None, wl.table)
         impl.forward(layer, wl.q[l], None, wl.v_new[l], page, md, wl.out[l])
-
-    def copy_in(l):
-        wl.q[l].copy_(pin_q[l], non_blocking=True)
-        wl.k_new[l].copy_(pin_k[l], non_blocking=True)
-        wl.v_new[l].copy_(pin_v[l], non_blocking=True)
 
     if graph:
         md = new_md()
@@ -307,18 +308,16 @@ def plugin_e2e(wl, steps, warmup, device, graph=False):
                 forward(l, md)
 
         def step():
-            for l in range(wl.L):
-                copy_in(l)
+            wl.inbuf.copy_(pin_in, non_blocking=True)
             g.replay()
-            for l in range(wl.L):
-                pin_o[l].copy_(wl.out[l], non_blocking=True)
+            pin_o.copy_(wl.outbuf, non_blocking=True)
     else:
         def step():
             md = new_md()
+            wl.inbuf.copy_(pin_in, non_blocking=True)
             for l in range(wl.L):
-                copy_in(l)
                 forward(l, md)
-                pin_o[l].copy_(wl.out[l], non_blocking=True)
+            pin_o.copy_(wl.outbuf, non_blocking=True)
 
     for _ in range(warmup):
         step()
@@ -724,6 +723,9 @@ def main():
 
     def run_steps(k):
         for _ in range(k):
+            if graphs is not None and sh is None:
+                graphs[0].replay()                         # the whole step
+                continue
             for l in range(wl.L):
                 if graphs is not None:
                     graphs[l].replay()
@@ -735,14 +737,16 @@ def main():
 
     run_steps(args.warmup)
     if not args.no_graph:
-        # one CUDA graph per layer, captured after the warm-up allocated every workspace; the
-        # replays launch exactly the kernels the eager layer launches
+        # CUDA graphs captured after the warm-up allocated every workspace; the replays launch
+        # exactly the kernels the eager layers launch. One graph for the whole step on one GPU;
+        # one per layer on several, with each layer's all-gather between the replays
         torch.cuda.synchronize(device)
         graphs = []
-        for l in range(wl.L):
+        for l in range(wl.L if sh is not None else 1):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                layer_work(l)
+                for ll in ([l] if sh is not None else range(wl.L)):
+                    layer_work(ll)
             graphs.append(g)
         torch.cuda.synchronize(device)
     run_steps(args.warmup)
@@ -791,22 +795,17 @@ def main():
     recon_flops = sum(wl.B * wl.max_seq * 2 * wl.r1s[l] * n_heads * 128 for l in range(wl.L))
     hbm, tc, peak_kind = _peaks()
 
-    # ---- e2e: the same step through the C-ABI with host buffers copied in and out every step
-    pin_q = [x.cpu().pin_memory() for x in wl.q]
-    pin_k = [x.cpu().pin_memory() for x in wl.k_new]
-    pin_v = [x.cpu().pin_memory() for x in wl.v_new]
-    pin_o = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in wl.out]
-    h2d = sum(x.numel() * x.element_size() for x in pin_q + pin_k + pin_v)
-    d2h = sum(x.numel() * x.element_size() for x in pin_o)
+    # ---- e2e: the same step through the C-ABI with host buffers copied in and out every step:
+    # every layer's q, K and V of the step in one pinned buffer, every layer's output back in one
+    pin_in = wl.inbuf.cpu().pin_memory()
+    pin_o = torch.empty(wl.outbuf.shape, dtype=wl.outbuf.dtype).pin_memory()
+    h2d = pin_in.numel() * pin_in.element_size()
+    d2h = pin_o.numel() * pin_o.element_size()
 
     def e2e_step():
-        for l in range(wl.L):
-            wl.q[l].copy_(pin_q[l], non_blocking=True)
-            wl.k_new[l].copy_(pin_k[l], non_blocking=True)
-            wl.v_new[l].copy_(pin_v[l], non_blocking=True)
+        wl.inbuf.copy_(pin_in, non_blocking=True)
         run_steps(1)
-        for l in range(wl.L):
-            pin_o[l].copy_(wl.out[l], non_blocking=True)
+        pin_o.copy_(wl.outbuf, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -868,7 +867,8 @@ def main():
                                                           for l in range(wl.L)),
                            "storage": ("storage-sharded: coefficient block + this rank's heads' rows"
                                        if world > 1 else "full blobs"),
-                           "launch": "one CUDA graph per layer (write + read)" if graphs else "eager"},
+                           "launch": ("eager" if not graphs else "one CUDA graph per step" if sh is None
+                                      else "one CUDA graph per layer (write + read), all-gathers between"),},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                              "kernel": "decode_tc_kernel<3> + merge_kernel (ttkv_decode_paged)",
