@@ -37,8 +37,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for an mbarrier phase: false after ~2 s.
+// Bounded wait for an mbarrier phase: false after ~2 s. The clock is read only when the first
+// test finds the phase still open.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity))
         if (clock64() - t0 > kWaitCycles) return false;
