@@ -643,6 +643,58 @@ def run_sweep(args):
     print(json.dumps(line))
 
 
+def run_dense(args):
+    """The dense comparator of configs 1 and 2: the same decode steps over a bf16 KV cache (4096 B
+    per token per layer, what stock vLLM stores), read by torch's scaled_dot_product_attention (a
+    library kernel, GQA) -- no TT-KV code. For each (batch, context) point of the sweep, one step =
+    28 layers of one query token per request attending over [B, 8, n, 128] K and V, replayed from
+    one CUDA graph. Reports each point's step time and its KV read rate."""
+    import torch
+    import torch.nn.functional as F
+    device = torch.device("cuda", 0)
+    ctxs = [int(x) for x in args.sweep_ctx.split(",")]
+    batches = [int(x) for x in args.sweep_batch.split(",")]
+    L, H, HQ, d = args.layers, 8, 24, 128
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    hbm, tc, peak_kind = _peaks()
+    points = []
+    for B in batches:
+        for n in ctxs:
+            k = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+            v = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+            q = [torch.randn(B, HQ, 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+            out = [None] * L
+
+            def step():
+                for l in range(L):
+                    out[l] = F.scaled_dot_product_attention(q[l], k[l], v[l], scale=d ** -0.5, enable_gqa=True)
+
+            step()
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            ms = _event_ms(g.replay, args.steps, args.warmup)
+            del g
+            kv = L * B * (n + 1) * H * d * 2 * 2
+            points.append({"batch": B, "ctx": n, "ms_per_step": ms, "tok_s": B / (ms * 1e-3),
+                           "kv_gbs": kv / (ms * 1e-3) / 1e9})
+            del k, v, q, out
+            torch.cuda.empty_cache()
+    top = max(points, key=lambda p: p["kv_gbs"])
+    line = {"metric": "dense bf16 decode step (comparator, torch SDPA)", "value": top["tok_s"],
+            "unit": "tok/s (best point)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "workload": "dense", "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"dense KV comparator: ctx {ctxs} x batch {batches}, {L} layers, "
+                                   f"24q/8kv heads, torch.nn.functional.scaled_dot_product_attention, "
+                                   f"one CUDA graph per step", "kv_bytes_per_token_per_layer": 4096},
+            "points": points,
+            "roofline": {"bound": "hbm", "achieved": top["kv_gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": top["kv_gbs"] / hbm, "peak_kind": peak_kind}}
+    print(json.dumps(line))
+
+
 # ---------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -657,9 +709,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying per-layer CUDA graphs")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "encode", "sweep"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "encode", "sweep", "dense"],
                     help="decode: config 1 (the default line); sweep: config 2; prefill: config 3; "
-                         "encode: config 4")
+                         "encode: config 4; dense: the bf16-KV comparator of configs 1 and 2")
     ap.add_argument("--sweep-ctx", default="1082,4322,8642,14402", help="sweep: cached tokens")
     ap.add_argument("--sweep-batch", default="1,8,32,64", help="sweep: batch sizes")
     ap.add_argument("--prompt-len", type=int, default=None,
@@ -668,6 +721,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "dense":
+        if args.steps == 200:
+            args.steps = 20
+        run_dense(args)
+        return
     if args.workload == "sweep":
         if args.cfg == "safe" and "--cfg" not in sys.argv:
             args.cfg = "campaign4x"                 # config 2 is quoted at 4-bit storage
