@@ -183,6 +183,33 @@ def test_continuation_matches_oracle_causal():
         assert err < 1e-4, (r, err)
 
 
+@pytest.mark.parametrize("HQ,block_size", [(56, 16), (24, 1), (8, 16)])
+def test_continuation_other_groups_and_block_sizes(HQ, block_size):
+    """G = 7 takes the fp32 continuation kernel (blocks of queries would not fit the decode's 8
+    rows); one token per block sizes the workspace beyond the default plan's, so the fp32 kernel
+    serves unless the workspace holds the tensor-core plan; G = 1 takes blocks of 8 queries."""
+    from vllm_ttkv import ops
+    st = stores.make_store(17, [90, 50], cfg="safe", r1=32, HQ=HQ, block_size=block_size)
+    q_lens = [20, 3]
+    rng = np.random.default_rng(3)
+    qs = [rng.standard_normal((HQ, ql, 128)).astype(np.float16).astype(np.float32) for ql in q_lens]
+    d = _dev(st)
+    flat = np.ascontiguousarray(np.concatenate([q.transpose(1, 0, 2) for q in qs]))
+    qt = torch.from_numpy(flat).cuda().to(torch.float16)
+    start = np.concatenate([[0], np.cumsum(q_lens)[:-1]]).astype(np.int32)
+    out = torch.zeros(qt.shape, dtype=torch.float32, device="cuda")
+    ops.reset_status()
+    ops.prefill_cont_paged(d["lay"], d["cache"], block_size, d["bt"], d["seq"], d["dec"], d["idx"],
+                           d["table"], torch.from_numpy(start).cuda(),
+                           torch.tensor(q_lens, dtype=torch.int32, device="cuda"), qt, 128 ** -0.5,
+                           out, max(q_lens), int(st["seq_lens"].max()))
+    ops.check_status()
+    got = out.cpu().numpy()
+    for r, ql in enumerate(q_lens):
+        want = stores.expected_continuation(st, r, qs[r])
+        assert np.abs(got[start[r]:start[r] + ql].transpose(1, 0, 2) - want).max() < 1e-4, (HQ, r)
+
+
 def test_continuation_with_one_query_equals_decode():
     from vllm_ttkv import ops
     st = stores.make_store(9, [77, 12], cfg="safe", r1=32)

@@ -278,6 +278,7 @@ struct TcMisc {
     long long sched_before;
     long long sched_T, sched_nv, sched_hi;   // the batch's units, virtual shares, this CTA's end
     long long seg_slot;                      // the current segment's partial slot
+    int lim[kMaxG];                          // row g sees the segment's rows before lim[g]
     uint64_t mb_r, mb_pv, mb_cf, mb_rp, mb_kv[2], mb_dec;
     uint32_t tmem_base;
 };
@@ -597,13 +598,15 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const int h = P.head_lo + hl;
 
         // ---- the cheap refusals (uniform); the block ids are checked as the set-up loads them
-        const int di = P.dec_index[r];
+        // a continuation launch's request r is a block of queries of stored request rq
+        const int rq = P.v_req ? P.v_req[r] : r;
+        const int di = P.dec_index[rq];
         bool bad = false;
         if (seq > P.max_seq) { if (tid == 0) report(P.status, TTKV_STATUS_SEQ_BOUND); bad = true; }
         if (!bad && (di < 0 || di >= P.n_decoders)) { if (tid == 0) report(P.status, TTKV_STATUS_DECODER); bad = true; }
         const int blocks_needed = (seq + P.block_size - 1) / P.block_size;
         if (!bad && blocks_needed > P.bt_cols) { if (tid == 0) report(P.status, TTKV_STATUS_ROW_SHORT); bad = true; }
-        const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
+        const int32_t* brow = P.block_table + int64_t(rq) * P.bt_stride;
         if (!bad && (t_end - 1) / P.block_size - t_begin / P.block_size + 1 > BT_CAP) {
             if (tid == 0) report(P.status, TTKV_STATUS_ROW_SHORT);   // the plan keeps a segment within BT_CAP blocks
             bad = true;
@@ -682,10 +685,29 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             for (int i = tid; i < G * 128; i += NTHR) {
                 const int g = i >> 7, j = i & 127;
                 const int qi = (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1);
-                qs[qi] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
+                float qv = 0.f;
+                if (!P.v_req) {
+                    qv = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
+                } else {                                 // row g = (query jq, head gh) of the block
+                    const int jq = g / P.g_real, gh = g - jq * P.g_real;
+                    if (jq < P.v_nq[r])
+                        qv = load_elt(P.q, P.q_dtype, int64_t(P.v_qrow[r] + jq) * P.q_stride +
+                                                      int64_t(h * P.g_real + gh) * 128 + j);
+                }
+                qs[qi] = qv;
             }
         }
-        if (tid < kMaxG) { M->m[tid] = -INFINITY; M->l[tid] = 0.f; }
+        if (tid < kMaxG) {
+            M->m[tid] = -INFINITY;
+            M->l[tid] = 0.f;
+            // causal rows of a continuation block: query jq sees positions <= v_pos + jq
+            int lim = 0x7fffffff;
+            if (P.v_req) {
+                const int jq = tid / P.g_real;
+                lim = jq < P.v_nq[r] ? P.v_pos[r] + jq + 1 : 0;
+            }
+            M->lim[tid] = lim;
+        }
         if (__syncthreads_or(local_bad)) {                 // block-table slice cached and checked
             if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
             bad = true;
@@ -1012,7 +1034,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                         #pragma unroll
                         for (int c = 0; c < NWG; ++c) v += tmem_ld1(t_row + RED_COL + uint32_t(8 * c + g));
                         tmem_wait_ld();
-                        sc[i] = valid ? v * scale : -INFINITY;
+                        sc[i] = (valid && tok < M->lim[g]) ? v * scale : -INFINITY;
                         const float mxg = warp_max(sc[i]);
                         if (lane == 0) M->red_max[w & 3][g] = mxg;
                     }
@@ -1202,8 +1224,40 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
         }
         v = den > 0.f ? acc / den : 0.f;
     }
-    const int head_q = (P.head_lo + hl) * P.G + g;
-    store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
+    if (!P.v_req) {
+        const int head_q = (P.head_lo + hl) * P.G + g;
+        store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
+    } else {                                                   // row g = (query jq, head gh)
+        const int jq = g / P.g_real, gh = g - jq * P.g_real;
+        if (jq < P.v_nq[r])
+            store_elt(P.out, P.out_dtype, int64_t(P.v_qrow[r] + jq) * P.out_stride +
+                                          int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
+    }
+}
+
+// The query blocks of a continuation launch (ttkv_prefill_cont_paged on the tensor-core decode):
+// block v = (stored request v / nqb, queries [b*cq, b*cq + cq) with b = v % nqb). Its row count
+// (the positions its last query sees), stored request, first query row, query count and first
+// position; a block past its request's queries gets no rows. Refuses q_len > seq_len.
+__global__ void cont_blocks_kernel(const int32_t* seq_lens, const int32_t* q_start, const int32_t* q_len,
+                                   int n_reqs, int nqb, int cq, int32_t* v_seq, int32_t* v_req,
+                                   int32_t* v_qrow, int32_t* v_nq, int32_t* v_pos, int32_t* status) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= n_reqs * nqb) return;
+    const int r = v / nqb, j0 = (v - r * nqb) * cq;
+    const int seq = seq_lens[r], ql = q_len[r];
+    int nq = min(cq, ql - j0);
+    if (ql < 0 || ql > seq) {
+        if (j0 == 0) report(status, TTKV_STATUS_QUERY);
+        nq = 0;
+    }
+    nq = max(nq, 0);
+    const int pos = seq - ql + j0;
+    v_seq[v] = nq > 0 ? pos + nq : 0;
+    v_req[v] = r;
+    v_qrow[v] = q_start[r] + j0;
+    v_nq[v] = nq;
+    v_pos[v] = pos;
 }
 
 // The decoders' operand images (ttkv_decoder_image): grid (decoders, KV heads), thread t = column
