@@ -444,6 +444,7 @@ def run_prefill(args):
         Ks.append(K.permute(1, 0, 2).contiguous())
         Vs.append(V.permute(1, 0, 2).contiguous())
     table = torch.from_numpy(synthetic.cos_sin_cache(N + 16, dtype="float32")).to(device).half()
+    images = ops.decoder_image(lay, dec)                       # made once per decoder, as the pool does
     q = torch.randn(B * Q, HQ, 128, generator=gen, device=device).half()
     out = torch.empty_like(q)
     idx = torch.arange(B, dtype=torch.int32, device=device)
@@ -460,7 +461,7 @@ def run_prefill(args):
         for c in chunks:
             encode.write_frozen(cache, c["slots"], c["k"], c["v"], c["tok"], dec, pinvT, lay)
             ops.prefill_cont_paged(lay, cache, bs, bt, c["seq"], dec, idx, table, c["q_start"], c["q_len"],
-                                   q, 128 ** -0.5, out, c["ql"], c["e"])
+                                   q, 128 ** -0.5, out, c["ql"], c["e"], images=images)
 
     ms = _event_ms(step, args.steps, args.warmup)
     # the continuation launches alone, on the launching stream
@@ -469,7 +470,7 @@ def run_prefill(args):
     for (a, b), c in zip(evs, chunks):
         a.record()
         ops.prefill_cont_paged(lay, cache, bs, bt, c["seq"], dec, idx, table, c["q_start"], c["q_len"],
-                               q, 128 ** -0.5, out, c["ql"], c["e"])
+                               q, 128 ** -0.5, out, c["ql"], c["e"], images=images)
         b.record()
     torch.cuda.synchronize()
     read_ms = sum(a.elapsed_time(b) for a, b in evs)

@@ -309,3 +309,31 @@ def test_decode_of_a_storage_shard_matches_the_full_decode_on_its_heads():
                          images=ops.decoder_image(lay, dec))
         ops.check_status()
         assert np.abs(out.cpu().numpy() - full[:, lo * G:hi * G]).max() < 1e-5, (lo, hi)
+
+
+def test_continuation_with_decoder_images_gives_the_same_bits():
+    """The tensor-core continuation stages a decoder image instead of converting the fp32 decoder:
+    the same operand, so the same outputs bit for bit."""
+    from vllm_ttkv import ops
+    st = stores.make_store(18, [140, 60], cfg="safe", r1=110)
+    q_lens = [33, 4]
+    rng = np.random.default_rng(4)
+    qs = [rng.standard_normal((24, ql, 128)).astype(np.float16).astype(np.float32) for ql in q_lens]
+    d = _dev(st)
+    qt = torch.from_numpy(np.ascontiguousarray(np.concatenate([q.transpose(1, 0, 2) for q in qs]))).cuda().half()
+    start = torch.tensor([0, q_lens[0]], dtype=torch.int32, device="cuda")
+    ql = torch.tensor(q_lens, dtype=torch.int32, device="cuda")
+    outs = []
+    for images in (None, ops.decoder_image(d["lay"], d["dec"])):
+        out = torch.zeros(qt.shape, dtype=torch.float32, device="cuda")
+        ops.reset_status()
+        ops.prefill_cont_paged(d["lay"], d["cache"], 16, d["bt"], d["seq"], d["dec"], d["idx"], d["table"],
+                               start, ql, qt, 128 ** -0.5, out, max(q_lens), int(st["seq_lens"].max()),
+                               images=images)
+        ops.check_status()
+        outs.append(out.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+    for r, n in enumerate(q_lens):
+        want = stores.expected_continuation(st, r, qs[r])
+        s0 = int(start[r])
+        assert np.abs(outs[1][s0:s0 + n].transpose(1, 0, 2) - want).max() < 1e-4

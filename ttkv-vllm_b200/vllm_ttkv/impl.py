@@ -400,7 +400,7 @@ class TTKVAttentionImpl(_ImplBase):
                                torch.tensor(rows, dtype=torch.int32, device=dev),
                                self._device_table(table, query), q_start, q_len, query, self.scale,
                                output, max(plan.qsl[r + 1] - plan.qsl[r] for r in cont),
-                               max(plan.seq_lens[r] for r in cont))
+                               max(plan.seq_lens[r] for r in cont), images=pool.images)
 
     # ------------------------------------------------------------------ resolution and guards
     @staticmethod

@@ -226,9 +226,10 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
                        dec_index: torch.Tensor, table: torch.Tensor, q_start: torch.Tensor,
                        q_len: torch.Tensor, q: torch.Tensor, scale: float, out: torch.Tensor,
                        max_q_len: int, max_seq_len: int, head_lo: int = 0,
-                       head_hi: int | None = None, status: torch.Tensor | None = None):
+                       head_hi: int | None = None, status: torch.Tensor | None = None, images=None):
     """Continuation read: request r's queries are rows q_start[r] .. +q_len[r] of q [N, HQ, d],
-    at positions seq_len - q_len + j, causal over the stored rows."""
+    at positions seq_len - q_len + j, causal over the stored rows. `images`: the pool's
+    (image, scales) from `decoder_image`, staged by the tensor-core path instead of converting."""
     _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q_start, q_len, q, out)
     head_hi = lay.H if head_hi is None else head_hi
     N, HQ, d = q.shape
@@ -243,7 +244,7 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
     ws = workspace(ws_n, q.device)
     st = status if status is not None else status_word(q.device)
     c_s = _cache_struct(lay, cache, block_size)
-    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index)
+    b_s = _batch_struct(block_table, seq_lens, decoders, dec_index, images)
     r_s = _rope_struct(table)
     _lib.check(L.ttkv_prefill_cont_paged(
         C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q_start.data_ptr(), q_len.data_ptr(),
