@@ -463,7 +463,12 @@ def run_prefill(args):
             ops.prefill_cont_paged(lay, cache, bs, bt, c["seq"], dec, idx, table, c["q_start"], c["q_len"],
                                    q, 128 ** -0.5, out, c["ql"], c["e"], images=images)
 
-    ms = _event_ms(step, args.steps, args.warmup)
+    for _ in range(args.warmup):                               # a profiler run with
+        step()                                                 # --profile-from-start off sees
+    torch.cuda.synchronize()                                   # the timed steps only
+    torch.cuda.cudart().cudaProfilerStart()
+    ms = _event_ms(step, args.steps, 0)
+    torch.cuda.cudart().cudaProfilerStop()
     # the continuation launches alone, on the launching stream
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in chunks]
     torch.cuda.synchronize()
