@@ -201,10 +201,10 @@ int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cach
  * Replaces vllm_ttkv/impl.py:725-778 (_prefill_continuation: krt_multi_from_slots
  * krt_triton.py:269-317, softmax, v_out_multi_from_slots v_out_triton.py:249-294), without
  * materialising the [HQ, Q, n] scores. Outputs at out + (q_start[r] + j)*out_stride.
- * With HQ/H <= 4 and a layout the tensor-core decode serves, the chunks run on it: each block of
- * 8/(HQ/H) consecutive queries is one decode request whose rows are (query, query head) pairs.
- * ttkv_prefill_workspace_bytes sizes the workspace for that plan with caches of 16 tokens per
- * block (for smaller blocks a workspace below the plan's needs makes the call use the fp32
+ * For a layout the tensor-core decode serves, the chunks run on it: a request's (query, query
+ * head) rows, query-major, in blocks of 8, each block one decode request with a causal limit per
+ * row. ttkv_prefill_workspace_bytes sizes the workspace for that plan with caches of 16 tokens
+ * per block (for smaller blocks a workspace below the plan's needs makes the call use the fp32
  * kernel instead). */
 size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
                                     int32_t max_q_len, int32_t max_seq_len,

@@ -183,13 +183,14 @@ def test_continuation_matches_oracle_causal():
         assert err < 1e-4, (r, err)
 
 
-@pytest.mark.parametrize("HQ,block_size", [(56, 16), (24, 1), (8, 16)])
-def test_continuation_other_groups_and_block_sizes(HQ, block_size):
-    """G = 7 takes the fp32 continuation kernel (blocks of queries would not fit the decode's 8
-    rows); one token per block sizes the workspace beyond the default plan's, so the fp32 kernel
-    serves unless the workspace holds the tensor-core plan; G = 1 takes blocks of 8 queries."""
+@pytest.mark.parametrize("HQ,block_size,r1", [(56, 16, 32), (24, 1, 32), (8, 16, 32), (24, 16, 200)])
+def test_continuation_other_groups_block_sizes_and_ranks(HQ, block_size, r1):
+    """Blocks of 8 (query, head) rows on the tensor-core decode for G = 7 (a block ends inside a
+    query) and G = 1 (8 queries per block); one token per block sizes the plan beyond the default
+    workspace, so the fp32 kernel serves unless the workspace holds it; r1 = 200 is beyond the
+    tensor-core decode and takes the fp32 kernel."""
     from vllm_ttkv import ops
-    st = stores.make_store(17, [90, 50], cfg="safe", r1=32, HQ=HQ, block_size=block_size)
+    st = stores.make_store(17, [90, 50], cfg="safe", r1=r1, HQ=HQ, block_size=block_size)
     q_lens = [20, 3]
     rng = np.random.default_rng(3)
     qs = [rng.standard_normal((HQ, ql, 128)).astype(np.float16).astype(np.float32) for ql in q_lens]

@@ -688,11 +688,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 float qv = 0.f;
                 if (!P.v_req) {
                     qv = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
-                } else {                                 // row g = (query jq, head gh) of the block
-                    const int jq = g / P.g_real, gh = g - jq * P.g_real;
-                    if (jq < P.v_nq[r])
-                        qv = load_elt(P.q, P.q_dtype, int64_t(P.v_qrow[r] + jq) * P.q_stride +
-                                                      int64_t(h * P.g_real + gh) * 128 + j);
+                } else if (g < P.v_nq[r]) {              // row g = (query jq, head gh) of the block
+                    const int f = P.v_f0[r] + g, jq = f / P.g_real, gh = f - jq * P.g_real;
+                    qv = load_elt(P.q, P.q_dtype, int64_t(P.v_qrow[r] + jq) * P.q_stride +
+                                                  int64_t(h * P.g_real + gh) * 128 + j);
                 }
                 qs[qi] = qv;
             }
@@ -702,10 +701,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             M->l[tid] = 0.f;
             // causal rows of a continuation block: query jq sees positions <= v_pos + jq
             int lim = 0x7fffffff;
-            if (P.v_req) {
-                const int jq = tid / P.g_real;
-                lim = jq < P.v_nq[r] ? P.v_pos[r] + jq + 1 : 0;
-            }
+            if (P.v_req) lim = tid < P.v_nq[r] ? P.v_pos[r] + (P.v_f0[r] + tid) / P.g_real + 1 : 0;
             M->lim[tid] = lim;
         }
         if (__syncthreads_or(local_bad)) {                 // block-table slice cached and checked
@@ -1227,37 +1223,40 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     if (!P.v_req) {
         const int head_q = (P.head_lo + hl) * P.G + g;
         store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
-    } else {                                                   // row g = (query jq, head gh)
-        const int jq = g / P.g_real, gh = g - jq * P.g_real;
-        if (jq < P.v_nq[r])
-            store_elt(P.out, P.out_dtype, int64_t(P.v_qrow[r] + jq) * P.out_stride +
-                                          int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
+    } else if (g < P.v_nq[r]) {                                // row g = (query jq, head gh)
+        const int f = P.v_f0[r] + g, jq = f / P.g_real, gh = f - jq * P.g_real;
+        store_elt(P.out, P.out_dtype, int64_t(P.v_qrow[r] + jq) * P.out_stride +
+                                      int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
     }
 }
 
-// The query blocks of a continuation launch (ttkv_prefill_cont_paged on the tensor-core decode):
-// block v = (stored request v / nqb, queries [b*cq, b*cq + cq) with b = v % nqb). Its row count
-// (the positions its last query sees), stored request, first query row, query count and first
-// position; a block past its request's queries gets no rows. Refuses q_len > seq_len.
+// The row blocks of a continuation launch (ttkv_prefill_cont_paged on the tensor-core decode):
+// request r's chunk has q_len * G (query, query head) rows, query-major; block v = (request
+// v / nqb, rows [b * rows, b * rows + rows) with b = v % nqb). Per block: the positions its last
+// query sees (its row count for the schedule), its request, the request's first query row, its
+// number of rows, the position of the request's first query and its first row; a block past
+// the request's rows gets none. Refuses q_len > seq_len.
 __global__ void cont_blocks_kernel(const int32_t* seq_lens, const int32_t* q_start, const int32_t* q_len,
-                                   int n_reqs, int nqb, int cq, int32_t* v_seq, int32_t* v_req,
-                                   int32_t* v_qrow, int32_t* v_nq, int32_t* v_pos, int32_t* status) {
+                                   int n_reqs, int nqb, int G, int rows, int32_t* v_seq, int32_t* v_req,
+                                   int32_t* v_qrow, int32_t* v_nq, int32_t* v_pos, int32_t* v_f0,
+                                   int32_t* status) {
     const int v = blockIdx.x * blockDim.x + threadIdx.x;
     if (v >= n_reqs * nqb) return;
-    const int r = v / nqb, j0 = (v - r * nqb) * cq;
+    const int r = v / nqb, f0 = (v - r * nqb) * rows;
     const int seq = seq_lens[r], ql = q_len[r];
-    int nq = min(cq, ql - j0);
+    int n = 0;
     if (ql < 0 || ql > seq) {
-        if (j0 == 0) report(status, TTKV_STATUS_QUERY);
-        nq = 0;
+        if (f0 == 0) report(status, TTKV_STATUS_QUERY);
+    } else {
+        n = max(0, min(rows, ql * G - f0));
     }
-    nq = max(nq, 0);
-    const int pos = seq - ql + j0;
-    v_seq[v] = nq > 0 ? pos + nq : 0;
+    const int p0 = seq - ql;
+    v_seq[v] = n > 0 ? p0 + (f0 + n - 1) / G + 1 : 0;
     v_req[v] = r;
-    v_qrow[v] = q_start[r] + j0;
-    v_nq[v] = nq;
-    v_pos[v] = pos;
+    v_qrow[v] = q_start[r];
+    v_nq[v] = n;
+    v_pos[v] = p0;
+    v_f0[v] = f0;
 }
 
 // The decoders' operand images (ttkv_decoder_image): grid (decoders, KV heads), thread t = column

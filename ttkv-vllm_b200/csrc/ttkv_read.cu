@@ -68,13 +68,14 @@ struct ReadParams {
     int max_seq;              // the call's max_seq_len: a longer request is refused on the device
     int64_t n_part_slots;     // tensor-core decode: partial slots the workspace holds
     // tensor-core decode of continuation chunks (null for a decode): request r of the launch is a
-    // block of v_nq[r] consecutive queries of stored request v_req[r], the first at query row
-    // v_qrow[r] and position v_pos[r]; its G rows are (query j = row / g_real, head row % g_real),
-    // and query j sees the stored rows before v_pos[r] + j + 1
+    // block of v_nq[r] consecutive (query, query head) rows of stored request v_req[r], numbered
+    // query-major from v_f0[r]: row i is query j = (v_f0 + i) / g_real, head (v_f0 + i) % g_real,
+    // at query row v_qrow[r] + j and position v_pos[r] + j, seeing the stored rows before it + 1
     const int32_t* v_req;
     const int32_t* v_qrow;
     const int32_t* v_nq;
     const int32_t* v_pos;
+    const int32_t* v_f0;
     int g_real;
     float* part_o;            // [req][head][qmax*G][split][128]
     float* part_ml;           // [req][head][qmax*G][split][2]
@@ -526,29 +527,28 @@ Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int
     return pl;
 }
 
-// Continuation chunks on the tensor-core decode: a block of cq consecutive queries of a request
-// is one request of a decode launch whose G * cq rows are (query, query head) pairs, so each
-// stored tile is rebuilt once per block of queries instead of once per query. cq = 8 / G (the
-// decode's rows), used when a block holds at least two queries (G <= 4).
-int cont_cq(int G) { return (G >= 1 && G <= kMaxG / 2) ? kMaxG / G : 0; }
+// Continuation chunks on the tensor-core decode: the (query, query head) rows of a request's
+// chunk, query-major, in blocks of the decode's 8 rows; each block is one request of a decode
+// launch with G = 8, so each stored tile is rebuilt once per 8 rows (8 / G queries) instead of
+// once per query.
+constexpr int kContRows = kMaxG;
 
 struct ContPlan {
-    int cq, nqb, n_v;
-    Plan pl;                 // the decode's plan over the n_v query blocks
-    size_t arrays_off;       // five int32 [n_v] arrays (block rows, request, first query row,
-    size_t bytes;            // query count, first position) after the partials
+    int nqb, n_v;            // blocks per request, blocks in all
+    Plan pl;                 // the decode's plan over the n_v blocks
+    size_t arrays_off;       // six int32 [n_v] arrays (block rows, request, first query row, row
+    size_t bytes;            // count, first query's position, first row) after the partials
 };
 
 ContPlan make_cont_plan(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_q, int max_seq,
                         int n_heads, int block_size) {
     ContPlan c{};
     const int G = HQ / lay->H;
-    c.cq = cont_cq(G);
-    c.nqb = (max_q + c.cq - 1) / c.cq;
+    c.nqb = int((int64_t(max_q) * G + kContRows - 1) / kContRows);
     c.n_v = n_reqs * c.nqb;
-    c.pl = make_plan_tc(lay, c.n_v, lay->H * G * c.cq, max_seq, n_heads, block_size);
+    c.pl = make_plan_tc(lay, c.n_v, lay->H * kContRows, max_seq, n_heads, block_size);
     c.arrays_off = (c.pl.part_o_bytes + c.pl.part_ml_bytes + 255) & ~size_t(255);
-    c.bytes = c.arrays_off + size_t(5) * c.n_v * sizeof(int32_t);
+    c.bytes = c.arrays_off + size_t(6) * c.n_v * sizeof(int32_t);
     return c;
 }
 
@@ -714,8 +714,7 @@ extern "C" size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t
     if (!lay || lay->H < 1 || HQ < lay->H || head_hi <= head_lo) return 0;
     const Plan pl = make_plan(lay, n_reqs, HQ, max_q_len, max_seq_len, head_hi - head_lo, true);
     size_t need = pl.part_o_bytes + pl.part_ml_bytes;
-    const int G = HQ / lay->H, cq = cont_cq(G);
-    if (cq >= 2 && max_q_len >= 1 && tc_serves(lay, lay->H * G * cq))   // sized for blocks of 16 tokens
+    if (max_q_len >= 1 && tc_serves(lay, lay->H * kContRows))            // sized for blocks of 16 tokens
         need = std::max(need, make_cont_plan(lay, n_reqs, HQ, max_q_len, max_seq_len, head_hi - head_lo,
                                              16).bytes);
     return need;
@@ -753,34 +752,34 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
         T = tc::tc_geom(lay, HQ / lay->H);
         use_tc = tc_maps(&maps, T, P);
     }
-    // continuation chunks: blocks of cq queries on the tensor-core decode when it serves the
-    // layout at G * cq rows and the workspace holds its plan (else the fp32 kernel below)
-    const int Gq = HQ / lay->H, cq = cont_cq(Gq);
-    if (multi && cq >= 2 && tc_serves(lay, lay->H * Gq * cq) && rope->dtype != TTKV_F32 &&
+    // continuation chunks: blocks of 8 (query, head) rows on the tensor-core decode when it
+    // serves the layout at 8 rows and the workspace holds its plan (else the fp32 kernel below)
+    const int Gq = HQ / lay->H;
+    if (multi && tc_serves(lay, lay->H * kContRows) && rope->dtype != TTKV_F32 &&
         (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0 &&
         (int64_t(max_seq_len) + 256) * cache->block_size < (int64_t(1) << 30)) {
         const ContPlan c = make_cont_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads,
                                           cache->block_size);
-        tc::TcGeom TC = tc::tc_geom(lay, Gq * cq);
+        tc::TcGeom TC = tc::tc_geom(lay, kContRows);
         tc::TcMaps mc;
         if (workspace && ws_bytes >= c.bytes && TC.smem > 0 && tc_maps(&mc, TC, P)) {
             int32_t* arr = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + c.arrays_off);
             int32_t *v_seq = arr, *v_req = arr + c.n_v, *v_qrow = arr + 2 * c.n_v;
-            int32_t *v_nq = arr + 3 * c.n_v, *v_pos = arr + 4 * c.n_v;
-            P.q = q; P.q_dtype = q_dtype; P.q_stride = q_stride; P.G = Gq * cq; P.HQ = lay->H * P.G;
+            int32_t *v_nq = arr + 3 * c.n_v, *v_pos = arr + 4 * c.n_v, *v_f0 = arr + 5 * c.n_v;
+            P.q = q; P.q_dtype = q_dtype; P.q_stride = q_stride; P.G = kContRows; P.HQ = lay->H * P.G;
             P.g_real = Gq; P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
             P.qmax = 1; P.n_qblk = 1; P.n_splits = c.pl.n_splits; P.chunk = 0;
             P.n_reqs = c.n_v; P.seq_lens = v_seq;
-            P.v_req = v_req; P.v_qrow = v_qrow; P.v_nq = v_nq; P.v_pos = v_pos;
+            P.v_req = v_req; P.v_qrow = v_qrow; P.v_nq = v_nq; P.v_pos = v_pos; P.v_f0 = v_f0;
             P.n_ctas = c.pl.n_splits; P.max_seq = max_seq_len; P.n_part_slots = c.pl.n_part_slots;
             P.part_o = reinterpret_cast<float*>(workspace);
             P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + c.pl.part_o_bytes);
             P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
             cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
             tc::cont_blocks_kernel<<<(c.n_v + 255) / 256, 256, 0, st>>>(
-                batch->seq_lens, q_start, q_len, batch->n_reqs, c.nqb, c.cq, v_seq, v_req, v_qrow, v_nq,
-                v_pos, status);
+                batch->seq_lens, q_start, q_len, batch->n_reqs, c.nqb, Gq, kContRows, v_seq, v_req,
+                v_qrow, v_nq, v_pos, v_f0, status);
             if (int e = check_launch("cont_blocks_kernel")) return e;
             return launch_tc(P, TC, mc, c.pl, c.n_v, st);
         }
