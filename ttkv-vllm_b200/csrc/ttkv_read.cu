@@ -763,7 +763,8 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                                           cache->block_size);
         tc::TcGeom TC = tc::tc_geom(lay, kContRows);
         tc::TcMaps mc;
-        if (workspace && ws_bytes >= c.bytes && TC.smem > 0 && tc_maps(&mc, TC, P)) {
+        // the merge's grid holds one z-index per block (at most 65535)
+        if (workspace && ws_bytes >= c.bytes && c.n_v <= 65535 && TC.smem > 0 && tc_maps(&mc, TC, P)) {
             int32_t* arr = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + c.arrays_off);
             int32_t *v_seq = arr, *v_req = arr + c.n_v, *v_qrow = arr + 2 * c.n_v;
             int32_t *v_nq = arr + 3 * c.n_v, *v_pos = arr + 4 * c.n_v, *v_f0 = arr + 5 * c.n_v;
