@@ -650,6 +650,32 @@ def run_sweep(args):
     print(json.dumps(line))
 
 
+def dense_point(B, n, L, steps, warmup, device, gen, H=8, HQ=24, d=128):
+    """One point of the dense comparator: L layers of one query token per request over a bf16
+    [B, H, n + 1, d] K and V (torch SDPA, GQA), one CUDA graph per step."""
+    import torch
+    import torch.nn.functional as F
+    k = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+    v = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+    q = [torch.randn(B, HQ, 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
+    out = [None] * L
+
+    def step():
+        for l in range(L):
+            out[l] = F.scaled_dot_product_attention(q[l], k[l], v[l], scale=d ** -0.5, enable_gqa=True)
+
+    step()
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    ms = _event_ms(g.replay, steps, warmup)
+    del g, k, v, q, out
+    torch.cuda.empty_cache()
+    kv = L * B * (n + 1) * H * d * 2 * 2
+    return {"batch": B, "ctx": n, "ms_per_step": ms, "tok_s": B / (ms * 1e-3), "kv_gbs": kv / (ms * 1e-3) / 1e9}
+
+
 def run_dense(args):
     """The dense comparator of configs 1 and 2: the same decode steps over a bf16 KV cache (4096 B
     per token per layer, what stock vLLM stores), read by torch's scaled_dot_product_attention (a
@@ -657,38 +683,14 @@ def run_dense(args):
     28 layers of one query token per request attending over [B, 8, n, 128] K and V, replayed from
     one CUDA graph. Reports each point's step time and its KV read rate."""
     import torch
-    import torch.nn.functional as F
     device = torch.device("cuda", 0)
     ctxs = [int(x) for x in args.sweep_ctx.split(",")]
     batches = [int(x) for x in args.sweep_batch.split(",")]
-    L, H, HQ, d = args.layers, 8, 24, 128
+    L = args.layers
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
     hbm, tc, peak_kind = _peaks()
-    points = []
-    for B in batches:
-        for n in ctxs:
-            k = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
-            v = [torch.randn(B, H, n + 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
-            q = [torch.randn(B, HQ, 1, d, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(L)]
-            out = [None] * L
-
-            def step():
-                for l in range(L):
-                    out[l] = F.scaled_dot_product_attention(q[l], k[l], v[l], scale=d ** -0.5, enable_gqa=True)
-
-            step()
-            torch.cuda.synchronize(device)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                step()
-            ms = _event_ms(g.replay, args.steps, args.warmup)
-            del g
-            kv = L * B * (n + 1) * H * d * 2 * 2
-            points.append({"batch": B, "ctx": n, "ms_per_step": ms, "tok_s": B / (ms * 1e-3),
-                           "kv_gbs": kv / (ms * 1e-3) / 1e9})
-            del k, v, q, out
-            torch.cuda.empty_cache()
+    points = [dense_point(B, n, L, args.steps, args.warmup, device, gen) for B in batches for n in ctxs]
     top = max(points, key=lambda p: p["kv_gbs"])
     line = {"metric": "dense bf16 decode step (comparator, torch SDPA)", "value": top["tok_s"],
             "unit": "tok/s (best point)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -769,6 +771,16 @@ def main():
     head_lo, head_hi = (sh.head_lo, sh.head_hi) if sh else (0, H)
 
     r1s = (S.LLAMA32_3B_R1 * ((args.layers + 27) // 28))[:args.layers]
+    dense = None
+    if world == 1:
+        # the same step over a dense bf16 KV cache (what stock vLLM stores), torch SDPA: context for
+        # the TT-KV step's time, not a measurement of this library (first, on a quiet device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1)
+        dense = dense_point(args.batch, args.ctx, len(r1s), min(args.steps, 50), args.warmup, device, gen)
+        dense = {"ms_per_step": dense["ms_per_step"], "tok_s": dense["tok_s"], "kv_gbs": dense["kv_gbs"],
+                 "api": "torch scaled_dot_product_attention over bf16 K/V, 4096 B per token per layer, "
+                        "one CUDA graph per step (bench.py --workload dense sweeps it)"}
     t0 = time.perf_counter()
     wl = Workload(args.batch, args.ctx, r1s, args.cfg, device, torch.bfloat16, seed=0)
     if sh is not None:
@@ -950,6 +962,8 @@ def main():
                 "setup_s": round(setup_s, 1), "fit_s": round(wl.fit_s, 1)}
         if plugin is not None:
             line["e2e_plugin"] = plugin
+        if dense is not None:
+            line["dense_comparator"] = dense
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
