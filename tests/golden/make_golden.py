@@ -240,11 +240,82 @@ def main(ref_root: str):
     save("paging", block_table=bt, seq_lens=np.array([37, 5, 64, 1], np.int32),
          slots=np.concatenate(slots))
 
+    cfg0(torch, codec, pc, dc, enc, L, R, syn, save, manifest)
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1))
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 
+CFG0_N, CFG0_R1 = 1082, 110
+
+
+def cfg0(torch, codec, pc, dc, enc, L, R, syn, save, manifest):
+    """H. BASELINE config 0 at its full size: one request of 1082 tokens, r1 = 110, `safe`, an fp16
+    model (K, V, q and the llama3-scaled RoPE table in fp16), encoded by the reference's own
+    encoder (fit_into_budget + pack_{k,v}_slots) and read by its CPU path (attend_raw_store).
+    K and V are not stored: they are `synth_kv(seed, 1082)` rounded to fp16 (checked by SHA-256),
+    except the (head, token) rows of V whose 81st and 82nd largest magnitudes tie (about 1% of
+    fp16 rows), which are redrawn so that the reference's torch.topk lane set is unique; those
+    rows are stored (`v_fix_rows`, `v_fix`)."""
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))       # noqa: E731
+    N = lambda t: t.detach().cpu().numpy()                          # noqa: E731
+    cfg = codec.CONFIGS["safe"]
+    lay = L.layout_for_config(cfg, CFG0_R1)
+    seed = 100
+    K, V0 = syn.synth_kv(seed, CFG0_N)
+    K = syn.round_to_dtype(K, "float16")
+    V0 = syn.round_to_dtype(V0, "float16")
+    V = _untie_v(np.random.default_rng(seed + 1), V0, cfg["k_lanes"], syn)
+    fix = np.nonzero(np.any(V.reshape(-1, 128) != V0.reshape(-1, 128), axis=1))[0].astype(np.int32)
+    out = {"seed": np.int32(seed), "n": np.int32(CFG0_N), "r1": np.int32(CFG0_R1),
+           "v_fix_rows": fix, "v_fix": V.reshape(-1, 128)[fix].astype(np.float16),
+           "K_sha256": np.frombuffer(hashlib.sha256(K.astype(np.float16).tobytes()).digest(), np.uint8),
+           "V_sha256": np.frombuffer(hashlib.sha256(V0.astype(np.float16).tobytes()).digest(), np.uint8)}
+    with cuda_division_rule(torch):
+        Xt = T(np.ascontiguousarray(K.transpose(1, 2, 0)))
+        cores, _ = codec.tt_svd(Xt, cfg["tols"], CFG0_R1)
+        fk = enc.fit_into_budget(T(K), lay, cfg)
+        kl = pc.build_k_layer(T(K), cfg["tols"], cfg["qbits"], cfg["res_frac"], cfg["res_bits"],
+                              max_rank=CFG0_R1)
+        dec = fk.decoder.decoder_f
+        r = int(fk.fitted_rank)
+        dq, ds = N(kl.dec_q), N(kl.dec_scale)
+        assert np.array_equal(N(dec)[:r], dq.astype(np.float32) * ds.astype(np.float32)[:, None])
+        ks = L.pack_k_slots(lay, fk.coeff_q, fk.coeff_scale, fk.resid)
+        vs = L.pack_v_slots(lay, enc.encode_v(T(V), lay))
+        table = syn.cos_sin_cache(CFG0_N + 6, dtype="float16")
+        cos, sin = dc.cos_sin_from_cache(T(table).half(), torch.arange(CFG0_N), 128)
+        q = syn.synth_queries(seed, (24, 128), "float16")
+        out.update(G1=N(cores[0]), G2=N(cores[1]), G3=N(cores[2]), fit_rank=np.int32(r),
+                   dec_q=dq, dec_scale=ds.view(np.uint16), k_slots=N(ks), v_slots=N(vs),
+                   q=q.astype(np.float16),
+                   attend=N(R.attend_raw_store(lay, ks, vs, dec, T(q), cos, sin)),
+                   attend_oracle=N(R.oracle_attend(lay, ks, vs, dec, T(q), cos, sin)))
+    save("store_cfg0_recip", **out)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <reference source tree>")
-    main(sys.argv[1])
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    if len(args) != 1:
+        sys.exit("usage: make_golden.py <reference source tree> [--only-cfg0]")
+    if "--only-cfg0" in sys.argv:
+        # add config 0's case to an existing golden set (the other files are left as they are)
+        ref = pathlib.Path(args[0]).resolve()
+        sys.path.insert(0, str(ref / "codec"))
+        sys.path.insert(0, str(ref))
+        import torch
+        import ttkv_codec as codec
+        import ttkv_packed_cache as pc
+        from vllm_ttkv import decode as dc
+        from vllm_ttkv import encode as enc
+        from vllm_ttkv import layout as L
+        from vllm_ttkv import reference as R
+        manifest = json.loads((HERE / "manifest.json").read_text())
+
+        def save(name, **arrays):
+            np.savez_compressed(HERE / f"{name}.npz", **arrays)
+            manifest["cases"][name] = sorted(arrays)
+        cfg0(torch, codec, pc, dc, enc, L, R, _load_synthetic(), save, manifest)
+        (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1))
+        print("wrote store_cfg0_recip.npz")
+    else:
+        main(args[0])

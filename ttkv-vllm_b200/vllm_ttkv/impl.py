@@ -338,10 +338,16 @@ class TTKVAttentionImpl(_ImplBase):
             if e <= s:
                 continue
             k = plan.keys[r]
-            if decoder_for_request(name, k) is not None:
+            # a first chunk (all of the request's tokens are in this step) is always fitted: a
+            # decoder already under its key belongs to a finished request whose first block the
+            # engine has since handed to this one, and projecting onto it would store this
+            # request's keys in another request's basis. The refit overwrites it in place (same
+            # pool row). The reference reuses the stale decoder here (impl.py:614).
+            first = plan.seq_lens[r] == e - s
+            if not first and decoder_for_request(name, k) is not None:
                 frozen.append((r, request_slot(k)))
                 continue
-            if plan.seq_lens[r] != e - s:
+            if not first:
                 raise RuntimeError(
                     f"request {k} has seq_len={plan.seq_lens[r]} but {e - s} tokens in this step and "
                     f"no fitted decoder: a continuation whose first chunk was never written")

@@ -11,6 +11,7 @@ each request's tokens INCLUDING the ones this step writes (the write runs before
 from __future__ import annotations
 
 import itertools
+import os
 from dataclasses import dataclass
 
 import torch
@@ -23,6 +24,8 @@ except Exception:                      # pragma: no cover - the impl itself does
     _BuilderBase = object
 
 _SERIAL = itertools.count(1)
+# steps a request may go unnamed before the builder releases its decoders (0: never)
+RELEASE_ENV = "VLLM_TTKV_RELEASE_AFTER"
 
 
 def next_serial() -> int:
@@ -82,6 +85,21 @@ class TTKVAttentionMetadataBuilder(_BuilderBase):
         if vllm_config is not None and getattr(vllm_config, "speculative_config", None) is not None:
             raise NotImplementedError(
                 "TT-KV does not support speculative decoding: drafted tokens are not stored keys.")
+        from vllm_ttkv import rope_store
+        self._reaper = rope_store.AbsenceReaper(int(os.environ.get(RELEASE_ENV, "0") or 0))
 
     def build(self, common_prefix_len, common_attn_metadata, fast_build: bool = False):
-        return build(common_attn_metadata)
+        md = build(common_attn_metadata)
+        if self._reaper.after > 0 and md.block_table is not None and md.seq_lens is not None:
+            n = int(md.seq_lens.shape[0])           # one readback per step, only when enabled
+            self._reaper.step(md.block_table[:n, 0].tolist())
+        return md
+
+    @staticmethod
+    def release_finished(keys) -> None:
+        """Return the decoders of finished requests, named by their keys (the first block id of
+        each request's block-table row, read before the engine frees the blocks): every layer's
+        pool row goes back to the free list and the device key map forgets the key."""
+        from vllm_ttkv import rope_store
+        for k in keys:
+            rope_store.release_request(int(k))

@@ -23,7 +23,6 @@ from __future__ import annotations
 
 import json
 import pathlib
-import re
 
 import torch
 
@@ -34,8 +33,6 @@ CONFIG_ENV = "VLLM_TTKV_CONFIG"
 CALIBRATION_ENV = "VLLM_TTKV_CALIBRATION"
 
 _STORES: dict[str, "TTKVRopeStore"] = {}
-_CALIBRATED: dict[int, TTKLayout] = {}
-_CALIBRATION: dict = {}
 _DECODERS: dict[tuple[str, int], "object"] = {}       # (layer, key) -> KDecoder
 _POOLS: dict[str, "DecoderPool"] = {}
 _REQ_SLOT: dict[int, int] = {}                         # request key -> pool row (all layers)
@@ -45,42 +42,71 @@ _KEY_ROWS: dict[torch.device, torch.Tensor] = {}       # device copy of _REQ_SLO
 _RESERVE = [16]                                        # pool rows a new pool starts with
 
 
-def _layer_index(layer_name: str) -> int | None:
-    m = re.search(r"layers\.(\d+)", layer_name)
-    if m:
-        return int(m.group(1))
-    nums = re.findall(r"(\d+)", layer_name)
-    return int(nums[-1]) if nums else None
+class Calibration:
+    """A loaded per-layer rank table: the artifact as read (its metadata travels with any slot
+    size derived from it) and the layout each transformer block gets from it.
+
+    The artifact is the reference's calibration JSON (keys `r1` = one rank per block, `layers`,
+    `heads`, `head_dim`, plus free-form provenance such as the corpus; rope_store.py:70-103 reads
+    the same keys). Layouts are built once at load time, so a lookup is a list index."""
+
+    def __init__(self, data: dict, cfg: dict, source: str = "<dict>"):
+        ranks = [int(x) for x in data["r1"]]
+        if len(ranks) != int(data["layers"]):
+            raise ValueError(f"{source}: calibration lists {len(ranks)} ranks (r1) for "
+                             f"{data['layers']} layers")
+        self.meta = dict(data)
+        self.layouts = [layout_for_config(cfg, r, H=int(data["heads"]), d=int(data["head_dim"]))
+                        for r in ranks]
+
+    def layout(self, block: int | None) -> TTKLayout | None:
+        if block is None or not 0 <= block < len(self.layouts):
+            return None
+        return self.layouts[block]
+
+
+_CAL: list[Calibration] = []                             # the loaded table (at most one)
+
+
+def block_index(layer_name: str) -> int | None:
+    """The transformer block a vLLM layer name belongs to: the integer component that follows a
+    `layers` component (`model.layers.7.self_attn.attn` -> 7); failing that, the last all-digit
+    component (a spec may carry a shortened name such as `attn.7`); None when there is none.
+    A name that resolves to no block is reported as uncalibrated by the lookup, never guessed."""
+    parts = layer_name.split(".")
+    for prev, cur in zip(parts, parts[1:]):
+        if prev == "layers" and cur.isdigit():
+            return int(cur)
+    digits = [p for p in parts if p.isdigit()]
+    return int(digits[-1]) if digits else None
 
 
 def load_calibration(path, cfg_name: str = "safe", cfg: dict | None = None) -> dict:
-    """Per-layer layouts from a calibration artifact with keys r1, layers, heads, head_dim
-    (the reference's tools/calibrate_r1.py format, rope_store.py:70-103)."""
-    global _CALIBRATION
-    cfg = config(cfg_name) if cfg is None else cfg
-    data = json.loads(pathlib.Path(path).read_text())
-    r1 = data["r1"]
-    if len(r1) != data["layers"]:
-        raise ValueError(f"{path}: r1 has {len(r1)} entries but layers={data['layers']}")
-    _CALIBRATED.clear()
-    for idx, rank in enumerate(r1):
-        _CALIBRATED[idx] = layout_for_config(cfg, int(rank), H=data["heads"], d=data["head_dim"])
-    _CALIBRATION = dict(data)
-    return _CALIBRATION
+    """Load a calibration artifact (see `Calibration`) under allocation `cfg` (default: the
+    named one) and make it the table `layout_for_layer` falls back to. Returns its metadata."""
+    cal = Calibration(json.loads(pathlib.Path(path).read_text()),
+                      config(cfg_name) if cfg is None else cfg, source=str(path))
+    _CAL[:] = [cal]
+    return dict(cal.meta)
 
 
 def calibration_info() -> dict:
-    return dict(_CALIBRATION)
+    """The loaded artifact's metadata, or {} when no table is loaded."""
+    return dict(_CAL[0].meta) if _CAL else {}
 
 
 def layout_for_layer(layer_name: str | None) -> TTKLayout | None:
+    """A layer's layout. A live store (one exists once a forward has fitted the layer) is the
+    truth; before any forward (cache sizing) only the calibration table can answer. None means
+    the layer cannot be served; callers raise."""
     if layer_name is None:
         return None
-    store = _STORES.get(layer_name)
-    if store is not None:
-        return store.layout
-    idx = _layer_index(layer_name)
-    return _CALIBRATED.get(idx) if idx is not None else None
+    live = _STORES.get(layer_name)
+    if live is not None:
+        return live.layout
+    if not _CAL:
+        return None
+    return _CAL[0].layout(block_index(layer_name))
 
 
 # ------------------------------------------------------------------ request keys
@@ -264,8 +290,54 @@ def release_decoder(layer_name: str, key: int) -> None:
 
 
 def release_request(key: int) -> None:
+    """Drop a finished request's decoder in every layer and return its pool row (the next
+    registered request takes it over). The engine calls this when the request completes; the
+    reference never releases (rope_store.py:230), so its registry grows for the whole run."""
     for name in [n for (n, k) in _DECODERS if k == key]:
         release_decoder(name, key)
+    s = _REQ_SLOT.pop(key, None)               # a key registered with no layer left (defensive)
+    if s is not None:
+        _FREE_SLOTS.append(s)
+        _set_key_row(key, -1)
+
+
+def live_keys() -> set[int]:
+    """Keys (first block ids) of the requests holding a decoder pool row."""
+    return set(_REQ_SLOT)
+
+
+def pool_rows_in_use() -> int:
+    return len(_REQ_SLOT)
+
+
+class AbsenceReaper:
+    """Releases requests that no step has named for `after` consecutive steps: a fallback for an
+    engine that does not report completions. A request that merely sits out steps (a prefill
+    chunk held back by the token budget, another pipeline micro-batch) must not be released, so
+    `after` has to exceed the longest such gap; off (0) unless VLLM_TTKV_RELEASE_AFTER is set."""
+
+    def __init__(self, after: int):
+        self.after = int(after)
+        self._missed: dict[int, int] = {}
+
+    def step(self, keys) -> list[int]:
+        """Record the keys of a step's requests; returns the keys released by this call."""
+        if self.after <= 0:
+            return []
+        seen = {int(k) for k in keys}
+        released = []
+        for k in list(_REQ_SLOT):
+            if k in seen:
+                self._missed.pop(k, None)
+                continue
+            n = self._missed.get(k, 0) + 1
+            if n >= self.after:
+                release_request(k)
+                self._missed.pop(k, None)
+                released.append(k)
+            else:
+                self._missed[k] = n
+        return released
 
 
 def clear_decoders() -> None:
