@@ -137,6 +137,17 @@ def _cache_struct(lay: TTKLayout, flat: torch.Tensor, block_size: int, flags: in
     return _lib.Cache(flat.data_ptr(), flat.shape[0], flat.stride(0), block_size, flags)
 
 
+def _lead_stride(t: torch.Tensor) -> int:
+    """Elements between consecutive rows of a contiguous pool. A size-1 leading dimension may carry
+    any stride (a numpy `x[None]` view has 0), so it is derived from the other dimensions."""
+    if t.shape[0] > 1:
+        return t.stride(0)
+    n = 1
+    for d in t.shape[1:]:
+        n *= d
+    return n
+
+
 def decoder_image(lay: TTKLayout, decoders: torch.Tensor, out=None):
     """The decode's operand images of decoders [n, r1, H*d] fp32: (image [n, bytes] uint8,
     scales [n, H] fp32), or None when the tensor-core decode does not serve the layout.
@@ -157,7 +168,7 @@ def decoder_image(lay: TTKLayout, decoders: torch.Tensor, out=None):
         image, scales = out
         if image.dtype != torch.uint8 or image.shape[0] < n or image.stride(0) < per or scales.shape[0] < n:
             raise ValueError("image / scales too small for the decoders")
-    _lib.check(L.ttkv_decoder_image(C.byref(la), decoders.data_ptr(), decoders.stride(0), n,
+    _lib.check(L.ttkv_decoder_image(C.byref(la), decoders.data_ptr(), _lead_stride(decoders), n,
                                     image.data_ptr(), image.stride(0), scales.data_ptr(), _stream()))
     return image, scales
 
@@ -181,7 +192,7 @@ def _batch_struct(block_table, seq_lens, decoders, dec_index, images=None) -> _l
             raise ValueError("one decoder image and scale row per pool row")
         img, istride, scl = image.data_ptr(), image.stride(0), scales.data_ptr()
     return _lib.Batch(block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
-                      seq_lens.data_ptr(), n, decoders.data_ptr(), decoders.stride(0),
+                      seq_lens.data_ptr(), n, decoders.data_ptr(), _lead_stride(decoders),
                       dec_index.data_ptr(), decoders.shape[0], img, istride, scl)
 
 
@@ -291,7 +302,7 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
     if pinvs is not None:
         if pinvs.shape != decoders.shape or not pinvs.is_contiguous() or pinvs.dtype != torch.float32:
             raise ValueError("pinvs must match the decoder pool's shape, contiguous float32")
-        pv, pv_stride, cq, cs = pinvs.data_ptr(), pinvs.stride(0), None, None
+        pv, pv_stride, cq, cs = pinvs.data_ptr(), _lead_stride(pinvs), None, None
     else:
         if coeff_q is None or coeff_scale is None:
             raise ValueError("the fit path needs coeff_q and coeff_scale")
@@ -303,7 +314,7 @@ def write_paged(lay: TTKLayout, cache: torch.Tensor, slot_mapping: torch.Tensor,
     _lib.check(L.ttkv_write_paged_shard(
         C.byref(la), h_lo, h_hi, C.byref(c_s), slot_mapping.data_ptr(), n, k.data_ptr(), dtype_code(k),
         _row_stride(k, "k"), v.data_ptr(), dtype_code(v), _row_stride(v, "v"), tok_dec.data_ptr(),
-        decoders.data_ptr(), decoders.stride(0), pv, pv_stride, decoders.shape[0], cq, cs,
+        decoders.data_ptr(), _lead_stride(decoders), pv, pv_stride, decoders.shape[0], cq, cs,
         ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
 
 
