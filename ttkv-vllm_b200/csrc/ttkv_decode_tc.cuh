@@ -642,7 +642,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         auto issue_cf = [&](int tile) {
             const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
             for (int i = tid; i < n; i += NTHR) {
-                const uint32_t u = __umulhi(uint32_t(i), mul_cf), c = uint32_t(i) - u * uint32_t(cch);
+                // i / cch as a multiply-high; a one-chunk block (r1 <= 14) has no such multiplier
+                const uint32_t u = cch == 1 ? uint32_t(i) : __umulhi(uint32_t(i), mul_cf),
+                               c = uint32_t(i) - u * uint32_t(cch);
                 cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
                            P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
             }
