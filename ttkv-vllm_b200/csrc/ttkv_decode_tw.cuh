@@ -16,14 +16,14 @@
 // with 16-byte cp.async (chunk-fastest over the tokens), and its lane 0 issues the MMAs. The two
 // sides meet only on mbarriers:
 //
-//   control                                  epilogue (tile it)
-//   ---------------------------------------  ---------------------------------------------------
-//   MMA 1 (it) once A(it) is converted  --->  wait K/V rows (it): bitmaps, code windows, rulers
-//   coefficients (it+1) into the free          wait PV (it-1): fold it into o
-//     staging buffer                            V codes -> V^T (fp16 integers)          -> K/V free
-//   K/V rows (it+1 or it+2) into the           wait MMA 1 (it); coefficients (it+1) -> A  -> A ready
-//     buffer the epilogue released              k = acc * (cs 2^e) + residual, RoPE, scores
-//   PV (it) once V^T and P' are written <---   tile max (one named barrier), p, P'      -> PV ready
+//   epilogue (tile j)                                      control, on each hand-off
+//   ----------------------------------------------------  ------------------------------------------
+//   wait K/V rows (j): bitmaps, code windows, rulers
+//   wait PV (j-1): fold it into o
+//   V codes -> V^T (fp16 integers)          -> K/V free    K/V rows of tile j+2 (or j+1) into it
+//   wait MMA 1 (j); coefficients (j+1) -> A -> A ready     MMA 1 (j+1); coefficients (j+2) staged
+//   k = acc * (cs 2^e) + residual, RoPE, scores            (MMA 1 (j+1) runs under this epilogue)
+//   tile max (one named barrier), p, P'     -> PV ready    PV (j)
 //
 //   MMA 1   acc[128 tokens x 128 lanes] = A . B_hi + A . B_lo in TMEM (two column sets, so MMA 1 of
 //           the next tile runs under this tile's epilogue), A = int8 coefficients as exact fp16, B =
@@ -284,38 +284,36 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
         const int koff = kfield & 15, voff = vfield & 15;
         const int cch = T.cb >> 4;
         const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
-        const int nkvc = kch + vch;
-        const uint32_t mul_cf = uint32_t((0x100000000ull + cch - 1) / cch);
-        const uint32_t mul_kv = uint32_t((0x100000000ull + nkvc - 1) / nkvc);
         const uint32_t bsz = uint32_t(P.block_size);
         const uint64_t mul_bs = (0x100000000ull + bsz - 1) / bsz;
         const int blk0 = t_begin / P.block_size;
-        auto slot_at = [&](int tok) -> int64_t {
+        // the slot row of token `tok` of this segment (its block from the cached block-table slice)
+        auto row_at = [&](int tok) -> const uint8_t* {
             const uint32_t blk = uint32_t((uint64_t(uint32_t(tok)) * mul_bs) >> 32);
-            return int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
+            return P.cache + (int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz)) *
+                             P.row_bytes;
         };
         auto ntok = [&](int tile) { return tile < n_tiles ? min(TM, t_end - (t_begin + tile * TM)) : 0; };
-        // control lanes only: one phase of copies, then one arrival per lane
+        // control lanes only. Lane l stages tokens l, l + 32, l + 64, l + 96 of the tile: the row
+        // address once per token, then the field's 16-byte chunks; one arrival per lane per phase
         auto issue_cf = [&](int tile) {
-            const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
-            for (int i = lane; i < n; i += 32) {
-                // i / cch as a multiply-high; a one-chunk block (r1 <= 14) has no such multiplier
-                const uint32_t u = cch == 1 ? uint32_t(i) : __umulhi(uint32_t(i), mul_cf),
-                               c = uint32_t(i) - u * uint32_t(cch);
-                cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
-                           P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
+            const int t0k = t_begin + tile * TM, n = ntok(tile);
+            for (int u = lane; u < n; u += 32) {
+                const uint8_t* src = row_at(t0k + u);
+                unsigned char* dst = cfb + u * T.cf_pitch;
+                const int swz = u & T.cf_swz;
+                for (int c = 0; c < cch; ++c) cp_async16(dst + 16 * (c ^ swz), src + 16 * c);
             }
             cp_async_arrive(&M->mb_cf);
         };
         auto issue_kv = [&](int tile) {
-            const int b = T.nkv == 2 ? (tile & 1) : 0, t0k = t_begin + tile * TM, n = ntok(tile) * nkvc;
+            const int b = T.nkv == 2 ? (tile & 1) : 0, t0k = t_begin + tile * TM, n = ntok(tile);
             unsigned char* dstb = kvb + size_t(b) * TM * T.kvrow;
-            for (int i = lane; i < n; i += 32) {
-                const uint32_t u = __umulhi(uint32_t(i), mul_kv), c = uint32_t(i) - u * uint32_t(nkvc);
-                const uint8_t* src = P.cache + slot_at(t0k + int(u)) * P.row_bytes;
+            for (int u = lane; u < n; u += 32) {
+                const uint8_t* src = row_at(t0k + u);
                 unsigned char* dst = dstb + u * T.kvrow;
-                if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
-                else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
+                for (int c = 0; c < kch; ++c) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
+                for (int c = 0; c < vch; ++c) cp_async16(dst + T.kr + 16 * c, src + (vfield - voff) + 16 * c);
             }
             cp_async_arrive(&M->mb_kv[b]);
         };
@@ -375,21 +373,22 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 if (tmo) return;
                 if (!mbar_wait(bar, ph)) tmo = true; else ph ^= 1u;
             };
-            for (int it = 0; it < n_tiles; ++it) {
-                // A(it) converted -- which also releases the coefficient buffer and the
-                // reconstruction columns MMA 1 (it) writes
+            // MMA 1 of tile j, and the coefficients of tile j + 1 into the buffer it frees, as soon as
+            // the epilogue has converted A(j) (which also means it is done with the reconstruction
+            // columns MMA 1 (j) writes, last read in tile j - 2)
+            auto recon = [&](int j) {
                 cwait(&M->mb_a, ph_a);
                 cwait(&M->mb_cff, ph_cff);
-                if (it == 0 && pend_dec) {
+                if (j == 0 && pend_dec) {
                     cwait(&M->mb_dec, ph_dec);
                     if (!tmo) pend_dec = false;
                 }
                 tmo = __any_sync(0xffffffffu, tmo);
-                if (tmo) break;
+                if (tmo) return;
                 if (lane == 0) {
                     tc_after();
                     constexpr uint32_t IDESC_R = idesc_f16(128, 128, false, false);
-                    const uint32_t d_tmem = taddr + uint32_t(it & 1) * 128u;
+                    const uint32_t d_tmem = taddr + uint32_t(j & 1) * 128u;
                     for (int ks = 0; ks < T.kp16 / 16; ++ks) {
                         const uint64_t k16 = uint64_t(((ks >> 2) * ATOM_BYTES + (ks & 3) * 32) >> 4);
                         mma_f16(d_tmem, dA + k16, dH + k16, IDESC_R, ks > 0 ? 1u : 0u);
@@ -399,20 +398,27 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     ++n_r;
                 }
                 __syncwarp();
-                if (it + 1 < n_tiles) issue_cf(it + 1);
-                // the K/V buffer tile `it` used, released by the epilogue after its V decode
+                if (j + 1 < n_tiles) issue_cf(j + 1);
+            };
+            // the control loop follows the epilogue's hand-offs of tile j in the order they come:
+            // K/V rows consumed, A(j + 1) converted, V^T and P' written
+            recon(0);
+            for (int j = 0; j < n_tiles && !tmo; ++j) {
                 if (T.nkv == 2) {
-                    if (it & 1) cwait(&M->mb_kvf[1], ph_kvf1); else cwait(&M->mb_kvf[0], ph_kvf0);
+                    if (j & 1) cwait(&M->mb_kvf[1], ph_kvf1); else cwait(&M->mb_kvf[0], ph_kvf0);
                     tmo = __any_sync(0xffffffffu, tmo);
                     if (tmo) break;
-                    if (it + 2 < n_tiles) issue_kv(it + 2);
+                    if (j + 2 < n_tiles) issue_kv(j + 2);
                 } else {
                     cwait(&M->mb_kvf[0], ph_kvf0);
                     tmo = __any_sync(0xffffffffu, tmo);
                     if (tmo) break;
-                    if (it + 1 < n_tiles) issue_kv(it + 1);
+                    if (j + 1 < n_tiles) issue_kv(j + 1);
                 }
-                // PV of this tile once V^T and P' are in shared memory
+                if (j + 1 < n_tiles) {
+                    recon(j + 1);
+                    if (tmo) break;
+                }
                 cwait(&M->mb_pvr, ph_pvr);
                 tmo = __any_sync(0xffffffffu, tmo);
                 if (tmo) break;
