@@ -37,19 +37,32 @@ for _p in (ROOT, ROOT / "ttkv-vllm_b200"):
 
 METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs peak"
 
-# DRAM bytes (read + write) of ONE decode launch, from the ncu capture summarised in
-# profiles/decode_tc_cfg1.md: layer 9 (r1 = 110) of this workload, 8 requests x 4323 rows.
-# The per-launch `traffic` of the roofline scales it by algorithmic bytes (the kernel reads each
-# slot byte once, so traffic grows in proportion to the rows and widths a launch reads).
-CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 37.01e6 + 0.005e6}
+# DRAM bytes (read + write) of ONE decode launch from an ncu capture of this workload's layer 9
+# (r1 = 110, 8 requests x 4323 rows), and a hash of the read kernel's sources at the time of the
+# capture. The per-launch `traffic` of the roofline scales it by algorithmic bytes (the kernel reads
+# each slot byte once, so traffic grows in proportion to the rows and widths a launch reads); when
+# the sources no longer hash the same, the capture describes another kernel and `traffic` is null.
+CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": None, "src_sha16": None, "kernel": None}
+READ_SOURCES = ("ttkv-vllm_b200/csrc/ttkv_read.cu", "ttkv-vllm_b200/csrc/ttkv_decode_tc.cuh",
+                "ttkv-vllm_b200/csrc/ttkv_decode_tw.cuh")
+
+
+def read_src_sha16() -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for f in READ_SOURCES:
+        h.update((ROOT / f).read_bytes())
+    return h.hexdigest()[:16]
 
 
 def _peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, "measured" | "fallback")."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -367,8 +380,15 @@ def cpu_sample(wl_params, sample_layers=(0, 9, 18, 27), reps=1, seed=0):
     return sum(per) / len(per)
 
 
+SAMPLE_LAYERS = (0, 9, 18, 27)          # the CPU sample's layers: r1 = 14, 110, 125, 67
+
+
 def run_reference(args):
-    """The reference arm: the reference's CPU path (the oracle port) on a bounded sample."""
+    """The reference arm: the reference's CPU path (the oracle's numpy port, BLAS on every host
+    thread) on a bounded sample of the same workload. Step k times one (request, layer) pair --
+    a write of the step's token and the read of the request's whole store -- at layer
+    SAMPLE_LAYERS[k % 4]; `ms_per_step` is that measured sample, and `value` extrapolates the mean
+    per-pair time to the full step (B requests x 28 layers), the factor named in the config."""
     from vllm_ttkv import synthetic as S
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -376,23 +396,27 @@ def run_reference(args):
     cores = os.cpu_count()
     B, n = args.batch, args.ctx
     r1s = S.LLAMA32_3B_R1
+    for k in range(args.warmup):
+        cpu_sample((B, n, r1s, "safe"), sample_layers=(SAMPLE_LAYERS[k % 4],), seed=100 + k)
     times = []
-    for _ in range(args.warmup):
-        cpu_sample((B, n, r1s, "safe"), sample_layers=(9,))
     for k in range(args.steps):
-        per = cpu_sample((B, n, r1s, "safe"), sample_layers=(9,), seed=k)
-        times.append(per * B * len(r1s))
-    step_s = statistics.median(times)
-    v = B / step_s
+        times.append(cpu_sample((B, n, r1s, "safe"), sample_layers=(SAMPLE_LAYERS[k % 4],), seed=k))
+    per_pair = statistics.mean(times)
+    factor = B * len(r1s)
+    v = B / (per_pair * factor)
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": per_pair * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"cfg1 decode step: B={B} x {n} ctx, 28 layers, safe", "batch": B,
-                       "ctx": n, "layers": len(r1s)},
+            "config": {"workload": f"cfg1 decode step: B={B} x {n} ctx, 28 layers, safe; each timed step is "
+                                   f"ONE (request, layer) pair cycling layers {list(SAMPLE_LAYERS)}, value "
+                                   f"extrapolated x{factor} (B x 28 layers)",
+                       "batch": B, "ctx": n, "layers": len(r1s), "extrapolation_factor": factor,
+                       "sample_layers": list(SAMPLE_LAYERS)},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"1 (request, layer) pair per step at n={n}, r1={r1s[9]}, "
-                                       f"scaled x{B * len(r1s)} to a full step"},
+                             "sample": f"1 (request, layer) pair per step at n={n}, layers "
+                                       f"{list(SAMPLE_LAYERS)} in turn (r1 {[r1s[l] for l in SAMPLE_LAYERS]}), "
+                                       f"scaled x{factor} to a full step"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -485,7 +509,7 @@ def run_prefill(args):
         s0 = c["e"] - c["ql"]
         pairs = c["ql"] * s0 + c["ql"] * (c["ql"] + 1) / 2
         flops += B * (4 * 128 * HQ * pairs + 2 * r1 * H * 128 * c["e"])
-    hbm, tc, peak_kind = _peaks()
+    hbm, tc, tc_sus, peak_kind = _peaks()
     tflops = flops / (read_ms * 1e-3) / 1e12
     line = {"metric": "chunked-prefill continuation tok/s (cfg3)", "value": B * (N - Q) / (ms * 1e-3),
             "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -503,52 +527,95 @@ def run_prefill(args):
 
 
 def run_encode(args):
-    """Config 4, the write path at prefill: one request of `--prompt-len` tokens (16384 for config 4),
-    `--layers` layers at the `tight` allocation with r1 = 110: per layer the TT-SVD fit
-    (`torch.linalg.svd`, a library call as in the reference) + the fit tail and the fitted write
-    (this repository's kernels). The config's 8 requests shard one per GPU with no exchange, so a
-    single GPU runs one request."""
+    """Config 4, the write path at prefill: requests of `--prompt-len` tokens (16384 for config 4),
+    `--layers` layers at the `tight` allocation with r1 = 110: per layer the TT-SVD fit (library
+    calls: `torch.linalg.svd` / the Gram matrix's `eigh`) + the fit tail and the fitted write (this
+    repository's kernels). The batch is split by request across ranks (torchrun: request r on rank
+    r, no exchange, `vllm_ttkv.shard.request_range`); a single GPU runs one request. `value` =
+    tokens of all ranks / the slowest rank's step time (weak scaling: one request per GPU)."""
     import numpy as np
     import torch
+    import torch.distributed as dist
 
     from vllm_ttkv import encode, ops, synthetic
     from vllm_ttkv.layout import layout_for_config
-    device = torch.device("cuda", 0)
+    from vllm_ttkv.shard import gather_bytes, request_range
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    lo, hi = request_range(rank, world, world)             # one request per GPU (weak scaling)
     n, H, r1, L = args.prompt_len, 8, 110, args.layers
     lay = layout_for_config("tight", r1, H=H)
-    gen = torch.Generator(device=device)
-    gen.manual_seed(0)
-    cache = torch.zeros(n, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device)
+    reqs = list(range(lo, hi))
+    caches, KVs = [], []
+    for r in reqs:
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1000 + r)                      # request r's keys, whichever rank has it
+        caches.append(torch.zeros(n, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device))
+        KVs.append([synth_kv_device(gen, H, n, dtype=torch.bfloat16) for _ in range(min(L, 4))])
+    toks = [[(K.permute(1, 0, 2).contiguous(), V.permute(1, 0, 2).contiguous()) for K, V in kv] for kv in KVs]
     slots = torch.arange(n, dtype=torch.int64, device=device)
-    KV = [synth_kv_device(gen, H, n, dtype=torch.bfloat16) for _ in range(min(L, 4))]
-    toks = [(K.permute(1, 0, 2).contiguous(), V.permute(1, 0, 2).contiguous()) for K, V in KV]
     fits = {}
 
     def step():
-        for l in range(L):
-            K, _ = KV[l % len(KV)]
-            kt, vt = toks[l % len(KV)]
-            fk = encode.fit_into_budget(K, lay, "tight")
-            encode.write_fitted(cache, slots, fk, kt, vt, lay)
-            fits[l % len(KV)] = fk
+        for i in range(len(reqs)):
+            for l in range(L):
+                K, _ = KVs[i][l % len(KVs[i])]
+                kt, vt = toks[i][l % len(KVs[i])]
+                fk = encode.fit_into_budget(K, lay, "tight")
+                encode.write_fitted(caches[i], slots, fk, kt, vt, lay)
+                fits[(i, l % len(KVs[i]))] = fk
 
-    ms = _event_ms(step, args.steps, args.warmup)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
     # this repository's write launch alone (the select/quantise/pack of every token), per layer
-    fk = fits[0]
-    kt, vt = toks[0]
-    w_ms = _event_ms(lambda: encode.write_fitted(cache, slots, fk, kt, vt, lay), 10, 3)
+    fk = fits[(0, 0)]
+    kt, vt = toks[0][0]
+    w_ms = _event_ms(lambda: encode.write_fitted(caches[0], slots, fk, kt, vt, lay), 10, 3)
+    # the slot bytes of every request, gathered for their checksum (the byte comparison itself is
+    # tests/test_baseline_configs.py's)
+    digest = None
+    if world > 1:
+        allb = gather_bytes(torch.cat(caches), None)
+        digest = int(allb.to(torch.int64).sum().item())
+        dist.barrier()
     alg = n * H * 128 * 2 * 2 + n * lay.compressed_bytes_per_token()     # K, V bf16 in; slots out
-    hbm, tc, peak_kind = _peaks()
+    hbm, tc, tc_sus, peak_kind = _peaks()
     gbs = alg / (w_ms * 1e-3) / 1e9
-    line = {"metric": "prefill encode tok/s (cfg4, one request per GPU)", "value": n / (ms * 1e-3),
-            "unit": f"tok/s ({L} layers)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "ms_per_layer": ms / L, "higher_is_better": True, "workload": "encode",
-            "dtype": "bf16 in, fp32 fit, u8 slots", "data": "synthetic",
-            "config": {"workload": f"cfg4: 1 request x {n} tokens, {L} layers, tight r1={r1}"},
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                         "peak_kind": peak_kind, "kernel": "encode_pack_kernel (ttkv_write_paged, fit path)",
-                         "write_ms_per_layer": w_ms, "alg_bytes_per_layer": alg}}
-    print(json.dumps(line))
+    total_req = world
+    if rank == 0:
+        line = {"metric": "prefill encode tok/s (cfg4, requests split across GPUs)",
+                "value": total_req * n / (ms * 1e-3), "unit": f"tok/s ({L} layers)", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms / L,
+                "higher_is_better": True, "scaling": "weak", "workload": "encode",
+                "dtype": "bf16 in, fp32 fit, u8 slots", "data": "synthetic",
+                "config": {"workload": f"cfg4: {total_req} request(s) x {n} tokens over {world} GPU(s) "
+                                       f"(request-sharded, no exchange), {L} layers, tight r1={r1}",
+                           "requests_per_rank": len(reqs), "slot_byte_sum": digest},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                             "peak_kind": peak_kind, "kernel": "encode_pack_kernel (ttkv_write_paged, fit path)",
+                             "write_ms_per_layer": w_ms, "alg_bytes_per_layer": alg}}
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_sweep(args):
@@ -601,7 +668,7 @@ def run_sweep(args):
     setup_s = time.perf_counter() - t0
     table = torch.from_numpy(synthetic.cos_sin_cache(nmax + 16, dtype="float32")).to(device).to(torch.bfloat16)
     dec_index = torch.arange(Bmax, dtype=torch.int32, device=device)
-    hbm, tc, peak_kind = _peaks()
+    hbm, tc, tc_sus, peak_kind = _peaks()
     ops.status_word(device)
     points = []
     for B in batches:
@@ -689,7 +756,7 @@ def run_dense(args):
     L = args.layers
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
-    hbm, tc, peak_kind = _peaks()
+    hbm, tc, tc_sus, peak_kind = _peaks()
     points = [dense_point(B, n, L, args.steps, args.warmup, device, gen) for B in batches for n in ctxs]
     top = max(points, key=lambda p: p["kv_gbs"])
     line = {"metric": "dense bf16 decode step (comparator, torch SDPA)", "value": top["tok_s"],
@@ -717,7 +784,10 @@ def main():
     ap.add_argument("--cfg", default="safe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-graph", action="store_true",
-                    help="launch every layer eagerly instead of replaying per-layer CUDA graphs")
+                    help="launch every layer eagerly instead of replaying a CUDA graph per step")
+    ap.add_argument("--layer-graphs", action="store_true",
+                    help="several GPUs: one CUDA graph per layer with the all-gathers outside them "
+                         "(default: one graph per step with the all-gathers captured in it)")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "encode", "sweep", "dense"],
                     help="decode: config 1 (the default line); sweep: config 2; prefill: config 3; "
@@ -797,34 +867,49 @@ def main():
             sh.pack(wl.out[l], bufs[l][0])
 
     graphs = None
+    whole_step = True                                 # one graph holds the whole step
 
     def run_steps(k):
         for _ in range(k):
-            if graphs is not None and sh is None:
-                graphs[0].replay()                         # the whole step
+            if graphs is not None and whole_step:
+                graphs[0].replay()                         # the whole step (all-gathers included)
                 continue
             for l in range(wl.L):
                 if graphs is not None:
                     graphs[l].replay()
                 else:
                     layer_work(l)
-                if sh is not None:                         # collectives stay outside the graphs
+                if sh is not None:                         # collectives between the layer graphs
                     sh.gather(*bufs[l])
                     sh.assemble(bufs[l][1], wl.out[l])     # every rank ends with all heads
 
+    def step_work():
+        for l in range(wl.L):
+            layer_work(l)
+            if sh is not None:
+                sh.gather(*bufs[l])
+                sh.assemble(bufs[l][1], wl.out[l])
+
     run_steps(args.warmup)
     if not args.no_graph:
-        # CUDA graphs captured after the warm-up allocated every workspace; the replays launch
-        # exactly the kernels the eager layers launch. One graph for the whole step on one GPU;
-        # one per layer on several, with each layer's all-gather between the replays
+        # CUDA graphs captured after the warm-up allocated every workspace (and, on several GPUs,
+        # after the NCCL communicator ran its first collectives); the replays launch exactly the
+        # kernels the eager steps launch. One graph for the whole step, each layer's all-gather
+        # captured in it; --layer-graphs keeps the collectives outside, one graph per layer
         torch.cuda.synchronize(device)
         graphs = []
-        for l in range(wl.L if sh is not None else 1):
+        whole_step = sh is None or not args.layer_graphs
+        if whole_step:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                for ll in ([l] if sh is not None else range(wl.L)):
-                    layer_work(ll)
+                step_work()
             graphs.append(g)
+        else:
+            for l in range(wl.L):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    layer_work(l)
+                graphs.append(g)
         torch.cuda.synchronize(device)
     run_steps(args.warmup)
     torch.cuda.synchronize(device)
@@ -870,7 +955,7 @@ def main():
     # algorithmic reconstruction FLOPs, (cq*cs) @ D over the heads read (the fp16 hi/lo split of
     # D doubles the tensor-core work actually issued; that is not counted)
     recon_flops = sum(wl.B * wl.max_seq * 2 * wl.r1s[l] * n_heads * 128 for l in range(wl.L))
-    hbm, tc, peak_kind = _peaks()
+    hbm, tc, tc_sus, peak_kind = _peaks()
 
     # ---- e2e: the same step through the C-ABI with host buffers copied in and out every step:
     # every layer's q, K and V of the step in one pinned buffer, every layer's output back in one
@@ -914,19 +999,27 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        per = cpu_sample((args.batch, args.ctx, r1s, args.cfg), sample_layers=(9,))
+        sl = [l for l in SAMPLE_LAYERS if l < len(r1s)]
+        per = cpu_sample((args.batch, args.ctx, r1s, args.cfg), sample_layers=tuple(sl))
         cpu_step = per * args.batch * len(r1s)
         cpu = {"value": args.batch / cpu_step, "unit": "tok/s", "cores": os.cpu_count(),
                "kind": "port",
-               "sample": f"1 (request, layer) pair (layer 9, r1={r1s[9]}, n={args.ctx}): oracle "
-                         f"frozen write of one token + decode read, scaled x{args.batch * len(r1s)}"}
+               "sample": f"{len(sl)} (request, layer) pairs (layers {sl}, r1 {[r1s[l] for l in sl]}, "
+                         f"n={args.ctx}): oracle frozen write of one token + decode read, mean scaled "
+                         f"x{args.batch * len(r1s)}"}
 
-    # per layer: write (write_frozen_kernel) + read (decode_tc_kernel + merge_kernel)
+    # per layer: write (write_frozen_kernel) + read (decode kernel + merge_sk_kernel)
     launches = wl.L * 3
     cap = CAPTURED_LAUNCH["layer"]
-    traffic = None
-    if cap < wl.L and n_heads == H:
+    traffic, traffic_src = None, "no ncu capture of this kernel build"
+    if CAPTURED_LAUNCH["dram_bytes"] and CAPTURED_LAUNCH["src_sha16"] == read_src_sha16() and cap < wl.L \
+            and n_heads == H:
         traffic = CAPTURED_LAUNCH["dram_bytes"] * (alg_bytes / wl.L) / wl.read_bytes(cap)
+        traffic_src = ("ncu dram__bytes_read+write of the layer-%d launch of %s (read sources %s), scaled "
+                       "per launch by algorithmic bytes" % (cap, CAPTURED_LAUNCH["kernel"],
+                                                           CAPTURED_LAUNCH["src_sha16"]))
+    elif CAPTURED_LAUNCH["dram_bytes"]:
+        traffic_src = "stale: the read kernel's sources changed since the ncu capture"
     if rank == 0:
         line = {"metric": METRIC, "value": args.batch / (ms * 1e-3), "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -945,16 +1038,19 @@ def main():
                            "storage": ("storage-sharded: coefficient block + this rank's heads' rows"
                                        if world > 1 else "full blobs"),
                            "launch": ("eager" if not graphs else "one CUDA graph per step" if sh is None
-                                      else "one CUDA graph per layer (write + read), all-gathers between"),},
+                                      else "one CUDA graph per step, the 28 all-gathers captured in it"
+                                      if whole_step else
+                                      "one CUDA graph per layer (write + read), all-gathers between"),},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
-                             "kernel": "decode_tc_kernel<3> + merge_kernel (ttkv_decode_paged)",
+                             "kernel": "decode_tw_kernel<3> + merge_sk_kernel (ttkv_decode_paged; "
+                                       "decode_tc_kernel<3> where the token-wide plan does not fit)",
                              "alg_bytes_per_launch": alg_bytes / wl.L,
                              "launch_us": dec_total_ms * 1e3 / wl.L,
-                             "traffic_source": "ncu dram__bytes_read+write of the layer-%d launch, "
-                                               "scaled per launch by algorithmic bytes" % cap,
+                             "traffic_source": traffic_src,
                              "tensor_tflops": recon_flops / (dec_total_ms * 1e-3) / 1e12,
-                             "tensor_frac": recon_flops / (dec_total_ms * 1e-3) / 1e12 / tc,
+                             "tensor_frac": recon_flops / (dec_total_ms * 1e-3) / 1e12 / tc_sus,
+                             "tensor_peak": tc_sus, "tensor_peak_kind": "bf16 sustained (%s)" % peak_kind,
                              "decode_ms_per_step": dec_total_ms},
                 "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},

@@ -22,6 +22,36 @@ import torch
 import torch.distributed as dist
 
 
+def request_range(rank: int, world: int, n_requests: int) -> tuple[int, int]:
+    """Requests [lo, hi) a rank encodes when a prefill batch is split by request (the encode has
+    no exchange: each request's fit and slots are its own). Contiguous shares in rank order, the
+    first n_requests % world ranks taking one more."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if n_requests < 0:
+        raise ValueError("negative request count")
+    base, extra = divmod(n_requests, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def gather_bytes(local: torch.Tensor, group=None) -> torch.Tensor:
+    """Every rank's uint8 tensor [n_r, C] concatenated in rank order on every rank (the byte
+    comparison of a request-sharded encode). Shapes may differ across ranks in dim 0."""
+    world = dist.get_world_size(group)
+    n = torch.tensor([local.shape[0]], dtype=torch.int64, device=local.device)
+    counts = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(counts, n, group=group)
+    counts = [int(c.item()) for c in counts]
+    width = local.shape[1]
+    pad = max(counts)
+    buf = torch.zeros(pad, width, dtype=local.dtype, device=local.device)
+    buf[:local.shape[0]] = local
+    outs = [torch.zeros_like(buf) for _ in range(world)]
+    dist.all_gather(outs, buf, group=group)
+    return torch.cat([o[:c] for o, c in zip(outs, counts)])
+
+
 def head_range(rank: int, world: int, H: int) -> tuple[int, int]:
     """KV heads [lo, hi) of `rank`: contiguous, equal shares in rank order."""
     if world < 1 or not 0 <= rank < world:
