@@ -315,3 +315,72 @@ def test_a_pinned_pool_refuses_to_grow():
     with pytest.raises(RuntimeError, match="reserve_rows"):
         pool._grow(pool.capacity + 1)
     ops._PINNED.pop(pool.decoders.data_ptr())
+
+
+# ---------------------------------------------------------------- decoder lifetime and memory
+def _rows(w, rows, seq_lens=None):
+    """A view of world `w` holding only requests `rows` (in that order)."""
+    st = dict(w["st"])
+    st["block_table"] = st["block_table"][rows]
+    st["seq_lens"] = st["seq_lens"][rows] if seq_lens is None else np.array(seq_lens, np.int32)
+    st["decoders"] = st["decoders"][rows]
+    st["pinvT"] = st["pinvT"][rows]
+    st["kv"] = [st["kv"][r] for r in rows]
+    return dict(w, st=st)
+
+
+def test_a_finished_requests_pool_row_goes_to_the_next_request_which_reads_correctly():
+    """Request 1 finishes and is released (the engine's completion hook); request 2's first chunk
+    then gets request 1's pool row, and a decode step over requests 0 and 2 reads each request's
+    own decoder from the pool."""
+    from vllm_ttkv import metadata as md_mod
+    w = _world(42, [70, 33, 41], fresh=(2,))
+    st = w["st"]
+    keys = [int(st["block_table"][r][0]) for r in range(3)]
+    s1 = rope_store.request_slot(keys[1])
+    assert s1 is not None and rope_store.request_slot(keys[2]) is None
+    md_mod.TTKVAttentionMetadataBuilder.release_finished([keys[1]])
+    assert rope_store.request_slot(keys[1]) is None
+    assert rope_store.decoder_for_request(w["layer"].layer_name, keys[1]) is None
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+    # request 2's first chunk: positions 0..39 (its store holds room for one more token)
+    w2 = _rows(w, [2], seq_lens=[40])
+    md, raw_k, value, q = _step(w2, [40])
+    _forward(impl, w2, md, raw_k, value, q, key=torch.randn(40, H, D, device="cuda").half())
+    assert rope_store.request_slot(keys[2]) == s1                       # the freed row, reused
+    kdec = rope_store.decoder_for_request(w["layer"].layer_name, keys[2])
+    # a decode step of requests 0 and 2 (request 2 now at 41 tokens)
+    w02 = _rows(w, [0, 2])
+    md2, raw_k2, value2, q2 = _step(w02, [1, 1], seed=3)
+    out = _forward(impl, w02, md2, raw_k2, value2, q2)
+    sta = _after(w02)
+    sta["decoders"] = np.stack([st["decoders"][0], kdec.decoder_f.cpu().numpy()])
+    _close(out, stores.expected_decode(sta, q=q2.float().cpu().numpy()))
+
+
+def test_a_decode_steps_peak_allocation_is_within_the_memory_accounting():
+    """The scratch a real step allocates (torch's peak over the step, fresh library buffers) is
+    covered by `memory.step_scratch_bytes`, and the accounting does not overstate it by more than
+    the parts a decode step does not use (the fit's tail)."""
+    from vllm_ttkv import memory, ops
+    w = _world(44, [300, 170, 257, 90, 33, 401, 12, 128])
+    md, raw_k, value, q = _step(w, [1] * 8)
+    impl = TTKVAttentionImpl(HQ, D, SCALE, H)
+    out = torch.empty(8, HQ, D, dtype=torch.float16, device="cuda")
+    ops.status_word(torch.device("cuda", torch.cuda.current_device()))
+    ops._WORKSPACE.clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    patch.stash_raw_k(w["layer"].layer_name, raw_k, None, w["table"])
+    impl.forward(w["layer"], q, None, value, w["page"], md, out)
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    lay = w["lay"]
+    predicted = memory.step_scratch_bytes([lay], 8, 1, int(w["st"]["seq_lens"].max()), HQ)
+    fit = int(ops._lib.lib().ttkv_fit_tail_scratch_bytes(lay.r1, lay.H, lay.H, lay.d))
+    print(f"decode step: peak {peak} B allocated, accounting {predicted} B (fit tail {fit} B)")
+    slack = 3 * (1 << 16) + (1 << 20)          # the 64 KiB floor of each cached buffer, small tensors
+    assert peak <= predicted + slack
+    assert predicted - fit <= peak + slack

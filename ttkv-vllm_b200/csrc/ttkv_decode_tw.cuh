@@ -39,7 +39,7 @@ namespace tw {
 
 using namespace tc;
 
-constexpr int NEPI = 128;                 // epilogue threads: one token of the tile each
+constexpr int NEPI = 256;                 // epilogue threads: two per token of the tile
 constexpr int NTHR = NEPI + 32;           // + the control warp
 constexpr uint32_t TMEM_COLS = 512;       // 2 x 128 reconstruction columns + 16 PV columns
 constexpr uint32_t PV_COL = 256;
@@ -49,7 +49,7 @@ struct TwGeom {            // host-computed shared-memory plan
     int natom, kp16;
     int cb, cf_pitch, cf_swz;
     int kr, vr, kvrow, nkv;
-    int off_bhi, off_blo, off_a, off_apv, off_bpv, off_q, off_lut, off_misc, off_bt, off_cf, off_kv;
+    int off_bhi, off_blo, off_a, off_apv, off_bpv, off_q, off_lut, off_misc, off_bt, off_cf, off_kv, off_xs;
     int smem;
 };
 
@@ -126,10 +126,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
     unsigned char* cfb = base + T.off_cf;                         // [token][cf_pitch]
     unsigned char* kvb = base + T.off_kv;                         // [buffer][token][K region | V region]
     int32_t* bts = reinterpret_cast<int32_t*>(base + T.off_bt);
+    float* xs = reinterpret_cast<float*>(base + T.off_xs);        // [half][g][token] partial scores
 
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const bool epi = tid < NEPI;
     const int t = tid & 127;                                      // epilogue: token / TMEM lane
+    const int half = (tid >> 7) & 1;                              // epilogue: which half of the lanes
     const int nh = P.n_heads;
     pdl_wait();
 
@@ -437,6 +439,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
             timed_out = tmo;
         } else {
             // ================================================================ epilogue
+            // thread (half, t): token t of the tile, RoPE pairs [32 half, 32 half + 32) -- the K
+            // lanes [32 half, +32) and [64 + 32 half, +32), bitmap bytes 4 half .. 4 half + 3 and
+            // 8 + 4 half .. -- and the V lanes [64 half, 64 half + 64), bitmap bytes 8 half .. + 7
             bool tmo = false;
             auto ewait = [&](uint64_t* bar, uint32_t& ph) {
                 if (tmo) return;
@@ -446,21 +451,24 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
             if (P.dec_image) {
                 s_up = P.dec_scales[int64_t(di) * P.H + h];
             } else {
-                // the decoder slice converted here: column t, power-of-two scale, fp16 hi + lo
+                // the decoder slice converted here: column t, power-of-two scale, fp16 hi + lo; the
+                // 8-row chunks split between the halves
                 const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * 128 + t;
                 const int64_t dstride = int64_t(P.H) * 128;
                 float mx = 0.f;
-                for (int rr = 0; rr < P.r1; ++rr) mx = fmaxf(mx, fabsf(dec[rr * dstride]));
+                for (int rr = half; rr < P.r1; rr += 2) mx = fmaxf(mx, fabsf(dec[rr * dstride]));
                 mx = warp_max(mx);
                 if (lane == 0) M->maxabs[w] = mx;
                 epi_sync();
-                mx = fmaxf(fmaxf(M->maxabs[0], M->maxabs[1]), fmaxf(M->maxabs[2], M->maxabs[3]));
+                mx = 0.f;
+                #pragma unroll
+                for (int i = 0; i < NEPI / 32; ++i) mx = fmaxf(mx, M->maxabs[i]);
                 int e = 0;
                 if (mx > 0.f) e = int((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13;
                 e = max(-100, min(100, e));
                 const float s_down = __uint_as_float(uint32_t(127 - e) << 23);
                 s_up = __uint_as_float(uint32_t(127 + e) << 23);
-                for (int cidx = 0; cidx < T.kp16 / 8; ++cidx) {
+                for (int cidx = half; cidx < T.kp16 / 8; cidx += 2) {
                     uint32_t hw[4], lw[4];
                     #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -482,11 +490,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
             }
 
             // A: token t's coefficients as exact fp16 (int8 -> 1024 + byte under the fp16 exponent,
-            // minus 1152), zero past r1 and for a token past the segment; returns its ruler
+            // minus 1152), zero past r1 and for a token past the segment, 16-coefficient chunks
+            // split between the halves; returns the token's ruler
             auto convert_a = [&](bool valid) {
                 const unsigned char* srow = cfb + t * T.cf_pitch;
                 const int swz = t & T.cf_swz;
-                for (int c16 = 0; c16 < T.kp16 / 16; ++c16) {
+                for (int c16 = half; c16 < T.kp16 / 16; c16 += 2) {
                     uint4 raw = valid ? *reinterpret_cast<const uint4*>(srow + 16 * (c16 ^ swz)) : make_uint4(0, 0, 0, 0);
                     const int left = P.r1 - 16 * c16;
                     uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -545,21 +554,21 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 const int kb = T.nkv == 2 ? (it & 1) : 0;
                 const float csp = csp_next;
 
-                // ---- this token's RoPE row (cos | sin), read early from L2 / HBM
-                uint4 cosw[8], sinw[8];
+                // ---- this token's RoPE row for this half's pairs (cos | sin), read early from L2
+                uint4 cosw[4], sinw[4];
                 {
                     const uint4* trow = reinterpret_cast<const uint4*>(
                         reinterpret_cast<const uint16_t*>(P.table) +
-                        int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128);
+                        int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128) + 4 * half;
                     #pragma unroll
-                    for (int i = 0; i < 8; ++i) { cosw[i] = __ldg(trow + i); sinw[i] = __ldg(trow + 8 + i); }
+                    for (int i = 0; i < 4; ++i) { cosw[i] = __ldg(trow + i); sinw[i] = __ldg(trow + 8 + i); }
                 }
 
-                // ---- K residual: bitmap, and the code window of each of the 16 bitmap bytes
+                // ---- K residual: bitmap, and the code windows of this half's 8 bitmap bytes
                 if (kb) ewait(&M->mb_kv[1], ph_kv1); else ewait(&M->mb_kv[0], ph_kv0);
                 const unsigned char* kvrow = kvb + (size_t(kb) * TM + t) * T.kvrow;
                 const uint32_t kv_off = uint32_t(kvrow - base);
-                uint32_t kbw[4], kwin[16];
+                uint32_t kbw[4], kwin[8];
                 float krs;
                 {
                     const uint4* kp = reinterpret_cast<const uint4*>(kvrow);
@@ -572,8 +581,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     pre[2] = pre[1] + __popc(kbw[1]);
                     pre[3] = pre[2] + __popc(kbw[2]);
                     #pragma unroll
-                    for (int g8 = 0; g8 < 16; ++g8)
-                        kwin[g8] = window32(base, kv_off + uint32_t(koff + 16), uint32_t(byte_rank(kbw, pre, g8) * kbits)) ^ kflip;
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const int gb = (q4 < 4 ? 0 : 8) + 4 * half + (q4 & 3);
+                        kwin[q4] = window32(base, kv_off + uint32_t(koff + 16), uint32_t(byte_rank(kbw, pre, gb) * kbits)) ^ kflip;
+                    }
                     krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
                 }
 
@@ -588,7 +599,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     for (int g = 0; g < G; ++g) o[g] = fmaf(o[g], corr_prev[g], pvv[g] + pvv[G + g]);
                 }
 
-                // ---- V^T (MN-major): all 128 lanes of this token as exact small integers
+                // ---- V^T (MN-major): this half's 64 lanes of the token as exact small integers
                 float vrs;
                 {
                     const unsigned char* vrow = kvrow + T.kr;
@@ -598,10 +609,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     bitmap_words(vp[0], vp[1], voff, bw);
                     if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
                     trim_bitmap(bw, P.v_lanes);
-                    int rank0 = 0;
+                    int rank0 = half ? __popc(bw[0]) + __popc(bw[1]) : 0;
                     #pragma unroll
-                    for (int wq = 0; wq < 4; ++wq) {
-                        const uint32_t word = bw[wq];
+                    for (int wq = 0; wq < 2; ++wq) {
+                        const uint32_t word = half ? bw[2 + wq] : bw[wq];
                         #pragma unroll
                         for (int gi = 0; gi < 4; ++gi) {
                             const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
@@ -616,7 +627,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                                 const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&x), vbias2);
                                 hv[k] = *reinterpret_cast<const uint32_t*>(&y);
                             }
-                            const int ch = 4 * wq + gi;
+                            const int ch = 8 * half + 4 * wq + gi;
                             const uint32_t off = uint32_t((t >> 3) * 2048 + (ch >> 3) * 1024 + (t & 7) * 128 +
                                                           (((ch & 7) ^ (t & 7)) << 4));
                             *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
@@ -639,33 +650,33 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     mbar_arrive(&M->mb_cff);
                 }
 
-                // ---- rebuild, patch, rotate, score: 8 pairs (j, j + 64) at a time
+                // ---- rebuild, patch, rotate, score this half's pairs: 8 pairs (j, j + 64) at a time
                 float2 s2[G], s2h[G];
                 #pragma unroll
                 for (int g = 0; g < G; ++g) { s2[g] = make_float2(0.f, 0.f); s2h[g] = s2[g]; }
                 {
                     const uint32_t rcol = uint32_t(it & 1) * 128u;
                     const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
-                    const float2 neg1 = make_float2(-1.f, -1.f);
                     #pragma unroll
-                    for (int hp = 0; hp < 8; ++hp) {
-                        const int j0 = 8 * hp;
+                    for (int hp = 0; hp < 4; ++hp) {
+                        const int j0 = 32 * half + 8 * hp;
                         float al[8], ah[8];
                         tmem_ld8(t_row + rcol + uint32_t(j0), al);
                         tmem_ld8(t_row + rcol + uint32_t(64 + j0), ah);
                         float rl[8], rh[8];
                         {
                             uint32_t f[8];
-                            group_fields(kwin[hp], bitmap_byte(kbw, hp), kbits, lutk, f);
+                            group_fields(kwin[hp], bitmap_byte(kbw, 4 * half + hp), kbits, lutk, f);
                             #pragma unroll
-                            for (int k = 0; k < 8; ++k) rl[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
-                            group_fields(kwin[8 + hp], bitmap_byte(kbw, 8 + hp), kbits, lutk, f);
+                            for (int k = 0; k < 8; ++k) rl[k] = __uint_as_float((f[k] & kmask) ^ kmag);
+                            group_fields(kwin[4 + hp], bitmap_byte(kbw, 8 + 4 * half + hp), kbits, lutk, f);
                             #pragma unroll
-                            for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag) - kmag_f;
+                            for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag);
                         }
                         tmem_wait_ld();
                         const uint32_t cwv[4] = {cosw[hp].x, cosw[hp].y, cosw[hp].z, cosw[hp].w};
                         const uint32_t swv[4] = {sinw[hp].x, sinw[hp].y, sinw[hp].z, sinw[hp].w};
+                        const float2 mag2 = make_float2(-kmag_f, -kmag_f);
                         #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             float2 cz, sz;
@@ -676,11 +687,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                                 cz = __half22float2(*reinterpret_cast<const __half2*>(&cwv[i]));
                                 sz = __half22float2(*reinterpret_cast<const __half2*>(&swv[i]));
                             }
-                            const float2 kl = f2fma(make_float2(rl[2 * i], rl[2 * i + 1]), krs2,
-                                                    f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
-                            const float2 kh = f2fma(make_float2(rh[2 * i], rh[2 * i + 1]), krs2,
-                                                    f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
-                            const float2 yl = f2fma(f2mul(kh, neg1), sz, f2mul(kl, cz));
+                            // residual codes as exact floats (magic 2^23 + code, minus the magic)
+                            const float2 rl2 = f2add(make_float2(rl[2 * i], rl[2 * i + 1]), mag2);
+                            const float2 rh2 = f2add(make_float2(rh[2 * i], rh[2 * i + 1]), mag2);
+                            const float2 kl = f2fma(rl2, krs2, f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
+                            const float2 kh = f2fma(rh2, krs2, f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
+                            const float2 yl = f2sub(f2mul(kl, cz), f2mul(kh, sz));
                             const float2 yh = f2fma(kl, sz, f2mul(kh, cz));
                             #pragma unroll
                             for (int g = 0; g < G; ++g) {
@@ -693,37 +705,44 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 }
                 tc_before();        // this tile's reconstruction columns are read (next use: tile it + 2)
 
-                // ---- online softmax over the tile: one named barrier (a reduction that also makes
-                // a timeout anywhere in the epilogue everyone's), the maxima double-buffered by tile
+                // ---- the two halves' partial scores, then the online softmax over the tile. The
+                // first barrier is a reduction that also makes a timeout anywhere in the epilogue
+                // everyone's; the maxima are double-buffered by tile parity
+                #pragma unroll
+                for (int g = 0; g < G; ++g) xs[(half * kMaxG + g) * 128 + t] = (s2[g].x + s2h[g].x) + (s2[g].y + s2h[g].y);
+                if (epi_any(tmo)) { tmo = true; break; }
                 float sc[G];
                 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float v = (s2[g].x + s2h[g].x) + (s2[g].y + s2h[g].y);
+                    const float v = xs[g * 128 + t] + xs[(kMaxG + g) * 128 + t];       // same order in both halves
                     sc[g] = (valid && tok < lim[g]) ? v * scale : -INFINITY;
                     const float mxg = warp_max(sc[g]);
                     if (lane == 0) M->red_max[it & 1][w][g] = mxg;
                 }
-                if (epi_any(tmo)) { tmo = true; break; }
+                epi_sync();
                 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float tmax = fmaxf(fmaxf(M->red_max[it & 1][0][g], M->red_max[it & 1][1][g]),
-                                             fmaxf(M->red_max[it & 1][2][g], M->red_max[it & 1][3][g]));
+                    float tmax = M->red_max[it & 1][0][g];
+                    #pragma unroll
+                    for (int i = 1; i < NEPI / 32; ++i) tmax = fmaxf(tmax, M->red_max[it & 1][i][g]);
                     const float m_new = fmaxf(m_run[g], tmax);
                     const float pg = (m_new == -INFINITY || sc[g] == -INFINITY) ? 0.f : expf(sc[g] - m_new);
                     const float corr = (m_run[g] == -INFINITY) ? 0.f : expf(m_run[g] - m_new);
                     lsum[g] = fmaf(lsum[g], corr, pg);
                     corr_prev[g] = corr;
                     m_run[g] = m_new;
-                    const float pv = pg * vrs;
-                    const uint32_t hb = f16_bits(pv);
-                    const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
-                    const int kt = t & 63, atom = t >> 6;
-                    #pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const int n = k == 0 ? g : G + g;
-                        const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
-                                                      (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
-                        *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
+                    if ((g & 1) == half) {                               // P' column g: one half writes it
+                        const float pv = pg * vrs;
+                        const uint32_t hb = f16_bits(pv);
+                        const uint32_t lb = f16_bits(pv - f16_bits_to_f32(hb));
+                        const int kt = t & 63, atom = t >> 6;
+                        #pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const int n = k == 0 ? g : G + g;
+                            const uint32_t off = uint32_t(atom * 2048 + (n >> 3) * 1024 + (n & 7) * 128 +
+                                                          (((kt >> 3) ^ (n & 7)) << 4) + (kt & 7) * 2);
+                            *reinterpret_cast<uint16_t*>(bpv + off) = uint16_t(k == 0 ? hb : lb);
+                        }
                     }
                 }
                 fence_async_smem();
@@ -744,24 +763,28 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 }
             }
             tmo = epi_any(tmo);
-            // softmax denominators: each warp's token sums
-            #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float sum = lsum[g];
+            // softmax denominators: the token sums of half 0's warps (half 1 holds the same)
+            if (half == 0) {
                 #pragma unroll
-                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                if (lane == 0) M->red_sum[w][g] = sum;
+                for (int g = 0; g < G; ++g) {
+                    float sum = lsum[g];
+                    #pragma unroll
+                    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                    if (lane == 0) M->red_sum[w][g] = sum;
+                }
             }
             epi_sync();
-            #pragma unroll
-            for (int g = 0; g < G; ++g) P.part_o[(slot * G + g) * 128 + t] = tmo ? 0.f : o[g];
-            if (t < G) {
-                float mt = -INFINITY;
+            if (half == 0) {
                 #pragma unroll
-                for (int g = 0; g < G; ++g) if (g == t) mt = m_run[g];
-                const float l = M->red_sum[0][t] + M->red_sum[1][t] + M->red_sum[2][t] + M->red_sum[3][t];
-                P.part_ml[(slot * G + t) * 2 + 0] = tmo ? -INFINITY : mt;
-                P.part_ml[(slot * G + t) * 2 + 1] = tmo ? 0.f : l;
+                for (int g = 0; g < G; ++g) P.part_o[(slot * G + g) * 128 + t] = tmo ? 0.f : o[g];
+                if (t < G) {
+                    float mt = -INFINITY;
+                    #pragma unroll
+                    for (int g = 0; g < G; ++g) if (g == t) mt = m_run[g];
+                    const float l = M->red_sum[0][t] + M->red_sum[1][t] + M->red_sum[2][t] + M->red_sum[3][t];
+                    P.part_ml[(slot * G + t) * 2 + 0] = tmo ? -INFINITY : mt;
+                    P.part_ml[(slot * G + t) * 2 + 1] = tmo ? 0.f : l;
+                }
             }
             timed_out = tmo;
         }
@@ -838,6 +861,7 @@ inline TwGeom tw_geom(const ttkv_layout_t* lay, int G) {
         T.off_lut = off; off += LUT_BYTES;
         T.off_misc = off; off += misc;
         T.off_bt = off; off += BT_CAP * 4;
+        T.off_xs = off; off += 2 * kMaxG * TM * 4;
         T.off_cf = off; off += TM * T.cf_pitch;
         T.off_kv = off; off += nkv * TM * T.kvrow + KV_PAD;
         T.nkv = nkv;
