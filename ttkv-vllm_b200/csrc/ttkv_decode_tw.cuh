@@ -7,23 +7,25 @@
 // Why a second kernel. In decode_tc_kernel four warpgroups split each token's 128 head lanes, so
 // every per-token cost that does not scale with lanes (the bitmaps, the rulers, the softmax, the
 // partial-score exchange, the barriers) is paid four times per token, and the SIMT issue slots,
-// not HBM, bound the read. Here ONE thread owns a whole (token, KV head): it decodes all 128
-// residual lanes and all 128 V lanes, rotates, scores all G query heads and runs the softmax of its
-// token, with no exchange between threads except the tile maximum.
+// not HBM, bound the read. Here two threads own a (token, KV head): each decodes 64 residual lanes
+// and 64 V lanes and scores its half of the rotation pairs for all G query heads; they exchange one
+// partial score per query head, and both run the token's softmax.
 //
-// Roles. Threads 0..127 (four warps, TMEM lanes 0..127) are the epilogue: thread t is token t of
-// the current 128-token tile. Warp 4 is the control warp: its 32 lanes stage the tile's slot fields
+// Roles. Threads 0..255 (eight warps; warps w and w + 4 share TMEM lanes 32 (w & 3) ..) are the
+// epilogue: threads t and 128 + t are token t of the current 128-token tile, each with half of the
+// head's lanes (a quarter of the old kernel's per-token overhead, half its code per thread), their
+// partial scores summed through shared memory. Warp 8 is the control warp: its 32 lanes stage the tile's slot fields
 // with 16-byte cp.async (chunk-fastest over the tokens), and its lane 0 issues the MMAs. The two
 // sides meet only on mbarriers:
 //
 //   epilogue (tile j)                                      control, on each hand-off
 //   ----------------------------------------------------  ------------------------------------------
 //   wait K/V rows (j): bitmaps, code windows, rulers
-//   wait PV (j-1): fold it into o
-//   V codes -> V^T (fp16 integers)          -> K/V free    K/V rows of tile j+2 (or j+1) into it
 //   wait MMA 1 (j); coefficients (j+1) -> A -> A ready     MMA 1 (j+1); coefficients (j+2) staged
 //   k = acc * (cs 2^e) + residual, RoPE, scores            (MMA 1 (j+1) runs under this epilogue)
-//   tile max (one named barrier), p, P'     -> PV ready    PV (j)
+//   wait PV (j-1) (long done): fold it into o
+//   V codes -> V^T (fp16 integers)          -> K/V free    K/V rows of tile j+2 (or j+1) into it
+//   partial scores exchanged, tile max, p, P' -> PV ready  PV (j)
 //
 //   MMA 1   acc[128 tokens x 128 lanes] = A . B_hi + A . B_lo in TMEM (two column sets, so MMA 1 of
 //           the next tile runs under this tile's epilogue), A = int8 coefficients as exact fp16, B =
@@ -403,9 +405,13 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 if (j + 1 < n_tiles) issue_cf(j + 1);
             };
             // the control loop follows the epilogue's hand-offs of tile j in the order they come:
-            // K/V rows consumed, A(j + 1) converted, V^T and P' written
+            // A(j + 1) converted, K/V rows consumed, V^T and P' written
             recon(0);
             for (int j = 0; j < n_tiles && !tmo; ++j) {
+                if (j + 1 < n_tiles) {
+                    recon(j + 1);
+                    if (tmo) break;
+                }
                 if (T.nkv == 2) {
                     if (j & 1) cwait(&M->mb_kvf[1], ph_kvf1); else cwait(&M->mb_kvf[0], ph_kvf0);
                     tmo = __any_sync(0xffffffffu, tmo);
@@ -416,10 +422,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     tmo = __any_sync(0xffffffffu, tmo);
                     if (tmo) break;
                     if (j + 1 < n_tiles) issue_kv(j + 1);
-                }
-                if (j + 1 < n_tiles) {
-                    recon(j + 1);
-                    if (tmo) break;
                 }
                 cwait(&M->mb_pvr, ph_pvr);
                 tmo = __any_sync(0xffffffffu, tmo);
@@ -588,55 +590,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
                 }
 
-                // ---- PV of the previous tile: this thread is head lane t of every query head
-                if (it > 0) {
-                    ewait(&M->mb_pv, ph_pv);
-                    tc_after();
-                    float pvv[16];
-                    tmem_ld16(t_row + PV_COL, pvv);
-                    tmem_wait_ld();
-                    #pragma unroll
-                    for (int g = 0; g < G; ++g) o[g] = fmaf(o[g], corr_prev[g], pvv[g] + pvv[G + g]);
-                }
-
-                // ---- V^T (MN-major): this half's 64 lanes of the token as exact small integers
-                float vrs;
-                {
-                    const unsigned char* vrow = kvrow + T.kr;
-                    const uint32_t vfo = kv_off + uint32_t(T.kr + voff);
-                    const uint4* vp = reinterpret_cast<const uint4*>(vrow);
-                    uint32_t bw[4];
-                    bitmap_words(vp[0], vp[1], voff, bw);
-                    if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
-                    trim_bitmap(bw, P.v_lanes);
-                    int rank0 = half ? __popc(bw[0]) + __popc(bw[1]) : 0;
-                    #pragma unroll
-                    for (int wq = 0; wq < 2; ++wq) {
-                        const uint32_t word = half ? bw[2 + wq] : bw[wq];
-                        #pragma unroll
-                        for (int gi = 0; gi < 4; ++gi) {
-                            const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
-                            const int rank = rank0 + (gi ? __popc(word >> (32 - 8 * gi)) : 0);
-                            const uint32_t win = window32(base, vfo + 16u, uint32_t(rank * vbits)) ^ vflip;
-                            uint32_t f[8];
-                            group_fields(win, byte, vbits, lutv, f);
-                            uint32_t hv[4];
-                            #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const uint32_t x = (__byte_perm(f[2 * k], f[2 * k + 1], 0x5410) & vmask2) ^ vmag2;
-                                const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&x), vbias2);
-                                hv[k] = *reinterpret_cast<const uint32_t*>(&y);
-                            }
-                            const int ch = 8 * half + 4 * wq + gi;
-                            const uint32_t off = uint32_t((t >> 3) * 2048 + (ch >> 3) * 1024 + (t & 7) * 128 +
-                                                          (((ch & 7) ^ (t & 7)) << 4));
-                            *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                        }
-                        rank0 += __popc(word);
-                    }
-                    vrs = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
-                }
-                mbar_arrive(&M->mb_kvf[kb]);                       // the K/V rows are in registers / V^T
 
                 // ---- MMA 1 of this tile done: A takes the next tile's coefficients
                 ewait(&M->mb_r, ph_r);
@@ -704,6 +657,56 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                     }
                 }
                 tc_before();        // this tile's reconstruction columns are read (next use: tile it + 2)
+
+                // ---- PV of the previous tile: this thread is head lane t of every query head
+                if (it > 0) {
+                    ewait(&M->mb_pv, ph_pv);
+                    tc_after();
+                    float pvv[16];
+                    tmem_ld16(t_row + PV_COL, pvv);
+                    tmem_wait_ld();
+                    #pragma unroll
+                    for (int g = 0; g < G; ++g) o[g] = fmaf(o[g], corr_prev[g], pvv[g] + pvv[G + g]);
+                }
+
+                // ---- V^T (MN-major): this half's 64 lanes of the token as exact small integers
+                float vrs;
+                {
+                    const unsigned char* vrow = kvrow + T.kr;
+                    const uint32_t vfo = kv_off + uint32_t(T.kr + voff);
+                    const uint4* vp = reinterpret_cast<const uint4*>(vrow);
+                    uint32_t bw[4];
+                    bitmap_words(vp[0], vp[1], voff, bw);
+                    if (!valid) bw[0] = bw[1] = bw[2] = bw[3] = 0u;
+                    trim_bitmap(bw, P.v_lanes);
+                    int rank0 = half ? __popc(bw[0]) + __popc(bw[1]) : 0;
+                    #pragma unroll
+                    for (int wq = 0; wq < 2; ++wq) {
+                        const uint32_t word = half ? bw[2 + wq] : bw[wq];
+                        #pragma unroll
+                        for (int gi = 0; gi < 4; ++gi) {
+                            const uint32_t byte = (word >> (24 - 8 * gi)) & 0xffu;
+                            const int rank = rank0 + (gi ? __popc(word >> (32 - 8 * gi)) : 0);
+                            const uint32_t win = window32(base, vfo + 16u, uint32_t(rank * vbits)) ^ vflip;
+                            uint32_t f[8];
+                            group_fields(win, byte, vbits, lutv, f);
+                            uint32_t hv[4];
+                            #pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t x = (__byte_perm(f[2 * k], f[2 * k + 1], 0x5410) & vmask2) ^ vmag2;
+                                const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&x), vbias2);
+                                hv[k] = *reinterpret_cast<const uint32_t*>(&y);
+                            }
+                            const int ch = 8 * half + 4 * wq + gi;
+                            const uint32_t off = uint32_t((t >> 3) * 2048 + (ch >> 3) * 1024 + (t & 7) * 128 +
+                                                          (((ch & 7) ^ (t & 7)) << 4));
+                            *reinterpret_cast<uint4*>(apv + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                        }
+                        rank0 += __popc(word);
+                    }
+                    vrs = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
+                }
+                mbar_arrive(&M->mb_kvf[kb]);                       // the K/V rows are in registers / V^T
 
                 // ---- the two halves' partial scores, then the online softmax over the tile. The
                 // first barrier is a reduction that also makes a timeout anywhere in the epilogue
