@@ -557,14 +557,12 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                 const float csp = csp_next;
 
                 // ---- this token's RoPE row for this half's pairs (cos | sin), read early from L2
-                uint4 cosw[4], sinw[4];
-                {
-                    const uint4* trow = reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const uint16_t*>(P.table) +
-                        int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128) + 4 * half;
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) { cosw[i] = __ldg(trow + i); sinw[i] = __ldg(trow + 8 + i); }
-                }
+                // (16 bytes of cos and of sin per 8 pairs; the first chunk's now, each next one a chunk
+                // ahead of its use, so only two chunks are held in registers at a time)
+                const uint4* trow = reinterpret_cast<const uint4*>(
+                    reinterpret_cast<const uint16_t*>(P.table) +
+                    int64_t(min(valid ? tok : t_begin, int(P.table_rows - 1))) * 128) + 4 * half;
+                uint4 cos_next = __ldg(trow), sin_next = __ldg(trow + 8);
 
                 // ---- K residual: bitmap, and the code windows of this half's 8 bitmap bytes
                 if (kb) ewait(&M->mb_kv[1], ph_kv1); else ewait(&M->mb_kv[0], ph_kv0);
@@ -627,8 +625,10 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tw_kernel(const ReadParams P, 
                             for (int k = 0; k < 8; ++k) rh[k] = __uint_as_float((f[k] & kmask) ^ kmag);
                         }
                         tmem_wait_ld();
-                        const uint32_t cwv[4] = {cosw[hp].x, cosw[hp].y, cosw[hp].z, cosw[hp].w};
-                        const uint32_t swv[4] = {sinw[hp].x, sinw[hp].y, sinw[hp].z, sinw[hp].w};
+                        const uint4 cw = cos_next, sw = sin_next;
+                        if (hp < 3) { cos_next = __ldg(trow + hp + 1); sin_next = __ldg(trow + 9 + hp); }
+                        const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w};
+                        const uint32_t swv[4] = {sw.x, sw.y, sw.z, sw.w};
                         const float2 mag2 = make_float2(-kmag_f, -kmag_f);
                         #pragma unroll
                         for (int i = 0; i < 4; ++i) {

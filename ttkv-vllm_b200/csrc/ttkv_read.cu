@@ -836,6 +836,8 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                 batch->seq_lens, q_start, q_len, batch->n_reqs, c.nqb, Gq, kContRows, v_seq, v_req,
                 v_qrow, v_nq, v_pos, v_f0, status);
             if (int e = check_launch("cont_blocks_kernel")) return e;
+            if (tw_serves(lay, lay->H * kContRows))                       // the token-wide kernel, 8 rows
+                return launch_tw(P, tw::tw_geom(lay, kContRows), c.n_v, st);
             return launch_tc(P, TC, mc, c.pl, c.n_v, st);
         }
     }
