@@ -43,8 +43,7 @@ METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs pe
 # each slot byte once, so traffic grows in proportion to the rows and widths a launch reads); when
 # the sources no longer hash the same, the capture describes another kernel and `traffic` is null.
 CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": None, "src_sha16": None, "kernel": None}
-READ_SOURCES = ("ttkv-vllm_b200/csrc/ttkv_read.cu", "ttkv-vllm_b200/csrc/ttkv_decode_tc.cuh",
-                "ttkv-vllm_b200/csrc/ttkv_decode_tw.cuh")
+READ_SOURCES = ("ttkv-vllm_b200/csrc/ttkv_read.cu", "ttkv-vllm_b200/csrc/ttkv_decode_tc.cuh")
 
 
 def read_src_sha16() -> str:
@@ -1043,8 +1042,7 @@ def main():
                                       "one CUDA graph per layer (write + read), all-gathers between"),},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
-                             "kernel": "decode_tw_kernel<3> + merge_sk_kernel (ttkv_decode_paged; "
-                                       "decode_tc_kernel<3> where the token-wide plan does not fit)",
+                             "kernel": "decode_tc_kernel<3> + merge_sk_kernel (ttkv_decode_paged)",
                              "alg_bytes_per_launch": alg_bytes / wl.L,
                              "launch_us": dec_total_ms * 1e3 / wl.L,
                              "traffic_source": traffic_src,

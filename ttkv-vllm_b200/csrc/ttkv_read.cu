@@ -22,7 +22,6 @@
 
 #include <algorithm>
 #include <cfloat>
-#include <cstdlib>
 #include <cstring>
 #include <cmath>
 #include <mutex>
@@ -447,7 +446,6 @@ __global__ void __launch_bounds__(128) merge_kernel(const ReadParams P) {
 }
 
 #include "ttkv_decode_tc.cuh"
-#include "ttkv_decode_tw.cuh"
 
 // ------------------------------------------------------------------ host side
 int qblock_for(int G, bool multi) {
@@ -527,19 +525,6 @@ Plan make_plan_tc(const ttkv_layout_t* lay, int n_reqs, int HQ, int max_seq, int
     pl.part_ml_bytes = slots * G * 2 * sizeof(float);
     pl.smem = size_t(tc::tc_geom(lay, G).smem);
     return pl;
-}
-
-// Whether the token-wide tensor-core decode (one thread per token and KV head) serves the layout:
-// the same conditions as the quarter-lane kernel, and its shared-memory plan must fit. Setting
-// TTKV_READ_KERNEL=quarter keeps every decode on the quarter-lane kernel (a diagnostic switch for
-// comparing the two; both compute the same outputs).
-bool tw_serves(const ttkv_layout_t* lay, int HQ) {
-    static const bool off = [] {
-        const char* e = std::getenv("TTKV_READ_KERNEL");
-        return e && std::strcmp(e, "quarter") == 0;
-    }();
-    const int G = HQ / lay->H;
-    return !off && tc_serves(lay, HQ) && tw::tw_geom(lay, G).smem > 0;
 }
 
 // Continuation chunks on the tensor-core decode: the (query, query head) rows of a request's
@@ -666,45 +651,6 @@ int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps
     e = cudaLaunchKernelEx(&cfg, tc::merge_sk_kernel, P);
     if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "merge_sk_kernel: %s", cudaGetErrorString(e));
     return TTKV_OK;
-}
-
-template <int G>
-int launch_tw_g(const ReadParams& P, const tw::TwGeom& T, int n_reqs, cudaStream_t st) {
-    auto k = tw::decode_tw_kernel<G>;
-    if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "decode_tw_kernel")) return e;
-    // both launches may start while the kernel before them runs (programmatic dependent launch)
-    cudaLaunchAttribute pdl[1];
-    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pdl[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(P.n_ctas);
-    cfg.blockDim = dim3(tw::NTHR);
-    cfg.dynamicSmemBytes = T.smem;
-    cfg.stream = st;
-    cfg.attrs = pdl;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k, P, T);
-    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "decode_tw_kernel: %s", cudaGetErrorString(e));
-    cfg.gridDim = dim3(P.G, P.n_heads, n_reqs);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = 0;
-    e = cudaLaunchKernelEx(&cfg, tc::merge_sk_kernel, P);
-    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "merge_sk_kernel: %s", cudaGetErrorString(e));
-    return TTKV_OK;
-}
-
-int launch_tw(const ReadParams& P, const tw::TwGeom& T, int n_reqs, cudaStream_t st) {
-    switch (P.G) {
-        case 1: return launch_tw_g<1>(P, T, n_reqs, st);
-        case 2: return launch_tw_g<2>(P, T, n_reqs, st);
-        case 3: return launch_tw_g<3>(P, T, n_reqs, st);
-        case 4: return launch_tw_g<4>(P, T, n_reqs, st);
-        case 5: return launch_tw_g<5>(P, T, n_reqs, st);
-        case 6: return launch_tw_g<6>(P, T, n_reqs, st);
-        case 7: return launch_tw_g<7>(P, T, n_reqs, st);
-        case 8: return launch_tw_g<8>(P, T, n_reqs, st);
-    }
-    return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
 }
 
 int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
@@ -836,17 +782,11 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                 batch->seq_lens, q_start, q_len, batch->n_reqs, c.nqb, Gq, kContRows, v_seq, v_req,
                 v_qrow, v_nq, v_pos, v_f0, status);
             if (int e = check_launch("cont_blocks_kernel")) return e;
-            if (tw_serves(lay, lay->H * kContRows))                       // the token-wide kernel, 8 rows
-                return launch_tw(P, tw::tw_geom(lay, kContRows), c.n_v, st);
             return launch_tc(P, TC, mc, c.pl, c.n_v, st);
         }
     }
-    // the token-wide kernel where its plan fits (same schedule and partials as the quarter-lane one)
-    const bool use_tw = use_tc && tw_serves(lay, HQ);
-    const tw::TwGeom TW = use_tw ? tw::tw_geom(lay, HQ / lay->H) : tw::TwGeom{};
-    Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads, cache->block_size)
-                     : make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
-    if (use_tw) pl.smem = size_t(TW.smem);
+    const Plan pl = use_tc ? make_plan_tc(lay, batch->n_reqs, HQ, max_seq_len, n_heads, cache->block_size)
+                           : make_plan(lay, batch->n_reqs, HQ, max_q_len, max_seq_len, n_heads, multi);
     if (pl.smem > 227 * 1024) return fail(TTKV_ERR_UNSUPPORTED, "r1=%d needs %zu B of shared memory", lay->r1, pl.smem);
     if (!workspace || ws_bytes < pl.part_o_bytes + pl.part_ml_bytes)
         return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, pl.part_o_bytes + pl.part_ml_bytes);
@@ -860,7 +800,6 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     P.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes);
     P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (use_tw) return launch_tw(P, TW, batch->n_reqs, st);
     if (use_tc) return launch_tc(P, T, maps, pl, batch->n_reqs, st);
     return multi ? launch<true>(P, pl, batch->n_reqs, st) : launch<false>(P, pl, batch->n_reqs, st);
 }
