@@ -784,9 +784,6 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying a CUDA graph per step")
-    ap.add_argument("--layer-graphs", action="store_true",
-                    help="several GPUs: one CUDA graph per layer with the all-gathers outside them "
-                         "(default: one graph per step with the all-gathers captured in it)")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "encode", "sweep", "dense"],
                     help="decode: config 1 (the default line); sweep: config 2; prefill: config 3; "
@@ -866,49 +863,30 @@ def main():
             sh.pack(wl.out[l], bufs[l][0])
 
     graphs = None
-    whole_step = True                                 # one graph holds the whole step
-
-    def run_steps(k):
-        for _ in range(k):
-            if graphs is not None and whole_step:
-                graphs[0].replay()                         # the whole step (all-gathers included)
-                continue
-            for l in range(wl.L):
-                if graphs is not None:
-                    graphs[l].replay()
-                else:
-                    layer_work(l)
-                if sh is not None:                         # collectives between the layer graphs
-                    sh.gather(*bufs[l])
-                    sh.assemble(bufs[l][1], wl.out[l])     # every rank ends with all heads
 
     def step_work():
         for l in range(wl.L):
             layer_work(l)
-            if sh is not None:
+            if sh is not None:                             # this layer's heads from every rank
                 sh.gather(*bufs[l])
-                sh.assemble(bufs[l][1], wl.out[l])
+                sh.assemble(bufs[l][1], wl.out[l])         # every rank ends with all heads
+
+    def run_steps(k):
+        for _ in range(k):
+            if graphs is not None:
+                graphs[0].replay()                         # the whole step (all-gathers included)
+            else:
+                step_work()
 
     run_steps(args.warmup)
     if not args.no_graph:
-        # CUDA graphs captured after the warm-up allocated every workspace (and, on several GPUs,
-        # after the NCCL communicator ran its first collectives); the replays launch exactly the
-        # kernels the eager steps launch. One graph for the whole step, each layer's all-gather
-        # captured in it; --layer-graphs keeps the collectives outside, one graph per layer
+        # one CUDA graph for the whole step, captured after the warm-up allocated every workspace
+        # (and, on several GPUs, after the NCCL communicator ran its first collectives); the 28
+        # all-gathers are captured in it. The replays launch exactly the eager steps' kernels
         torch.cuda.synchronize(device)
-        graphs = []
-        whole_step = sh is None or not args.layer_graphs
-        if whole_step:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                step_work()
-            graphs.append(g)
-        else:
-            for l in range(wl.L):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    layer_work(l)
-                graphs.append(g)
+        graphs = [torch.cuda.CUDAGraph()]
+        with torch.cuda.graph(graphs[0]):
+            step_work()
         torch.cuda.synchronize(device)
     run_steps(args.warmup)
     torch.cuda.synchronize(device)
@@ -1037,9 +1015,7 @@ def main():
                            "storage": ("storage-sharded: coefficient block + this rank's heads' rows"
                                        if world > 1 else "full blobs"),
                            "launch": ("eager" if not graphs else "one CUDA graph per step" if sh is None
-                                      else "one CUDA graph per step, the 28 all-gathers captured in it"
-                                      if whole_step else
-                                      "one CUDA graph per layer (write + read), all-gathers between"),},
+                                      else "one CUDA graph per step, the 28 all-gathers captured in it"),},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                              "kernel": "decode_tc_kernel<3> + merge_sk_kernel (ttkv_decode_paged)",
