@@ -193,101 +193,166 @@ struct EncParams {
     int32_t* status;
 };
 
-// grid (heads written, n_tok), 128 threads: CTA x = KV head h_lo + x.
-__global__ void __launch_bounds__(128) encode_pack_kernel(const EncParams P) {
-    const int h = P.h_lo + int(blockIdx.x), t = blockIdx.y, hs = int(blockIdx.x);
+// ------------------------------------------------------------------ encode + pack, many tokens a CTA
+// The write given the coefficients (the fit path's codes, or the frozen path's projected c),
+// computed by CTAs of EB_THREADS threads over blocks of `tb`
+// tokens of one KV head (grid: heads written x token blocks). The per-(token, head) form reads the
+// head's [r1, 128] fp32 decoder slice once per token from L2 (56 KB at r1 = 110, ~7 GB per layer
+// of a 16k-token fit, at 1.1% of HBM); a CTA here stages it in shared memory once for its block (re-staged only
+// where the block's tokens change decoder, i.e. cross a request boundary). Per block:
+//
+//   stage     the decoder slice D [r1][128] and, per token, g[r] = cq * cs (given codes and rulers on
+//             the fit path; quantised from the projected c on the frozen path) and the token's checks
+//   residual  R[t][j] = K[t][h*128 + j] - sum_r g_t[r] D[r][j], the same four interleaved partial
+//             sums as a per-token dot product would take, 8 tokens per pass per thread
+//   pack      warp w selects, quantises and packs the K residual rows and the V rows of tokens
+//             w, w + 8, ...; the head-0 CTA writes each token's coefficient block and ruler
+constexpr int EB_THREADS = 256;
+constexpr int EB_WARPS = EB_THREADS / 32;
+
+// Shared memory of encode_block_kernel for r1 and a block of tb tokens.
+inline size_t eb_smem(int r1, int tb) {
+    return size_t(r1) * 128 * 4 + size_t(r1) * tb * 4 + size_t(tb) * 128 * 4 + size_t(tb) * (4 + 4) +
+           size_t(EB_WARPS) * 256 + size_t(tb) * r1 + 64;
+}
+
+__global__ void __launch_bounds__(EB_THREADS) encode_block_kernel(const EncParams P, int tb, int n_tok) {
+    extern __shared__ __align__(16) unsigned char eb_dyn[];
+    const int hs = int(blockIdx.x), h = P.h_lo + hs;
+    const int t0 = int(blockIdx.y) * tb;
+    const int nb = min(tb, n_tok - t0);
     const int tid = threadIdx.x, w = tid >> 5, L = tid & 31;
-    __shared__ float g_s[kMaxRank];          // cq * cs
-    __shared__ int8_t cq_s[kMaxRank];
-    __shared__ float r_s[kHeadDim];
-    __shared__ uint8_t codes_s[2][128];
-    __shared__ float wmax_s[4];
-    __shared__ float cs_s;
+    float* D = reinterpret_cast<float*>(eb_dyn);                       // [r1][128]
+    float* g = D + P.r1 * 128;                                          // [r1][tb]
+    float* R = g + P.r1 * tb;                                           // [tb][128]
+    float* cs_s = R + tb * 128;                                         // [tb]
+    int* ok_s = reinterpret_cast<int*>(cs_s + tb);                      // [tb] token valid
+    uint8_t* codes_s = reinterpret_cast<uint8_t*>(ok_s + tb);          // [warps][2][128]
+    int8_t* cq_s = reinterpret_cast<int8_t*>(codes_s + EB_WARPS * 256); // [tb][r1]
+    __shared__ int run_end;
 
-    const int64_t slot = P.slots[t];
-    if (slot < 0 && P.skip_pad) return;
-    if (slot < 0 || slot >= P.n_slots) {
-        if (tid == 0) report(P.status, TTKV_STATUS_SLOT_RANGE);
-        return;
+    // token checks (every CTA of the token's head group reports the same way)
+    for (int tt = tid; tt < nb; tt += EB_THREADS) {
+        const int t = t0 + tt;
+        const int64_t slot = P.slots[t];
+        int ok = 1;
+        if (slot < 0 && P.skip_pad) ok = 0;
+        else if (slot < 0 || slot >= P.n_slots) { ok = 0; report(P.status, TTKV_STATUS_SLOT_RANGE); }
+        const int di = P.tok_dec ? P.tok_dec[t] : 0;
+        if (ok && P.decoders && (di < 0 || di >= P.n_decoders)) { ok = 0; report(P.status, TTKV_STATUS_DECODER); }
+        ok_s[tt] = ok;
     }
-    const int di = P.tok_dec ? P.tok_dec[t] : 0;
-    if (P.decoders && (di < 0 || di >= P.n_decoders)) {
-        if (tid == 0) report(P.status, TTKV_STATUS_DECODER);
-        return;
-    }
-    uint8_t* row = P.cache + slot * P.row_bytes;
+    __syncthreads();
 
-    // ---- coefficient codes and ruler
-    if (P.c) {
-        // frozen path (vllm_ttkv/encode.py:329-333): cs = amax|c| * fp32(1/127), 0 -> 1;
-        // cq = clamp(rint(c / cs), -128, 127) with a correctly rounded division
-        float a = 0.f;
-        for (int i = tid; i < P.r1; i += 128) a = fmaxf(a, fabsf(P.c[int64_t(t) * P.r1 + i]));
-        a = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(a)));
-        if (L == 0) wmax_s[w] = a;
-        __syncthreads();
+    int staged = -1;                                   // the decoder whose slice D holds
+    for (int a = 0; a < nb;) {
+        // ---- the run of tokens [a, b) that share a decoder
         if (tid == 0) {
-            const float amax = fmaxf(fmaxf(wmax_s[0], wmax_s[1]), fmaxf(wmax_s[2], wmax_s[3]));
-            float cs = __fmul_rn(amax, inv_ruler(8));
-            cs_s = (cs == 0.f) ? 1.f : cs;
+            const int da = P.tok_dec ? P.tok_dec[t0 + a] : 0;
+            int b = a + 1;
+            while (b < nb && (P.tok_dec ? P.tok_dec[t0 + b] : 0) == da) ++b;
+            run_end = b;
         }
         __syncthreads();
-        const float cs = cs_s;
-        for (int i = tid; i < P.r1; i += 128) {
-            const float qf = fminf(fmaxf(rintf(__fdiv_rn(P.c[int64_t(t) * P.r1 + i], cs)), -128.f), 127.f);
-            cq_s[i] = int8_t(qf);
-            g_s[i] = qf * cs;
-        }
-    } else {
-        const float cs = P.coeff_scale[t];
-        if (tid == 0) cs_s = cs;
-        for (int i = tid; i < P.r1; i += 128) {
-            const int8_t q = P.coeff_q[int64_t(t) * P.r1 + i];
-            cq_s[i] = q;
-            g_s[i] = float(q) * cs;
-        }
-    }
-    __syncthreads();
-
-    // ---- residual of this head: R = K - (cq*cs) @ decoder[:, h]   (encode.py:335-336)
-    {
-        const int j = tid;
-        float kd = 0.f;
-        if (P.decoders) {
-            const float* dec = P.decoders + int64_t(di) * P.dec_stride + h * kHeadDim + j;
-            const int64_t stride = int64_t(P.H) * kHeadDim;
-            // four independent partial sums keep four decoder loads in flight
-            float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
-            int rr = 0;
-            for (; rr + 4 <= P.r1; rr += 4) {
-                k0 = fmaf(g_s[rr], dec[rr * stride], k0);
-                k1 = fmaf(g_s[rr + 1], dec[(rr + 1) * stride], k1);
-                k2 = fmaf(g_s[rr + 2], dec[(rr + 2) * stride], k2);
-                k3 = fmaf(g_s[rr + 3], dec[(rr + 3) * stride], k3);
+        const int b = run_end;
+        const int di = P.tok_dec ? P.tok_dec[t0 + a] : 0;
+        const bool dec_ok = di >= 0 && di < P.n_decoders;
+        if (dec_ok && di != staged) {
+            const float4* src = reinterpret_cast<const float4*>(P.decoders + int64_t(di) * P.dec_stride + h * kHeadDim);
+            const int64_t rs4 = int64_t(P.H) * kHeadDim / 4;
+            for (int i = tid; i < P.r1 * 32; i += EB_THREADS) {
+                const int rr = i >> 5, c4 = i & 31;
+                reinterpret_cast<float4*>(D)[i] = src[rr * rs4 + c4];
             }
-            for (; rr < P.r1; ++rr) k0 = fmaf(g_s[rr], dec[rr * stride], k0);
-            kd = (k0 + k1) + (k2 + k3);
+            staged = di;
         }
-        const float kv = load_elt(P.k, P.k_dtype, int64_t(t) * P.k_stride + h * kHeadDim + j);
-        r_s[j] = kv - kd;
-    }
-    __syncthreads();
+        // ---- the run's coefficients: g[r][tt] = cq * cs, and the codes for the coefficient block
+        if (P.c) {
+            // frozen path (vllm_ttkv/encode.py:329-333): a warp per token
+            for (int tt = a + w; tt < b; tt += EB_WARPS) {
+                const float* c = P.c + int64_t(t0 + tt) * P.r1;
+                float amax = 0.f;
+                for (int i = L; i < P.r1; i += 32) amax = fmaxf(amax, fabsf(c[i]));
+                amax = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(amax)));
+                float cs = __fmul_rn(amax, inv_ruler(8));
+                cs = (cs == 0.f) ? 1.f : cs;
+                for (int i = L; i < P.r1; i += 32) {
+                    const float qf = fminf(fmaxf(rintf(__fdiv_rn(c[i], cs)), -128.f), 127.f);
+                    cq_s[tt * P.r1 + i] = int8_t(qf);
+                    g[i * tb + tt] = qf * cs;
+                }
+                if (L == 0) cs_s[tt] = cs;
+            }
+        } else {
+            for (int i = tid; i < (b - a) * P.r1; i += EB_THREADS) {
+                const int tt = a + i / P.r1, rr = i - (tt - a) * P.r1;
+                const int8_t q = P.coeff_q[int64_t(t0 + tt) * P.r1 + rr];
+                const float cs = P.coeff_scale[t0 + tt];
+                cq_s[tt * P.r1 + rr] = q;
+                g[rr * tb + tt] = float(q) * cs;
+                if (rr == 0) cs_s[tt] = cs;
+            }
+        }
+        __syncthreads();
 
-    if (w == 0) {
-        float x[4];
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) x[i] = r_s[4 * L + i];
-        warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + hs * P.k_row, codes_s[0]);
-    } else if (w == 1) {
-        float x[4];
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
-        warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + hs * P.v_row, codes_s[1]);
-    } else if (w == 2 && hs == 0) {
-        // the coefficient block and its fp16 ruler, once per token (encode.py:570-573)
-        for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[i]);
-        if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs_s);
+        // ---- residual rows of the run: thread (j, half) takes tokens a + half*8 + 16 i .. + 7
+        {
+            const int j = tid & 127, half = tid >> 7;
+            for (int base = a + 8 * half; base < b; base += 16) {
+                float k0[8], k1[8], k2[8], k3[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) { k0[u] = 0.f; k1[u] = 0.f; k2[u] = 0.f; k3[u] = 0.f; }
+                if (P.decoders && dec_ok) {
+                    int rr = 0;
+                    for (; rr + 4 <= P.r1; rr += 4) {
+                        const float d0 = D[rr * 128 + j], d1 = D[(rr + 1) * 128 + j];
+                        const float d2 = D[(rr + 2) * 128 + j], d3 = D[(rr + 3) * 128 + j];
+                        #pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int tt = min(base + u, b - 1);
+                            k0[u] = fmaf(g[rr * tb + tt], d0, k0[u]);
+                            k1[u] = fmaf(g[(rr + 1) * tb + tt], d1, k1[u]);
+                            k2[u] = fmaf(g[(rr + 2) * tb + tt], d2, k2[u]);
+                            k3[u] = fmaf(g[(rr + 3) * tb + tt], d3, k3[u]);
+                        }
+                    }
+                    for (; rr < P.r1; ++rr) {
+                        const float d0 = D[rr * 128 + j];
+                        #pragma unroll
+                        for (int u = 0; u < 8; ++u) k0[u] = fmaf(g[rr * tb + min(base + u, b - 1)], d0, k0[u]);
+                    }
+                }
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int tt = base + u;
+                    if (tt < b) {
+                        const float kv = load_elt(P.k, P.k_dtype, int64_t(t0 + tt) * P.k_stride + h * kHeadDim + j);
+                        R[tt * 128 + j] = kv - ((k0[u] + k1[u]) + (k2[u] + k3[u]));
+                    }
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- pack: K residual and V rows, a warp per token; the coefficient block once per token
+        for (int tt = a + w; tt < b; tt += EB_WARPS) {
+            if (!ok_s[tt]) continue;
+            const int t = t0 + tt;
+            uint8_t* row = P.cache + P.slots[t] * P.row_bytes;
+            float x[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = R[tt * 128 + 4 * L + i];
+            warp_select_pack(x, P.res_k, P.res_bits, row + P.coeff_bytes + 2 + hs * P.k_row, codes_s + w * 256);
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = load_elt(P.v, P.v_dtype, int64_t(t) * P.v_stride + h * kHeadDim + 4 * L + i);
+            warp_select_pack(x, P.v_lanes, P.v_bits, row + P.v_offset + hs * P.v_row, codes_s + w * 256 + 128);
+            if (hs == 0) {
+                for (int i = L; i < P.r1; i += 32) row[i] = uint8_t(cq_s[tt * P.r1 + i]);
+                if (L == 0) store_f16_bytes(row + P.coeff_bytes, cs_s[tt]);
+            }
+        }
+        __syncthreads();
+        a = b;
     }
 }
 
@@ -761,8 +826,12 @@ extern "C" int ttkv_write_paged_shard(const ttkv_layout_t* lay, int32_t h_lo, in
     ep.decoders = decoders; ep.dec_stride = dec_stride; ep.n_decoders = n_decoders;
     ep.c = c; ep.coeff_q = frozen ? nullptr : coeff_q; ep.coeff_scale = frozen ? nullptr : coeff_scale;
     ep.status = status;
-    encode_pack_kernel<<<dim3(h_hi - h_lo, n_tok), 128, 0, st>>>(ep);
-    return check_launch("encode_pack_kernel");
+    // blocks of 64 tokens, or 32 where the staged decoder slice leaves too little shared memory
+    const int tb = eb_smem(lay->r1, 64) <= 160 * 1024 ? 64 : 32;
+    const size_t smem = eb_smem(lay->r1, tb);
+    if (int e = raise_smem_limit(reinterpret_cast<const void*>(encode_block_kernel), "encode_block_kernel")) return e;
+    encode_block_kernel<<<dim3(h_hi - h_lo, (n_tok + tb - 1) / tb), EB_THREADS, smem, st>>>(ep, tb, n_tok);
+    return check_launch("encode_block_kernel");
 }
 
 extern "C" int ttkv_write_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
