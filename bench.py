@@ -610,7 +610,7 @@ def run_encode(args):
                                        f"(request-sharded, no exchange), {L} layers, tight r1={r1}",
                            "requests_per_rank": len(reqs), "slot_byte_sum": digest},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                             "peak_kind": peak_kind, "kernel": "encode_pack_kernel (ttkv_write_paged, fit path)",
+                             "peak_kind": peak_kind, "kernel": "encode_block_kernel (ttkv_write_paged, fit path)",
                              "write_ms_per_layer": w_ms, "alg_bytes_per_layer": alg}}
         print(json.dumps(line))
     if world > 1:

@@ -2,11 +2,12 @@
 //
 //   project_kernel       c = M @ pinv for every token of the layer (frozen projection,
 //                        vllm_ttkv/encode.py:301-351), one warp per (token, coefficient)
-//   encode_pack_kernel   one CTA per (token, KV head): the per-token int8 quantisation of c,
-//                        the head's residual R = K - (cq*cs) @ decoder, then the exact top-k lane
-//                        select + quantise + MSB-first pack of the K residual row and the V row,
-//                        written at the token's slot (select_triton.py:157-232); the head-0 CTA
-//                        also writes the coefficient block and its ruler
+//   encode_block_kernel  one CTA per (KV head, block of 64 tokens): the per-token int8
+//                        quantisation of c, the head's residual R = K - (cq*cs) @ decoder with the
+//                        decoder slice staged once per block, then the exact top-k lane select +
+//                        quantise + MSB-first pack of the K residual rows and the V rows, written
+//                        at the tokens' slots (select_triton.py:157-232); the head-0 CTA also
+//                        writes the coefficient blocks and their rulers
 //   select_rows_kernel   the same select/pack for caller-supplied (head, token) rows
 //   fit-tail kernels     everything build_k_layer (codec/ttkv_packed_cache.py:337-375) does after
 //                        the SVDs: coefficient quantisation, core quantisation, the decoder
