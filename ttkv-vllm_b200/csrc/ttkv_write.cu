@@ -44,13 +44,20 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
     #pragma unroll
     for (int i = 0; i < 4; ++i) u[i] = __float_as_uint(fabsf(x[i]));
 
+    // two bits per step (bits 30..1, then bit 0): the three candidates' counts are independent
+    // reductions, and the greedy choice among them equals two one-bit steps (the count of lanes
+    // at or above a threshold does not grow with the threshold)
+    auto count_ge = [&](uint32_t c) {
+        return __reduce_add_sync(FULL, int(u[0] >= c) + int(u[1] >= c) + int(u[2] >= c) + int(u[3] >= c));
+    };
     uint32_t t = 0;
-    for (int b = 30; b >= 0; --b) {
-        const uint32_t cand = t | (1u << b);
-        const int local = int(u[0] >= cand) + int(u[1] >= cand) + int(u[2] >= cand) + int(u[3] >= cand);
-        const int cnt = __reduce_add_sync(FULL, local);
-        if (cnt >= lanes) t = cand;
+    #pragma unroll
+    for (int b = 30; b >= 2; b -= 2) {
+        const uint32_t c3 = t | (3u << (b - 1)), c2 = t | (2u << (b - 1)), c1 = t | (1u << (b - 1));
+        const int n3 = count_ge(c3), n2 = count_ge(c2), n1 = count_ge(c1);
+        t = n3 >= lanes ? c3 : n2 >= lanes ? c2 : n1 >= lanes ? c1 : t;
     }
+    if (count_ge(t | 1u) >= lanes) t |= 1u;
     const int above_local = int(u[0] > t) + int(u[1] > t) + int(u[2] > t) + int(u[3] > t);
     const int n_above = __reduce_add_sync(FULL, above_local);
     const int tie_local = int(u[0] == t) + int(u[1] == t) + int(u[2] == t) + int(u[3] == t);
@@ -208,7 +215,7 @@ struct EncParams {
 //             sums as a per-token dot product would take, 8 tokens per pass per thread
 //   pack      warp w selects, quantises and packs the K residual rows and the V rows of tokens
 //             w, w + 8, ...; the head-0 CTA writes each token's coefficient block and ruler
-constexpr int EB_THREADS = 256;
+constexpr int EB_THREADS = 512;
 constexpr int EB_WARPS = EB_THREADS / 32;
 
 // Shared memory of encode_block_kernel for r1 and a block of tb tokens.
@@ -296,10 +303,10 @@ __global__ void __launch_bounds__(EB_THREADS) encode_block_kernel(const EncParam
         }
         __syncthreads();
 
-        // ---- residual rows of the run: thread (j, half) takes tokens a + half*8 + 16 i .. + 7
+        // ---- residual rows of the run: thread (j, q) takes tokens a + 8 q + 8 * (EB_THREADS / 128) i
         {
-            const int j = tid & 127, half = tid >> 7;
-            for (int base = a + 8 * half; base < b; base += 16) {
+            const int j = tid & 127, q = tid >> 7;
+            for (int base = a + 8 * q; base < b; base += 8 * (EB_THREADS / 128)) {
                 float k0[8], k1[8], k2[8], k3[8];
                 #pragma unroll
                 for (int u = 0; u < 8; ++u) { k0[u] = 0.f; k1[u] = 0.f; k2[u] = 0.f; k3[u] = 0.f; }
