@@ -185,7 +185,13 @@ int ttkv_decode_paged(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
  *     calling thread's current device); make that first call before any stream capture;
  *   - every call on a device shares the one array and it keeps the last call's contents (every
  *     byte a launch reads it has written first, so nothing is cleared); calls that can overlap
- *     on the GPU (two streams, two threads) race on it, so the caller serialises them. */
+ *     on the GPU (two streams, two threads) race on it, so the caller serialises them;
+ *   - the refusal is conservative: the scratch is sized as ttkv_decode_workspace_bytes at the
+ *     cache's block size (the larger of the two decode plans), and the argument checks of
+ *     ttkv_decode_paged come first;
+ *   - the device address of the array is looked up once per device and kept: a device reset
+ *     (cudaDeviceReset, or a primary-context reset) invalidates it, so a process that resets a
+ *     device must not call this entry point on that device afterwards. */
 #define TTKV_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
 int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
                               const ttkv_batch_t* batch, const ttkv_rope_t* rope,

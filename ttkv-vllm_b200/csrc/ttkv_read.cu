@@ -720,12 +720,12 @@ extern "C" size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t
     return need;
 }
 
-static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* cache,
-                      const ttkv_batch_t* batch, const ttkv_rope_t* rope, const int32_t* q_start,
-                      const int32_t* q_len, const void* q, int32_t q_dtype, int64_t q_stride,
-                      int32_t HQ, float scale, int32_t head_lo, int32_t head_hi, void* out,
-                      int32_t out_dtype, int64_t out_stride, int32_t max_q_len, int32_t max_seq_len,
-                      void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+// The host-side refusals every read makes before it looks at its scratch.
+static int check_read_args(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                           const ttkv_batch_t* batch, const ttkv_rope_t* rope, const int32_t* q_start,
+                           const int32_t* q_len, const void* q, int32_t q_dtype, int64_t q_stride,
+                           int32_t HQ, int32_t head_lo, int32_t head_hi, const void* out,
+                           int32_t out_dtype, int64_t out_stride, int32_t max_q_len, int32_t max_seq_len) {
     if (int e = check_common(lay, cache, batch, rope, HQ, head_lo, head_hi)) return e;
     if (!q || !out) return fail(TTKV_ERR_ARG, "q/out null");
     if (q_dtype < TTKV_F32 || q_dtype > TTKV_BF16 || out_dtype < TTKV_F32 || out_dtype > TTKV_BF16)
@@ -737,6 +737,18 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     if (max_seq_len > rope->rows)
         return fail(TTKV_ERR_ARG, "position %d is past the model's cos_sin_cache, which holds %lld rows",
                     max_seq_len - 1, (long long)rope->rows);
+    return TTKV_OK;
+}
+
+static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                      const ttkv_batch_t* batch, const ttkv_rope_t* rope, const int32_t* q_start,
+                      const int32_t* q_len, const void* q, int32_t q_dtype, int64_t q_stride,
+                      int32_t HQ, float scale, int32_t head_lo, int32_t head_hi, void* out,
+                      int32_t out_dtype, int64_t out_stride, int32_t max_q_len, int32_t max_seq_len,
+                      void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+    if (int e = check_read_args(multi, lay, cache, batch, rope, q_start, q_len, q, q_dtype, q_stride, HQ,
+                                head_lo, head_hi, out, out_dtype, out_stride, max_q_len, max_seq_len))
+        return e;
     if (batch->n_reqs == 0 || max_seq_len == 0) return TTKV_OK;
     const int n_heads = head_hi - head_lo;
     // the tensor-core kernel divides token indices by the block size as a 32-bit multiply-high and
@@ -886,7 +898,11 @@ extern "C" int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_ca
                                          int32_t HQ, float scale, int32_t head_lo, int32_t head_hi,
                                          void* out, int32_t out_dtype, int64_t out_stride,
                                          int32_t max_seq_len, int32_t* status, void* stream) {
-    if (int e = check_common(lay, cache, batch, rope, HQ, head_lo, head_hi)) return e;
+    // the same refusals as ttkv_decode_paged, before the scratch is sized (a bad argument is
+    // TTKV_ERR_ARG, never TTKV_ERR_WORKSPACE)
+    if (int e = check_read_args(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ,
+                                head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len))
+        return e;
     const size_t need = decode_workspace(lay, batch->n_reqs, HQ, max_seq_len, head_lo, head_hi, cache->block_size);
     if (need > size_t(TTKV_NOALLOC_SCRATCH_BYTES))
         return fail(TTKV_ERR_WORKSPACE,
