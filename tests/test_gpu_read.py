@@ -159,22 +159,36 @@ def test_decode_over_reference_golden_store():
     assert np.abs(got - s["attend"]).max() < 1e-4
 
 
-def test_continuation_matches_oracle_causal():
+def _queries(rng, shape, qdt):
+    """Standard normal queries, exact in the query dtype (returned as float32)."""
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    return x.to({"float16": torch.float16, "bfloat16": torch.bfloat16}[qdt]).float().numpy()
+
+
+@pytest.mark.parametrize("images,qdt,seqs,q_lens", [
+    (False, "float16", [70, 40, 129], [6, 1, 37]),
+    (True, "float16", [70, 40, 129], [6, 1, 37]),
+    (True, "bfloat16", [70, 40, 129], [6, 1, 37]),
+    (True, "float16", [300, 130, 47], [100, 129, 47])])
+def test_continuation_matches_oracle_causal(images, qdt, seqs, q_lens):
+    """With the decoders' images the chunk runs on the tensor-core continuation (row blocks of
+    42 queries x 3 heads; 100 queries span three blocks, 300 stored rows three tiles, a chunk
+    equal to its request a prompt read); without them on the 8-row blocks of the decode."""
     from vllm_ttkv import ops
-    st = stores.make_store(8, [70, 40, 129], cfg="safe", r1=32)
-    q_lens = [6, 1, 37]
+    st = stores.make_store(8, seqs, cfg="safe", r1=32)
     rng = np.random.default_rng(0)
-    qs = [rng.standard_normal((24, ql, 128)).astype(np.float16).astype(np.float32) for ql in q_lens]
+    qs = [_queries(rng, (24, ql, 128), qdt) for ql in q_lens]
     d = _dev(st)
     flat = np.ascontiguousarray(np.concatenate([q.transpose(1, 0, 2) for q in qs]))   # [N, HQ, d]
-    qt = torch.from_numpy(flat).cuda().to(torch.float16)
+    qt = torch.from_numpy(flat).cuda().to({"float16": torch.float16, "bfloat16": torch.bfloat16}[qdt])
     start = np.concatenate([[0], np.cumsum(q_lens)[:-1]]).astype(np.int32)
     out = torch.zeros(qt.shape, dtype=torch.float32, device="cuda")
     ops.reset_status()
     ops.prefill_cont_paged(d["lay"], d["cache"], st["block_size"], d["bt"], d["seq"], d["dec"],
                            d["idx"], d["table"], torch.from_numpy(start).cuda(),
                            torch.tensor(q_lens, dtype=torch.int32, device="cuda"), qt,
-                           128 ** -0.5, out, max(q_lens), int(st["seq_lens"].max()))
+                           128 ** -0.5, out, max(q_lens), int(st["seq_lens"].max()),
+                           images=ops.decoder_image(d["lay"], d["dec"]) if images else None)
     ops.check_status()
     got = out.cpu().numpy()
     for r, ql in enumerate(q_lens):
@@ -183,14 +197,18 @@ def test_continuation_matches_oracle_causal():
         assert err < 1e-4, (r, err)
 
 
+@pytest.mark.parametrize("images", [False, True])
 @pytest.mark.parametrize("HQ,block_size,r1,cfg,q_lens", [
     (56, 16, 32, "safe", [20, 3]), (24, 1, 32, "safe", [20, 3]), (8, 16, 32, "safe", [20, 3]),
-    (24, 16, 200, "safe", [20, 3]), (24, 16, 48, "campaign4x", [20, 3]), (24, 16, 32, "safe", [0, 11])])
-def test_continuation_other_groups_block_sizes_and_ranks(HQ, block_size, r1, cfg, q_lens):
-    """Blocks of 8 (query, head) rows on the tensor-core decode for G = 7 (a block ends inside a
-    query) and G = 1 (8 queries per block); one token per block sizes the plan beyond the default
-    workspace, so the fp32 kernel serves unless the workspace holds it; r1 = 200 is beyond the
-    tensor-core decode and takes the fp32 kernel; the 4-bit store; a request with no queries."""
+    (24, 16, 200, "safe", [20, 3]), (24, 16, 48, "campaign4x", [20, 3]), (24, 16, 32, "safe", [0, 11]),
+    (24, 16, 126, "safe", [20, 3]), (24, 16, 14, "safe", [20, 3])])
+def test_continuation_other_groups_block_sizes_and_ranks(HQ, block_size, r1, cfg, q_lens, images):
+    """Without images: blocks of 8 (query, head) rows on the tensor-core decode for G = 7 (a block
+    ends inside a query) and G = 1 (8 queries per block); one token per block sizes the plan
+    beyond the default workspace, so the fp32 kernel serves unless the workspace holds it. With
+    images: the tensor-core continuation (18 queries x 7 heads, 128 queries x 1 head per block).
+    r1 = 200 is beyond both and takes the fp32 kernel; r1 = 126 is the continuation's largest
+    rank, r1 = 14 a one-chunk coefficient block; the 4-bit store; a request with no queries."""
     from vllm_ttkv import ops
     st = stores.make_store(17, [90, 50], cfg=cfg, r1=r1, HQ=HQ, block_size=block_size)
     rng = np.random.default_rng(3)
@@ -204,7 +222,8 @@ def test_continuation_other_groups_block_sizes_and_ranks(HQ, block_size, r1, cfg
     ops.prefill_cont_paged(d["lay"], d["cache"], block_size, d["bt"], d["seq"], d["dec"], d["idx"],
                            d["table"], torch.from_numpy(start).cuda(),
                            torch.tensor(q_lens, dtype=torch.int32, device="cuda"), qt, 128 ** -0.5,
-                           out, max(q_lens), int(st["seq_lens"].max()))
+                           out, max(q_lens), int(st["seq_lens"].max()),
+                           images=ops.decoder_image(d["lay"], d["dec"]) if images else None)
     ops.check_status()
     got = out.cpu().numpy()
     for r, ql in enumerate(q_lens):
@@ -315,9 +334,9 @@ def test_decode_of_a_storage_shard_matches_the_full_decode_on_its_heads():
         assert np.abs(out.cpu().numpy() - full[:, lo * G:hi * G]).max() < 1e-5, (lo, hi)
 
 
-def test_continuation_with_decoder_images_gives_the_same_bits():
-    """The tensor-core continuation stages a decoder image instead of converting the fp32 decoder:
-    the same operand, so the same outputs bit for bit."""
+def test_continuation_paths_agree():
+    """The 8-row blocks of the decode (no images) and the tensor-core continuation (images) on the
+    same chunk: both within the kernel bound of the oracle, and within it of each other."""
     from vllm_ttkv import ops
     st = stores.make_store(18, [140, 60], cfg="safe", r1=110)
     q_lens = [33, 4]
@@ -336,8 +355,9 @@ def test_continuation_with_decoder_images_gives_the_same_bits():
                                images=images)
         ops.check_status()
         outs.append(out.cpu().numpy())
-    assert np.array_equal(outs[0], outs[1])
+    assert np.abs(outs[0] - outs[1]).max() < 1e-4
     for r, n in enumerate(q_lens):
         want = stores.expected_continuation(st, r, qs[r])
         s0 = int(start[r])
-        assert np.abs(outs[1][s0:s0 + n].transpose(1, 0, 2) - want).max() < 1e-4
+        for o in outs:
+            assert np.abs(o[s0:s0 + n].transpose(1, 0, 2) - want).max() < 1e-4

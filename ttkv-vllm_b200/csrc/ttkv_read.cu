@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const ReadParams P) {
 }
 
 #include "ttkv_decode_tc.cuh"
+#include "ttkv_cont_tc.cuh"
 
 // ------------------------------------------------------------------ host side
 int qblock_for(int G, bool multi) {
@@ -668,6 +669,38 @@ int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, 
     return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
 }
 
+// Whether cont_tc_kernel serves a continuation call: the tensor-core layouts whose coefficient
+// block fits one 128-byte row (r1 <= 126), a 16-bit query (it is an MMA operand as is, read as
+// 16-byte rows), the decoders' operand images, and 16-byte aligned slot rows and RoPE rows.
+bool ct_serves(const ttkv_layout_t* lay, int HQ, const ttkv_batch_t* batch, const ttkv_cache_t* cache,
+               const ttkv_rope_t* rope, const void* q, int32_t q_dtype, int64_t q_stride) {
+    return tc_serves(lay, HQ) && ct::ct_geom(lay, HQ / lay->H).smem > 0 && batch->dec_image &&
+           batch->dec_scales && batch->n_reqs <= 65535 && (q_dtype == TTKV_F16 || q_dtype == TTKV_BF16) &&
+           (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (q_stride & 7) == 0 && rope->dtype != TTKV_F32 &&
+           (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0;
+}
+
+int launch_ct(const ReadParams& P, const ct::CtGeom& T, int max_q_len, int n_reqs, cudaStream_t st) {
+    auto k = ct::cont_tc_kernel;
+    if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "cont_tc_kernel")) return e;
+    // may start while the step's write runs (programmatic dependent launch): the kernel waits for
+    // it before its first read
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((max_q_len + T.nq - 1) / T.nq, P.n_heads, n_reqs);
+    cfg.blockDim = dim3(ct::NTHR);
+    cfg.dynamicSmemBytes = T.smem;
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k, P, T);
+    if (e != cudaSuccess) return fail(TTKV_ERR_CUDA, "cont_tc_kernel: %s", cudaGetErrorString(e));
+    return TTKV_OK;
+}
+
 template <bool MULTI>
 int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     switch (P.G) {
@@ -764,9 +797,19 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
         T = tc::tc_geom(lay, HQ / lay->H);
         use_tc = tc_maps(&maps, T, P);
     }
-    // continuation chunks: blocks of 8 (query, head) rows on the tensor-core decode when it
-    // serves the layout at 8 rows and the workspace holds its plan (else the fp32 kernel below)
     const int Gq = HQ / lay->H;
+    // continuation chunks: blocks of up to 128 (query, head) rows with every product on the tensor
+    // cores, when cont_tc_kernel serves the call (no scratch)
+    if (multi && ct_serves(lay, HQ, batch, cache, rope, q, q_dtype, q_stride)) {
+        P.q = q; P.q_dtype = q_dtype; P.q_stride = q_stride; P.HQ = HQ; P.G = Gq;
+        P.q_start = q_start; P.q_len = q_len;
+        P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
+        P.n_reqs = batch->n_reqs; P.max_seq = max_seq_len;
+        P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
+        return launch_ct(P, ct::ct_geom(lay, Gq), max_q_len, batch->n_reqs, reinterpret_cast<cudaStream_t>(stream));
+    }
+    // else blocks of 8 (query, head) rows on the tensor-core decode when it serves the layout at 8
+    // rows and the workspace holds its plan (else the fp32 kernel below)
     if (multi && tc_serves(lay, lay->H * kContRows) && rope->dtype != TTKV_F32 &&
         (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0 &&
