@@ -152,11 +152,12 @@ def test_write_given_coefficients_is_bit_exact():
     assert (got == want).mean() > 0.995
 
 
-@pytest.mark.parametrize("r1", [32, 143, 208])
-def test_frozen_write_matches_oracle_end_to_end(r1):
-    """r1 <= 200: the fused cluster write; 208: its two slices exceed shared memory, so the
-    two-launch write (projection, then encode + pack) runs."""
-    st, g, K, V, tok_dec = _frozen_case(seed=1, n_tok=9, r1=r1)
+@pytest.mark.parametrize("r1,n_tok", [(32, 9), (143, 9), (208, 9), (32, 200), (110, 200)])
+def test_frozen_write_matches_oracle_end_to_end(r1, n_tok):
+    """Up to 96 tokens with r1 <= 200: the fused cluster write; 208: its two slices exceed shared
+    memory, and 200 tokens (a prefill chunk) are past its token limit, so the two-launch write
+    (projection, then encode + pack) runs."""
+    st, g, K, V, tok_dec = _frozen_case(seed=1, n_tok=n_tok, r1=r1)
     got = _write_gpu(g, K, V, tok_dec, st["decoders"], pinvT=st["pinvT"])
     want = []
     for t in range(K.shape[1]):

@@ -14,20 +14,20 @@
 //           -> V [tokens x lanes]; the V ruler -> vr[token]
 //   S       S[rows x tokens] = Q . Y_hi^T + Q . Y_lo^T   (Q exact in its dtype: q is the model's)
 //   softmax scale, causal limit (stored row <= the query's position), online max and sum;
-//           P' = p * vr split into fp16 hi + lo; O rescaled in TMEM when a row's max moved
-//   PV      O[rows x lanes] += P'_hi . V + P'_lo . V
+//           P' = p * vr split into fp16 hi + lo, written over S in tensor memory; O rescaled in
+//           tensor memory when a row's max moved
+//   PV      O[rows x lanes] += P'_hi . V + P'_lo . V   (A from tensor memory)
 //
 // and finally writes O / l for its rows. The decoder slice and Y share one buffer (the slice is
-// re-staged, from L2, once S has read Y), Q and P' another (Q is re-read once PV has read P'), so
-// the plan fits with hi/lo on every inexact operand. No scratch and no merge: each CTA owns its
-// rows.
+// re-staged, from L2, once S has read Y), so the plan fits with hi/lo on every inexact operand.
+// No scratch and no merge: each CTA owns its rows.
 //
-// Threads: four epilogue warpgroups and one control warp. Epilogue thread (wg, t) owns TMEM lane
-// t (a token for the keys, a row for the softmax) and a quarter of its columns, as the decode
-// splits them: RoPE pairs [16wg, 16wg + 16), V lanes [32wg, 32wg + 32), stored rows
-// [32wg, 32wg + 32) of the tile, output lanes [32wg, 32wg + 32). The control warp stages the slot
-// fields with cp.async (all lanes) and issues the MMAs and the decoder copies (lane 0). Every
-// mbarrier wait is bounded (TTKV_STATUS_TIMEOUT).
+// Threads: four epilogue warpgroups, an MMA warp and a producer warp. Epilogue thread (wg, t)
+// owns TMEM lane t (a token for the keys, a row for the softmax) and a quarter of its columns, as
+// the decode splits them: RoPE pairs [16wg, 16wg + 16), V lanes [32wg, 32wg + 32), stored rows
+// [32wg, 32wg + 32) of the tile, output lanes [32wg, 32wg + 32). The producer warp stages each
+// tile's slot fields with cp.async; lane 0 of the MMA warp issues the MMAs and the decoder copies.
+// Every mbarrier wait is bounded (TTKV_STATUS_TIMEOUT).
 //
 // This is vllm_ttkv/impl.py:725-778 (_prefill_continuation) with krt_multi_from_slots
 // (krt_triton.py:269-317), the causal softmax and v_out_multi_from_slots (v_out_triton.py:249-294).
@@ -38,16 +38,21 @@ using namespace tc;
 
 constexpr int NWGE = 4;                       // epilogue warpgroups
 constexpr int NEPI = 128 * NWGE;
-constexpr int NTHR = NEPI + 32;
+constexpr int NTHR = NEPI + 64;             // + the MMA warp and the producer warp
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t ACC_COL = 0, S_COL = 128, O_COL = 256;
+// tensor memory: the reconstruction, S (then P'_hi in its first 64 columns and P'_lo in the
+// next 64, two 16-bit values per column), O
+constexpr uint32_t ACC_COL = 0, S_COL = 128, PH_COL = 128, PL_COL = 192, O_COL = 256;
+constexpr int RAW_PITCH = 144;                // raw coefficient rows: 128 B + 16 (conflict-free reads)
+constexpr int CT_BT_CAP = TM + 1;             // block ids of one tile (block size 1: 128, plus one)
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct CtGeom {
     int natom, kp16, cb;
     int kr, vr, kvrow;
     int nq;                           // queries per row block
-    int off_by, off_qp, off_a, off_v, off_kv, off_vr, off_red, off_lut, off_misc;
+    int bs_shift;                     // log2(block size) when it is a power of two, else -1
+    int off_by, off_q, off_a, off_raw, off_v, off_kv, off_vr, off_red, off_bt, off_lut, off_misc;
     int smem;
 };
 
@@ -61,6 +66,15 @@ struct CtMisc {
 // Instruction descriptor of a kind::f16 MMA with fp16 or bf16 operands and an fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_16(int M, int N, bool a_mn, bool b_mn, bool bf16) {
     return idesc_f16(M, N, a_mn, b_mn) | (bf16 ? ((1u << 7) | (1u << 10)) : 0u);
+}
+
+// D (+)= A . B with A read from tensor memory (lane = row, two 16-bit K values per column).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
+        :: "r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void ct_arrive(uint64_t* bar) {
@@ -113,6 +127,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+           "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+           "r"(v[15])
+        : "memory");
+}
+
 // Two 16-bit values (fp16 or bf16) of x, y, round to nearest even: the hi word and the remainder's.
 __device__ __forceinline__ void split16(float x, float y, bool bf16, uint32_t& hi, uint32_t& lo) {
     if (bf16) {
@@ -135,12 +160,14 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
     extern __shared__ __align__(1024) unsigned char smem_dyn[];
     unsigned char* base = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
     unsigned char* by = base + T.off_by;        // decoder slice hi || lo, then Y hi || lo
-    unsigned char* qp = base + T.off_qp;        // Q, then P' hi || lo
-    unsigned char* amat = base + T.off_a;       // coefficients as fp16 (raw codes staged in its last atom)
+    unsigned char* qb = base + T.off_q;         // Q [rows x dims], K-major
+    unsigned char* amat = base + T.off_a;       // coefficients as fp16, K-major
+    unsigned char* raw = base + T.off_raw;      // raw coefficient blocks [token][RAW_PITCH]
     unsigned char* vb = base + T.off_v;         // V [tokens x lanes], MN-major
     unsigned char* kvb = base + T.off_kv;       // [token][K region | V region]
     float* vr_s = reinterpret_cast<float*>(base + T.off_vr);      // [tile parity][token]
     float* red = reinterpret_cast<float*>(base + T.off_red);      // [warpgroup][row]
+    int32_t* bts = reinterpret_cast<int32_t*>(base + T.off_bt);   // the staged tile's block ids
     uint4* lutk = reinterpret_cast<uint4*>(base + T.off_lut);
     uint4* lutv = lutk + 16;
     CtMisc* M = reinterpret_cast<CtMisc*>(base + T.off_misc);
@@ -212,45 +239,16 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
     const int kfield = P.coeff_bytes + 2 + h * P.k_row;
     const int vfield = P.v_offset + h * P.v_row;
     const int koff = kfield & 15, voff = vfield & 15;
-    const int cch = T.cb >> 4;
-    const int kch = (koff + P.k_row + 15) >> 4, vch = (voff + P.v_row + 15) >> 4;
-    const int raw_atom = T.natom - 1;                         // raw coefficients staged in A's last atom
-
-    // slot row of stored token `tok` (a block id outside the cache is reported; block 0 is read)
-    auto row_at = [&](int tok) -> const uint8_t* {
-        int32_t blk = brow[tok / P.block_size];
-        if (blk < 0 || blk >= n_blocks) { M->bad = 1; blk = 0; }
-        return P.cache + (int64_t(blk) * P.block_size + tok % P.block_size) * P.row_bytes;
-    };
-    // control lanes: lane l stages tokens l, l + 32, ... of tile `it`
-    auto issue_cf = [&](int it) {
-        const int t0 = it * TM, n = min(TM, limit - t0);
-        for (int u = lane; u < n; u += 32) {
-            const uint8_t* src = row_at(t0 + u);
-            unsigned char* dst = amat + raw_atom * ATOM_BYTES;
-            for (int c = 0; c < cch; ++c) cp_async16(dst + kmajor_off(u, c), src + 16 * c);
-        }
-        cp_async_arrive(&M->mb_cf);
-    };
-    auto issue_kv = [&](int it) {
-        const int t0 = it * TM, n = min(TM, limit - t0);
-        for (int u = lane; u < n; u += 32) {
-            const uint8_t* src = row_at(t0 + u);
-            unsigned char* dst = kvb + u * T.kvrow;
-            for (int c = 0; c < kch; ++c) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
-            for (int c = 0; c < vch; ++c) cp_async16(dst + T.kr + 16 * c, src + (vfield - voff) + 16 * c);
-        }
-        cp_async_arrive(&M->mb_kv);
-    };
+    const uint32_t kbytes = uint32_t((koff + P.k_row + 15) & ~15), vbytes = uint32_t((voff + P.v_row + 15) & ~15);
 
     const uint32_t img_bytes = uint32_t(2 * T.natom * ATOM_BYTES);
     const unsigned char* img = P.dec_image + int64_t(di) * P.image_stride + int64_t(h) * img_bytes;
     const float s_up = P.dec_scales[int64_t(di) * P.H + h];
     bool timed_out = false;
 
-    if (!epi) {
-        // ============================================================== control warp
-        uint32_t ph_a = 0, ph_y = 0, ph_kvf = 0, ph_p = 0, ph_b = 0, ph_r = 0, ph_s = 0;
+    if (w == NEPI / 32) {
+        // ============================================================== MMA warp
+        uint32_t ph_a = 0, ph_y = 0, ph_p = 0, ph_b = 0, ph_s = 0, ph_pv = 0;
         uint32_t n_r = 0, n_s = 0, n_pv = 0, n_b = 0;
         bool tmo = false;
         auto cwait = [&](uint64_t* bar, uint32_t& ph) {
@@ -260,9 +258,8 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
         const uint64_t dA = sw128_desc(smem_u32(amat), 16, 1024);
         const uint64_t dBh = sw128_desc(smem_u32(by), 16, 1024);
         const uint64_t dBl = sw128_desc(smem_u32(by + T.natom * ATOM_BYTES), 16, 1024);
-        const uint64_t dQ = sw128_desc(smem_u32(qp), 16, 1024);
+        const uint64_t dQ = sw128_desc(smem_u32(qb), 16, 1024);
         const uint64_t dYh = sw128_desc(smem_u32(by), 16, 1024), dYl = sw128_desc(smem_u32(by + 2 * ATOM_BYTES), 16, 1024);
-        const uint64_t dPh = dQ, dPl = sw128_desc(smem_u32(qp + 2 * ATOM_BYTES), 16, 1024);
         const uint64_t dV = sw128_desc(smem_u32(vb), 1024, 2048);
         auto k16 = [](int ks) { return uint64_t(((ks >> 2) * ATOM_BYTES + (ks & 3) * 32) >> 4); };
         if (lane == 0) {
@@ -270,8 +267,6 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
             bulk_g2s(by, img, img_bytes, &M->mb_b);
             ++n_b;
         }
-        issue_cf(0);
-        issue_kv(0);
         for (int it = 0; it < n_tiles && !tmo; ++it) {
             // MMA 1 once A(it) is converted and the decoder slice is back
             cwait(&M->mb_a, ph_a);
@@ -289,13 +284,9 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 ++n_r;
             }
             __syncwarp();
-            // A is free once MMA 1 has read it: the next tile's coefficients
-            cwait(&M->mb_r, ph_r);
-            tmo = __any_sync(0xffffffffu, tmo);
-            if (tmo) break;
-            if (it + 1 < n_tiles) issue_cf(it + 1);
-            // S once Y, V and Q are written (the epilogue's Q of this tile)
+            // S once Y is written, and PV (it - 1) has read P'(it - 1) from S's columns
             cwait(&M->mb_y, ph_y);
+            if (it > 0) cwait(&M->mb_pv, ph_pv);
             tmo = __any_sync(0xffffffffu, tmo);
             if (tmo) break;
             if (lane == 0) {
@@ -309,11 +300,6 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 ++n_s;
             }
             __syncwarp();
-            // the K/V rows are consumed (the keys and V are built): the next tile's
-            cwait(&M->mb_kvf, ph_kvf);
-            tmo = __any_sync(0xffffffffu, tmo);
-            if (tmo) break;
-            if (it + 1 < n_tiles) issue_kv(it + 1);
             // Y is read once S completes: the decoder slice back into the shared buffer
             cwait(&M->mb_s, ph_s);
             tmo = __any_sync(0xffffffffu, tmo);
@@ -325,7 +311,7 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 ++n_b;
             }
             __syncwarp();
-            // PV once P' is written and O rescaled
+            // PV once P' is in tensor memory and O rescaled
             cwait(&M->mb_p, ph_p);
             tmo = __any_sync(0xffffffffu, tmo);
             if (tmo) break;
@@ -334,24 +320,93 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 constexpr uint32_t ID_PV = idesc_16(128, 128, false, true, false);
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t dv = dV + uint64_t((ks * 4096) >> 4);
-                    mma_f16(taddr + O_COL, dPh + k16(ks), dv, ID_PV, (it > 0 || ks > 0) ? 1u : 0u);
-                    mma_f16(taddr + O_COL, dPl + k16(ks), dv, ID_PV, 1u);
+                    mma_f16_ts(taddr + O_COL, taddr + PH_COL + 8 * ks, dv, ID_PV, (it > 0 || ks > 0) ? 1u : 0u);
+                    mma_f16_ts(taddr + O_COL, taddr + PL_COL + 8 * ks, dv, ID_PV, 1u);
                 }
                 mma_commit(&M->mb_pv);
                 ++n_pv;
             }
             __syncwarp();
         }
-        if (tmo) {
-            // drain what was started (at most one batch of each kind is in flight)
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            if (lane == 0) {
-                if (n_r) mbar_wait(&M->mb_r, (n_r - 1) & 1u);
-                if (n_s) mbar_wait(&M->mb_s, (n_s - 1) & 1u);
-                if (n_pv) mbar_wait(&M->mb_pv, (n_pv - 1) & 1u);
-                if (n_b) mbar_wait(&M->mb_b, (n_b - 1) & 1u);
-            }
+        if (tmo && lane == 0) {
+            // drain what was started: the last batch of each kind (every earlier one was waited for)
+            if (n_r) mbar_wait(&M->mb_r, (n_r - 1) & 1u);
+            if (n_s) mbar_wait(&M->mb_s, (n_s - 1) & 1u);
+            if (n_pv) mbar_wait(&M->mb_pv, (n_pv - 1) & 1u);
+            if (n_b) mbar_wait(&M->mb_b, (n_b - 1) & 1u);
         }
+        timed_out = tmo;
+    } else if (!epi) {
+        // ============================================================== producer warp
+        // ---- staging (producer warp). A tile's block ids are cached in shared memory first (each
+        // checked against the cache; an id outside it is reported and block 0 read instead), then the
+        // 16-byte chunks are copied chunk-fastest over the tile's tokens, so a warp's copies cover a
+        // few consecutive slot fields rather than 32 scattered rows. Every lane arrives once per phase
+        // after its own copies.
+        const int bsz = P.block_size;
+        auto blk_of = [&](int tok) { return T.bs_shift >= 0 ? tok >> T.bs_shift : tok / bsz; };
+        auto load_bt = [&](int it) {
+            const int t0 = it * TM, n = min(TM, limit - t0);
+            const int b0 = blk_of(t0), nb = blk_of(t0 + n - 1) - b0 + 1;         // <= CT_BT_CAP
+            for (int i = lane; i < nb; i += 32) {
+                int32_t blk = brow[b0 + i];
+                if (blk < 0 || blk >= n_blocks) { M->bad = 1; blk = 0; }
+                bts[i] = blk;
+            }
+            __syncwarp();
+        };
+        auto slot_row = [&](int tok, int b0) -> const uint8_t* {
+            const int bi = blk_of(tok);
+            return P.cache + (int64_t(bts[bi - b0]) * bsz + (tok - bi * bsz)) * P.row_bytes;
+        };
+        const int cch = T.cb >> 4, nkvc = int(kbytes + vbytes) >> 4, kch = int(kbytes) >> 4;
+        const uint32_t mul_cf = uint32_t((0x100000000ull + cch - 1) / cch);
+        const uint32_t mul_kv = uint32_t((0x100000000ull + nkvc - 1) / nkvc);
+        // i / d as a multiply-high (i < 2^12, so the rounding of the multiplier never reaches a
+        // quotient boundary); d = 1 has no 32-bit multiplier
+        auto div_small = [](uint32_t i, uint32_t mul, int d) { return d == 1 ? i : __umulhi(i, mul); };
+        auto issue_cf = [&](int it) {                // the tile's block ids are in bts
+            const int t0 = it * TM, n = min(TM, limit - t0), b0 = blk_of(t0);
+            for (int i = lane; i < n * cch; i += 32) {
+                const uint32_t u = div_small(uint32_t(i), mul_cf, cch), c = uint32_t(i) - u * uint32_t(cch);
+                cp_async16(raw + u * RAW_PITCH + 16 * c, slot_row(t0 + int(u), b0) + 16 * c);
+            }
+            cp_async_arrive(&M->mb_cf);
+        };
+        auto issue_kv = [&](int it) {                // the tile's block ids are in bts
+            const int t0 = it * TM, n = min(TM, limit - t0), b0 = blk_of(t0);
+            for (int i = lane; i < n * nkvc; i += 32) {
+                const uint32_t u = div_small(uint32_t(i), mul_kv, nkvc), c = uint32_t(i) - u * uint32_t(nkvc);
+                const uint8_t* src = slot_row(t0 + int(u), b0);
+                unsigned char* dst = kvb + u * T.kvrow;
+                if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
+                else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
+            }
+            cp_async_arrive(&M->mb_kv);
+        };
+        uint32_t ph_a = 0, ph_kvf = 0;
+        bool tmo = false;
+        auto pwait = [&](uint64_t* bar, uint32_t& ph) {
+            if (tmo) return;
+            if (!mbar_wait(bar, ph)) tmo = true; else ph ^= 1u;
+        };
+        load_bt(0);
+        issue_cf(0);
+        issue_kv(0);
+        for (int it = 0; it + 1 < n_tiles && !tmo; ++it) {
+            // the raw blocks of tile it are converted (A(it) arrived): the next tile's
+            pwait(&M->mb_a, ph_a);
+            tmo = __any_sync(0xffffffffu, tmo);
+            if (tmo) break;
+            load_bt(it + 1);                          // kv(it) was issued from the slice before
+            issue_cf(it + 1);
+            // the K/V rows of tile it are consumed (the keys and V are built): the next tile's
+            pwait(&M->mb_kvf, ph_kvf);
+            tmo = __any_sync(0xffffffffu, tmo);
+            if (tmo) break;
+            issue_kv(it + 1);
+        }
+        if (tmo) asm volatile("cp.async.wait_all;" ::: "memory");   // this warp's copies land first
         timed_out = tmo;
     } else {
         // ============================================================== epilogue
@@ -378,28 +433,34 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
         const int row_lim = row_ok ? p0 + j0 + jq + 1 : 0;       // sees stored rows < row_lim
         float m_run = -INFINITY, l_run = 0.f;
 
-        // A(it): token t's coefficients (staged raw in the last atom's row t) as exact fp16; this
-        // warpgroup converts 16-coefficient chunks wg and wg + 4. Every raw chunk is read before
-        // any converted one is written (they share the atom). Returns the coefficient scale x 2^e.
-        auto convert_a = [&](bool valid) {
-            const unsigned char* raw = amat + raw_atom * ATOM_BYTES;
-            const int nc16 = T.kp16 / 16;
-            uint4 rw[2];
+        // Q row t (query jq, head g), dims [32wg, 32wg + 32), into its operand once for all tiles
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                static_cast<const uint16_t*>(P.q) + int64_t(qrow0 + (row_ok ? jq : 0)) * P.q_stride +
+                int64_t(h * G + (row_ok ? g : 0)) * 128) + 4 * wg;
+            uint4 qv[4];
             #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int c16 = wg + NWGE * i;
-                rw[i] = (valid && c16 < nc16) ? *reinterpret_cast<const uint4*>(raw + kmajor_off(t, c16))
-                                              : make_uint4(0, 0, 0, 0);
+            for (int c = 0; c < 4; ++c) qv[c] = row_ok ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int ch = 4 * wg + c;
+                *reinterpret_cast<uint4*>(qb + (ch >> 3) * ATOM_BYTES + kmajor_off(t, ch & 7)) = qv[c];
             }
+        }
+
+        // A: token t's coefficients (its raw block) as exact fp16; this warpgroup converts the
+        // 16-coefficient chunks wg and wg + 4. Returns the coefficient scale x 2^e.
+        auto convert_a = [&](bool valid) {
+            const unsigned char* rrow = raw + t * RAW_PITCH;
+            const int nc16 = T.kp16 / 16;
             const int sb = P.coeff_bytes;
-            auto raw_byte = [&](int b) { return uint32_t(raw[kmajor_off(t, b >> 4) + (b & 15)]); };
-            const float cs = valid ? f16_bits_to_f32(raw_byte(sb) | (raw_byte(sb + 1) << 8)) : 0.f;
-            epi_sync();
+            const float cs = valid ? f16_bits_to_f32(uint32_t(rrow[sb]) | (uint32_t(rrow[sb + 1]) << 8)) : 0.f;
             #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int c16 = wg + NWGE * i;
                 if (c16 >= nc16) break;
-                uint32_t wds[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
+                const uint4 rw = valid ? *reinterpret_cast<const uint4*>(rrow + 16 * c16) : make_uint4(0, 0, 0, 0);
+                uint32_t wds[4] = {rw.x, rw.y, rw.z, rw.w};
                 const int left = P.r1 - 16 * c16;
                 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -475,7 +536,7 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 }
                 krs = valid ? f16_at(kvrow + koff + 16 + P.k_pb) : 0.f;
             }
-            // ---- V and Q of this tile need PV (it - 1) done (it read V and P', which shares Q's buffer)
+            // ---- V of this tile needs PV (it - 1) done (it read V); so does the O rescale below
             if (it > 0) ewait(&M->mb_pv, ph_pv);
             tc_after();
             {
@@ -509,20 +570,6 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                     *reinterpret_cast<uint4*>(vb + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
                 if (wg == 0) vr_s[(it & 1) * TM + t] = valid ? f16_at(vrow + voff + 16 + P.v_pb) : 0.f;
-            }
-            {
-                // Q row t (query jq, head g), dims [32wg, 32wg + 32), copied as is into its operand
-                uint4 qv[4];
-                const uint4* src = reinterpret_cast<const uint4*>(
-                    static_cast<const uint16_t*>(P.q) + int64_t(qrow0 + (row_ok ? jq : 0)) * P.q_stride +
-                    int64_t(h * G + (row_ok ? g : 0)) * 128) + 4 * wg;
-                #pragma unroll
-                for (int c = 0; c < 4; ++c) qv[c] = row_ok ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-                #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int ch = 4 * wg + c;
-                    *reinterpret_cast<uint4*>(qp + (ch >> 3) * ATOM_BYTES + kmajor_off(t, ch & 7)) = qv[c];
-                }
             }
             ct_arrive(&M->mb_kvf);                               // the K/V rows are read
 
@@ -580,7 +627,7 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
             }
             fence_async_smem();
             tc_before();
-            ct_arrive(&M->mb_y);                                  // Y, V, Q written; the accumulator read
+            ct_arrive(&M->mb_y);                                  // Y and V written; the accumulator read
 
             // ---- the next tile's coefficients into A (MMA 1 (it) has read it)
             if (it + 1 < n_tiles) {
@@ -604,22 +651,30 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                 tmem_ld32(t_row + S_COL + uint32_t(32 * wg), sv);
                 tmem_wait_ld();
                 float mt = -INFINITY;
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool ok = (t0 + 32 * wg + i) < row_lim;
-                    sv[i] = ok ? sv[i] * sl2 : -INFINITY;
-                    mt = fmaxf(mt, sv[i]);
+                const int c0 = t0 + 32 * wg;                      // the stored row of sv[0]
+                if (__all_sync(0xffffffffu, c0 + 32 <= row_lim)) {      // no row of the warp is cut here
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) { sv[i] *= sl2; mt = fmaxf(mt, sv[i]); }
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        sv[i] = c0 + i < row_lim ? sv[i] * sl2 : -INFINITY;
+                        mt = fmaxf(mt, sv[i]);
+                    }
                 }
                 red[wg * TM + t] = mt;
-                epi_sync();
+                epi_sync();                                        // every S column is read too
                 const float tmax = fmaxf(fmaxf(red[t], red[TM + t]), fmaxf(red[2 * TM + t], red[3 * TM + t]));
                 const float m_new = fmaxf(m_run, tmax);
                 // nothing seen yet: O and l are zero, nothing to rescale
                 const float corr = (m_run == -INFINITY) ? 1.f : ex2(m_run - m_new);
                 float lsum = 0.f;
+                uint32_t phi[16], plo[16];
                 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint32_t ph4[4], pl4[4];
+                    const float4 va = reinterpret_cast<const float4*>(vrt)[2 * c];
+                    const float4 vb4 = reinterpret_cast<const float4*>(vrt)[2 * c + 1];
+                    const float vrc[8] = {va.x, va.y, va.z, va.w, vb4.x, vb4.y, vb4.z, vb4.w};
                     #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         float pp[2];
@@ -628,19 +683,18 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                             const int tt = 8 * c + 2 * i + k;
                             const float pg = sv[tt] == -INFINITY ? 0.f : ex2(sv[tt] - m_new);
                             lsum += pg;
-                            pp[k] = pg * vrt[tt];
+                            pp[k] = pg * vrc[2 * i + k];
                         }
                         const __half2 hh = __floats2half2_rn(pp[0], pp[1]);
                         const float2 hf = __half22float2(hh);
                         const __half2 ll = __floats2half2_rn(pp[0] - hf.x, pp[1] - hf.y);
-                        ph4[i] = *reinterpret_cast<const uint32_t*>(&hh);
-                        pl4[i] = *reinterpret_cast<const uint32_t*>(&ll);
+                        phi[4 * c + i] = *reinterpret_cast<const uint32_t*>(&hh);
+                        plo[4 * c + i] = *reinterpret_cast<const uint32_t*>(&ll);
                     }
-                    const int ch = 4 * wg + c;
-                    const uint32_t off = uint32_t((ch >> 3) * ATOM_BYTES) + kmajor_off(t, ch & 7);
-                    *reinterpret_cast<uint4*>(qp + off) = make_uint4(ph4[0], ph4[1], ph4[2], ph4[3]);
-                    *reinterpret_cast<uint4*>(qp + 2 * ATOM_BYTES + off) = make_uint4(pl4[0], pl4[1], pl4[2], pl4[3]);
                 }
+                // P' over S: stored rows 32wg.. are columns 16wg.. of each half
+                tmem_st16u(t_row + PH_COL + uint32_t(16 * wg), phi);
+                tmem_st16u(t_row + PL_COL + uint32_t(16 * wg), plo);
                 l_run = l_run * corr + lsum;                       // this warpgroup's share of the sum
                 // O lanes [32wg, 32wg + 32) (after PV (it - 1), waited above) rescaled where a max moved
                 if (it > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
@@ -650,11 +704,10 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
                     #pragma unroll
                     for (int i = 0; i < 32; ++i) o32[i] *= corr;
                     tmem_st32(t_row + O_COL + uint32_t(32 * wg), o32);
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 m_run = m_new;
             }
-            fence_async_smem();
             tc_before();
             ct_arrive(&M->mb_p);
             // no early exit after a timeout: every epilogue warp runs every tile's named barriers
@@ -694,12 +747,15 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
 // ------------------------------------------------------------------ host plan
 // The shared-memory plan of cont_tc_kernel, or smem == 0 where it does not fit (layouts with
 // more than two 64-rank atoms, or a coefficient block of more than 128 bytes, use the decode path).
-inline CtGeom ct_geom(const ttkv_layout_t* lay, int G) {
+inline CtGeom ct_geom(const ttkv_layout_t* lay, int G, int block_size) {
     CtGeom T{};
     T.kp16 = round_up(lay->r1, 16);
     T.natom = (T.kp16 + 63) / 64;
     T.cb = round_up(lay->coeff_bytes + 2, 16);
     T.nq = 128 / G;
+    T.bs_shift = -1;
+    for (int s = 0; s < 31; ++s)
+        if (block_size == (1 << s)) T.bs_shift = s;
     int kr = 0, vr = 0;
     for (int hh = 0; hh < lay->H; ++hh) {
         const int kf = lay->coeff_bytes + 2 + hh * lay->k_row_bytes;
@@ -714,13 +770,15 @@ inline CtGeom ct_geom(const ttkv_layout_t* lay, int G) {
     if (T.natom > 2 || T.cb > 128) { T.smem = 0; return T; }
     int off = 0;
     T.off_by = off; off += std::max(2 * T.natom * ATOM_BYTES, 4 * ATOM_BYTES);
-    T.off_qp = off; off += 4 * ATOM_BYTES;
+    T.off_q = off; off += 2 * ATOM_BYTES;
     T.off_a = off; off += T.natom * ATOM_BYTES;
     T.off_v = off; off += APV_BYTES;
+    T.off_raw = off; off += TM * RAW_PITCH;
     T.off_kv = off; off += TM * T.kvrow + KV_PAD;
     off = round_up(off, 16);
     T.off_vr = off; off += 2 * TM * 4;
     T.off_red = off; off += NWGE * TM * 4;
+    T.off_bt = off; off += round_up(CT_BT_CAP * 4, 16);
     T.off_lut = off; off += LUT_BYTES;
     T.off_misc = off; off += round_up(int(sizeof(CtMisc)), 16);
     T.smem = round_up(off, 16) + 1024;

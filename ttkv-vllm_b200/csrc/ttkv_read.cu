@@ -674,8 +674,9 @@ int launch_tc(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, 
 // 16-byte rows), the decoders' operand images, and 16-byte aligned slot rows and RoPE rows.
 bool ct_serves(const ttkv_layout_t* lay, int HQ, const ttkv_batch_t* batch, const ttkv_cache_t* cache,
                const ttkv_rope_t* rope, const void* q, int32_t q_dtype, int64_t q_stride) {
-    return tc_serves(lay, HQ) && ct::ct_geom(lay, HQ / lay->H).smem > 0 && batch->dec_image &&
-           batch->dec_scales && batch->n_reqs <= 65535 && (q_dtype == TTKV_F16 || q_dtype == TTKV_BF16) &&
+    return tc_serves(lay, HQ) && ct::ct_geom(lay, HQ / lay->H, cache->block_size).smem > 0 &&
+           batch->dec_image && batch->dec_scales && batch->n_reqs <= 65535 &&
+           (q_dtype == TTKV_F16 || q_dtype == TTKV_BF16) &&
            (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (q_stride & 7) == 0 && rope->dtype != TTKV_F32 &&
            (reinterpret_cast<uintptr_t>(rope->table) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(cache->base) & 15) == 0 && (cache->row_bytes & 15) == 0;
@@ -806,7 +807,8 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
         P.scale = scale; P.head_lo = head_lo; P.n_heads = n_heads;
         P.n_reqs = batch->n_reqs; P.max_seq = max_seq_len;
         P.out = out; P.out_dtype = out_dtype; P.out_stride = out_stride; P.status = status;
-        return launch_ct(P, ct::ct_geom(lay, Gq), max_q_len, batch->n_reqs, reinterpret_cast<cudaStream_t>(stream));
+        return launch_ct(P, ct::ct_geom(lay, Gq, cache->block_size), max_q_len, batch->n_reqs,
+                         reinterpret_cast<cudaStream_t>(stream));
     }
     // else blocks of 8 (query, head) rows on the tensor-core decode when it serves the layout at 8
     // rows and the workspace holds its plan (else the fp32 kernel below)

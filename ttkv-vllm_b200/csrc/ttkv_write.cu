@@ -410,6 +410,11 @@ struct FrozenMaps {
 
 constexpr int WF_THREADS = 256;
 constexpr size_t kFusedWriteSmemMax = 200 * 1024;      // the two slices, r1 <= 200
+// The fused write stages both slices once per token, the two-launch write its decoder slice once
+// per 64-token block: the fused one is faster up to about a hundred tokens (a decode step's
+// batch; B200, r1 = 110, H = 8: 56 vs 72 us at 64 tokens, 97 vs 77 us at 128), the two-launch one
+// beyond (a prefill chunk: 215 vs 1421 us at 2048 tokens).
+constexpr int32_t kFusedMaxTokens = 96;
 constexpr int32_t kMaxGridY = 65535;
 
 __device__ __forceinline__ void cluster_arrive() {
@@ -804,7 +809,7 @@ extern "C" int ttkv_write_paged_shard(const ttkv_layout_t* lay, int32_t h_lo, in
         return fail(TTKV_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes,
                     ttkv_write_workspace_bytes(lay, n_tok));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (frozen) {
+    if (frozen && n_tok <= kFusedMaxTokens) {
         const int r = launch_frozen_fused(lay, &out, h_lo, cache, slot_mapping, n_tok, k, k_dtype, k_stride,
                                           v, v_dtype, v_stride, tok_dec, decoders, dec_stride, pinvs,
                                           pinv_stride, n_decoders, status, st);
