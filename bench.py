@@ -518,8 +518,8 @@ def run_prefill(args):
                        "chunks": len(chunks)},
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc, "unit": "TFLOP/s",
                          "frac": tflops / tc, "peak_kind": peak_kind, "read_ms_per_step": read_ms,
-                         "kernel": "decode_tc_kernel<8> over blocks of 8 (query, head) rows + "
-                                   "merge_sk_kernel (ttkv_prefill_cont_paged)",
+                         "kernel": "cont_tc_kernel (ttkv_prefill_cont_paged: a CTA per (request, KV head, "
+                                   "block of 42 queries x 3 heads), S and PV on tcgen05)",
                          "algorithmic_flop_per_step": flops},
             "gpu_launches": len(chunks) * 4}
     print(json.dumps(line))

@@ -129,20 +129,10 @@ __device__ __forceinline__ uint32_t kmajor_off(int row, int chunk) {
 }
 
 // ------------------------------------------------------------------ packed fp32 pairs (sm_100)
-__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
-__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
+// The compiler's own f32x2 builtins: it places the pairs in adjacent registers itself and can
+// fold a negated operand, which an asm block that packs its operands with mov.b64 cannot.
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 // ------------------------------------------------------------------ branch-free code decode
 // x >> s with s in [0, 32]; s = 32 gives 0.
@@ -949,7 +939,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                 #pragma unroll
                 for (int g = 0; g < G; ++g) { s2[g] = make_float2(0.f, 0.f); s2h[g] = s2[g]; }
                 const float2 csp2 = make_float2(csp, csp), krs2 = make_float2(krs, krs);
-                const float2 neg1 = make_float2(-1.f, -1.f);
                 #pragma unroll
                 for (int hp = 0; hp < 2; ++hp) {                        // 8 RoPE pairs at a time
                     const int j0 = 16 * wg + 8 * hp;
@@ -983,7 +972,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
                                                 f2mul(make_float2(al[2 * i], al[2 * i + 1]), csp2));
                         const float2 kh = f2fma(make_float2(rh[2 * i], rh[2 * i + 1]), krs2,
                                                 f2mul(make_float2(ah[2 * i], ah[2 * i + 1]), csp2));
-                        const float2 yl = f2fma(f2mul(kh, neg1), sz, f2mul(kl, cz));
+                        const float2 yl = f2fma(make_float2(-kh.x, -kh.y), sz, f2mul(kl, cz));
                         const float2 yh = f2fma(kl, sz, f2mul(kh, cz));
                         #pragma unroll
                         for (int g = 0; g < G; ++g) {
