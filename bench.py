@@ -521,7 +521,7 @@ def run_prefill(args):
                          "frac": tflops / tc_sus, "peak_kind": "bf16 sustained (%s)" % peak_kind,
                          "read_ms_per_step": read_ms,
                          "kernel": "cont_tc_kernel (ttkv_prefill_cont_paged: a CTA per (request, KV head, "
-                                   "block of 42 queries x 3 heads), S and PV on tcgen05)",
+                                   "block of 128 (query, head) rows), S and PV on tcgen05)",
                          "algorithmic_flop_per_step": flops},
             "gpu_launches": len(chunks) * 4}
     print(json.dumps(line))

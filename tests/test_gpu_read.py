@@ -171,9 +171,10 @@ def _queries(rng, shape, qdt):
     (True, "bfloat16", [70, 40, 129], [6, 1, 37]),
     (True, "float16", [300, 130, 47], [100, 129, 47])])
 def test_continuation_matches_oracle_causal(images, qdt, seqs, q_lens):
-    """With the decoders' images the chunk runs on the tensor-core continuation (row blocks of
-    42 queries x 3 heads; 100 queries span three blocks, 300 stored rows three tiles, a chunk
-    equal to its request a prompt read); without them on the 8-row blocks of the decode."""
+    """With the decoders' images the chunk runs on the tensor-core continuation (blocks of 128
+    (query, head) rows: 100 queries x 3 heads span three blocks and queries 42 and 85 have heads in
+    two blocks; 300 stored rows are three tiles; a chunk equal to its request is a prompt read);
+    without them on the 8-row blocks of the decode."""
     from vllm_ttkv import ops
     st = stores.make_store(8, seqs, cfg="safe", r1=32)
     rng = np.random.default_rng(0)
@@ -206,7 +207,8 @@ def test_continuation_other_groups_block_sizes_and_ranks(HQ, block_size, r1, cfg
     """Without images: blocks of 8 (query, head) rows on the tensor-core decode for G = 7 (a block
     ends inside a query) and G = 1 (8 queries per block); one token per block sizes the plan
     beyond the default workspace, so the fp32 kernel serves unless the workspace holds it. With
-    images: the tensor-core continuation (18 queries x 7 heads, 128 queries x 1 head per block).
+    images: the tensor-core continuation (128 (query, head) rows per block: 20 queries x 7 heads
+    are two blocks, the first ending inside query 18; 128 queries x 1 head).
     r1 = 200 is beyond both and takes the fp32 kernel; r1 = 126 is the continuation's largest
     rank, r1 = 14 a one-chunk coefficient block; the 4-bit store; a request with no queries."""
     from vllm_ttkv import ops

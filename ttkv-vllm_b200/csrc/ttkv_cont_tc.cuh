@@ -4,8 +4,10 @@
 //
 // A continuation chunk has many query rows per stored token, so the stored tile is rebuilt ONCE
 // for a whole block of rows and every product with it runs on the tensor pipe. One CTA per
-// (request, KV head, block of NQ = floor(128 / G) queries x G query heads = rows; row i is query
-// i / G, head i % G). It walks the stored 128-token tiles the block's last query can see:
+// (request, KV head, block of 128 consecutive (query, query head) rows: row i of the request's
+// chunk is query i / G, head i % G, so a query's heads may sit in two blocks and a chunk of q
+// queries takes ceil(q G / 128) CTAs per KV head). It walks the stored 128-token tiles the block's
+// last query can see:
 //
 //   MMA 1   acc[128 tokens x 128 dims] = A . B_hi + A . B_lo      (as the decode: A = int8
 //           coefficients as exact fp16, B = the decoder slice as fp16 hi + lo)
@@ -50,7 +52,6 @@ constexpr float LOG2E = 1.4426950408889634f;
 struct CtGeom {
     int natom, kp16, cb;
     int kr, vr, kvrow;
-    int nq;                           // queries per row block
     int bs_shift;                     // log2(block size) when it is a power of two, else -1
     int off_by, off_q, off_a, off_raw, off_v, off_kv, off_vr, off_red, off_bt, off_lut, off_misc;
     int smem;
@@ -177,38 +178,38 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
     const int wg = (tid >> 7) & (NWGE - 1), t = tid & 127;
     const int G = P.G;
     const int hl = int(blockIdx.y), h = P.head_lo + hl, r = int(blockIdx.z);
-    const int j0 = int(blockIdx.x) * T.nq;                   // first query of the block
+    const int row0 = int(blockIdx.x) * TM;                    // first (query, head) row of the block
     pdl_wait();
 
     // ---- the block: its queries, the stored rows its last query sees, the refusals (uniform)
     const int seq = P.seq_lens[r], ql = P.q_len[r];
-    if (j0 >= ql) return;                                    // no rows here (also for ql <= 0)
+    if (row0 >= ql * G) return;                              // no rows here (also for ql <= 0)
     if (ql > seq) {
-        if (tid == 0 && j0 == 0 && hl == 0) report(P.status, TTKV_STATUS_QUERY);
+        if (tid == 0 && blockIdx.x == 0 && hl == 0) report(P.status, TTKV_STATUS_QUERY);
         return;
     }
     if (seq > P.max_seq) {
-        if (tid == 0 && j0 == 0 && hl == 0) report(P.status, TTKV_STATUS_SEQ_BOUND);
+        if (tid == 0 && blockIdx.x == 0 && hl == 0) report(P.status, TTKV_STATUS_SEQ_BOUND);
         return;
     }
     const int di = P.dec_index[r];
     if (di < 0 || di >= P.n_decoders) {
-        if (tid == 0 && j0 == 0 && hl == 0) report(P.status, TTKV_STATUS_DECODER);
+        if (tid == 0 && blockIdx.x == 0 && hl == 0) report(P.status, TTKV_STATUS_DECODER);
         return;
     }
     if ((seq + P.block_size - 1) / P.block_size > P.bt_cols) {
-        if (tid == 0 && j0 == 0 && hl == 0) report(P.status, TTKV_STATUS_ROW_SHORT);
+        if (tid == 0 && blockIdx.x == 0 && hl == 0) report(P.status, TTKV_STATUS_ROW_SHORT);
         return;
     }
-    const int nqb = min(T.nq, ql - j0);                       // queries of this block
-    const int nrows = nqb * G;
+    const int nrows = min(TM, ql * G - row0);                 // rows of this block
+    const int jlast = (row0 + nrows - 1) / G;                 // the block's last query
     const int p0 = seq - ql;                                  // position of query 0
-    const int limit = min(seq, p0 + j0 + nqb);                // stored rows the last query sees
+    const int limit = min(seq, p0 + jlast + 1);               // stored rows the last query sees
     const int n_tiles = (limit + TM - 1) / TM;
     const int32_t* brow = P.block_table + int64_t(r) * P.bt_stride;
     const int64_t n_blocks = P.n_slots / P.block_size;
     const bool qbf = P.q_dtype == TTKV_BF16;
-    const int qrow0 = P.q_start[r] + j0;
+    const int qrow0 = P.q_start[r];                           // the chunk's query 0 in q / out
 
     // ---- set-up: TMEM, barriers, shift tables
     if (w == NEPI / 32) tmem_alloc(&M->tmem_base, TMEM_COLS);
@@ -428,9 +429,9 @@ __global__ void __launch_bounds__(NTHR, 1) cont_tc_kernel(const ReadParams P, co
         const bool tbf16 = P.table_dtype == TTKV_BF16;
         const float sl2 = P.scale * LOG2E;                    // scores in base 2
         // this thread's row (softmax): query jq of the block, head g; its causal limit
-        const int jq = t / G, g = t - (t / G) * G;
+        const int jq = (row0 + t) / G, g = row0 + t - jq * G;
         const bool row_ok = t < nrows;
-        const int row_lim = row_ok ? p0 + j0 + jq + 1 : 0;       // sees stored rows < row_lim
+        const int row_lim = row_ok ? p0 + jq + 1 : 0;            // sees stored rows < row_lim
         float m_run = -INFINITY, l_run = 0.f;
 
         // Q row t (query jq, head g), dims [32wg, 32wg + 32), into its operand once for all tiles
@@ -752,7 +753,6 @@ inline CtGeom ct_geom(const ttkv_layout_t* lay, int G, int block_size) {
     T.kp16 = round_up(lay->r1, 16);
     T.natom = (T.kp16 + 63) / 64;
     T.cb = round_up(lay->coeff_bytes + 2, 16);
-    T.nq = 128 / G;
     T.bs_shift = -1;
     for (int s = 0; s < 31; ++s)
         if (block_size == (1 << s)) T.bs_shift = s;

@@ -691,7 +691,7 @@ int launch_ct(const ReadParams& P, const ct::CtGeom& T, int max_q_len, int n_req
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((max_q_len + T.nq - 1) / T.nq, P.n_heads, n_reqs);
+    cfg.gridDim = dim3(unsigned((int64_t(max_q_len) * P.G + tc::TM - 1) / tc::TM), P.n_heads, n_reqs);
     cfg.blockDim = dim3(ct::NTHR);
     cfg.dynamicSmemBytes = T.smem;
     cfg.stream = st;
