@@ -29,7 +29,8 @@ constexpr uint32_t FULL = 0xffffffffu;
 // ------------------------------------------------------------------ warp select + pack
 // One warp packs one 128-lane row x (lane L of the warp holds lanes 4L..4L+3) into `dst`
 // (bitmap d/8 bytes, ceil(lanes*bits/8) code bytes, fp16 ruler). `codes` is 128 bytes of
-// per-warp scratch in shared memory.
+// per-warp scratch in shared memory, 4-byte aligned: the code stream is assembled there as 32
+// big-endian words (stream bit p is bit 31 - p % 32 of word p / 32).
 //
 // Selection (select_triton.py:180-193): the k-th largest |x| is built one bit at a time on the
 // fp32 magnitude bits (monotone for non-negative floats); every lane above it is kept, then the
@@ -91,12 +92,24 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
     const float rmax = __uint_as_float(umax);
     const float sc = __fmul_rn(rmax == 0.f ? 1.f : rmax, inv_ruler(bits));
     const float lo = -float(1 << (bits - 1)), hi = float((1 << (bits - 1)) - 1);
+    uint32_t* words = reinterpret_cast<uint32_t*>(codes);
+    words[L] = 0u;
+    __syncwarp();
+    // the k-th kept code occupies stream bits [k * bits, (k + 1) * bits), MSB first; a code that
+    // crosses a word boundary is split over the two words
     #pragma unroll
     for (int i = 0; i < 4; ++i) {
         if (sel[i]) {
             float qf = rintf(__fdiv_rn(x[i], sc));
             qf = fminf(fmaxf(qf, lo), hi) + float(1 << (bits - 1));
-            codes[rank] = uint8_t(qf);
+            const uint32_t c = uint32_t(qf);
+            const int pos = rank * bits, wi = pos >> 5, off = pos & 31, spill = off + bits - 32;
+            if (spill <= 0) {
+                atomicOr(&words[wi], c << (32 - bits - off));
+            } else {
+                atomicOr(&words[wi], c >> spill);
+                atomicOr(&words[wi + 1], c << (32 - spill));
+            }
             ++rank;
         }
     }
@@ -106,20 +119,11 @@ __device__ __forceinline__ void warp_select_pack(const float (&x)[4], int lanes,
     const uint32_t other = __shfl_down_sync(FULL, nib, 1);
     if ((L & 1) == 0) dst[L >> 1] = uint8_t((nib << 4) | other);
     __syncwarp();
-    // codes: MSB-first stream, row padded to whole bytes (codec/ttkv_packed_cache.py:50-66)
+    // codes: MSB-first stream, row padded to whole bytes (codec/ttkv_packed_cache.py:50-66); byte
+    // j of the stream is byte 3 - j % 4 of word j / 4
     const int pb = packed_row_bytes(lanes, bits);
-    for (int by = L; by < pb; by += 32) {
-        uint32_t v = 0;
-        #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const int pos = by * 8 + b;
-            const int ci = pos / bits;
-            uint32_t bit = 0;
-            if (ci < lanes) bit = (uint32_t(codes[ci]) >> (bits - 1 - pos % bits)) & 1u;
-            v |= bit << (7 - b);
-        }
-        dst[16 + by] = uint8_t(v);
-    }
+    for (int by = L; by < pb; by += 32)
+        dst[16 + by] = uint8_t(words[by >> 2] >> (24 - 8 * (by & 3)));
     if (L == 0) store_f16_bytes(dst + 16 + pb, sc);
     __syncwarp();
 }
@@ -443,7 +447,7 @@ __global__ void __launch_bounds__(WF_THREADS) write_frozen_kernel(const FrozenPa
     __shared__ float g_s[kMaxRank];
     __shared__ int8_t cq_s[kMaxRank];
     __shared__ float kd_s[2][kHeadDim];
-    __shared__ uint8_t codes_s[2][128];
+    __shared__ __align__(16) uint8_t codes_s[2][128];
     __shared__ float wmax_s[WF_THREADS / 32];
     __shared__ float cs_s;
     __shared__ __align__(8) uint64_t bar;
@@ -572,7 +576,7 @@ struct RowsParams {
 
 // 4 rows per CTA, one warp each; row i = h*n_tok + t (select_triton.py:173-177).
 __global__ void __launch_bounds__(128) select_rows_kernel(const RowsParams P) {
-    __shared__ uint8_t codes_s[4][128];
+    __shared__ __align__(16) uint8_t codes_s[4][128];
     const int w = threadIdx.x >> 5, L = threadIdx.x & 31;
     const int64_t i = int64_t(blockIdx.x) * 4 + w;
     if (i >= int64_t(P.n_tok) * P.heads) return;
