@@ -13,10 +13,13 @@ the stores are encoded by this repository's own encoder (device TT-SVD fit per r
 layer, then the CUDA writer). The per-step working set (~0.9 GB of slots) exceeds L2, so no flush
 is needed between steps.
 
-Multi-GPU (torchrun): KV heads are sharded across ranks for the read (rank g reads heads
-[g*H/N, (g+1)*H/N) of every request from its replica of the cache) and the per-layer head outputs
-are all-gathered over NCCL; the write is replicated (each rank encodes the step's tokens into its
-own replica). Total work is fixed as N grows ("strong").
+Multi-GPU (torchrun): KV heads are sharded across ranks for the read (rank g stores and reads heads
+[g*H/N, (g+1)*H/N) of every request, the storage-sharded format) and every rank ends each layer
+with every head of the output: by default the decode's merge stores its rows into every rank's
+output over NVLink peer memory and the step waits on the device for the other ranks' rows
+(`--gather p2p`, no collective per layer), or through an NCCL all-gather per layer (`--gather
+nccl`). The write's projection is replicated (every rank projects the step's tokens, then packs
+its own heads). Total work is fixed as N grows ("strong").
 """
 from __future__ import annotations
 
@@ -201,6 +204,7 @@ class Workload:
             self.q.append(qv)
             self.out.append(self.outbuf[l * B * HQ * 128:(l + 1) * B * HQ * 128].view(B, HQ, 128))
         self.heads = (0, H)
+        self.peers = None                      # per layer ttkv_peers_t of a fused gather (PeerGather)
         self.read_layouts = list(self.layouts)
         self.read_dec = list(self.decoders)
         self.table = torch.from_numpy(synthetic.cos_sin_cache(seq + 16, dtype="float32")).to(device).to(dtype)
@@ -249,7 +253,8 @@ class Workload:
         G = self.HQ // self.H
         ops.decode_paged(self.read_layouts[l], self.caches[l], self.bs, self.block_table, self.seq_lens,
                          self.read_dec[l], self.dec_index, self.table, self.q[l][:, lo * G:hi * G],
-                         self.scale, self.out[l][:, lo * G:hi * G], self.max_seq, images=self.images[l])
+                         self.scale, self.out[l][:, lo * G:hi * G], self.max_seq, images=self.images[l],
+                         peers=self.peers[l] if self.peers else None)
 
     def layer_step(self, l):
         """One layer: write the step's token of every request, then read every request's store."""
@@ -785,6 +790,9 @@ def main():
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--cfg", default="safe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: the head outputs gathered by the decode's merge over NVLink peer "
+                         "stores (p2p) or by an NCCL all-gather per layer (nccl)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying a CUDA graph per step")
     ap.add_argument("--workload", default="decode",
@@ -856,13 +864,24 @@ def main():
         wl.shard(head_lo, head_hi)                 # each rank stores only its heads' rows
     setup_s = time.perf_counter() - t0
 
+    pg = None
+    if sh is not None and args.gather == "p2p":
+        # the layer outputs live in memory every rank maps (CUDA IPC); the decode's merge stores
+        # each row into every rank's copy and the step waits on the device for the others' rows
+        from vllm_ttkv.shard import PeerGather
+        pg = PeerGather(sh, wl.L, wl.B, 128, wl.dtype, device)
+        wl.outbuf = pg.all_out.reshape(-1)
+        wl.out = [pg.out(l) for l in range(wl.L)]
+        wl.peers = [pg.peers(l) for l in range(wl.L)]
     bufs = [sh.buffers(wl.B, 128, wl.dtype, device) for _ in range(wl.L)] if sh else None
 
     def layer_work(l):
-        """The layer's launches on this rank (what a layer graph holds): write, read, and the copy
-        of this rank's query heads into the all-gather's send buffer."""
+        """The layer's launches on this rank: write, read, and either the wait for the other
+        ranks' rows (p2p) or the copy of this rank's query heads into the all-gather's send buffer."""
         wl.layer_step(l)
-        if sh is not None:
+        if pg is not None:
+            pg.wait(l)
+        elif sh is not None:
             sh.pack(wl.out[l], bufs[l][0])
 
     graphs = None
@@ -870,7 +889,7 @@ def main():
     def step_work():
         for l in range(wl.L):
             layer_work(l)
-            if sh is not None:                             # this layer's heads from every rank
+            if sh is not None and pg is None:              # this layer's heads from every rank
                 sh.gather(*bufs[l])
                 sh.assemble(bufs[l][1], wl.out[l])         # every rank ends with all heads
 
@@ -882,6 +901,20 @@ def main():
                 step_work()
 
     run_steps(args.warmup)
+    gather_check = None
+    if pg is not None:
+        # once, outside the timing: every rank's gathered outputs against an NCCL all-gather of
+        # the ranks' own heads (the same collectives on every rank, in the same order)
+        torch.cuda.synchronize(device)
+        err = 0.0
+        for l in range(wl.L):
+            send, recv = bufs[l]
+            sh.pack(wl.out[l], send)
+            sh.gather(send, recv)
+            ref = torch.empty_like(wl.out[l])
+            sh.assemble(recv, ref)
+            err = max(err, float((ref.float() - wl.out[l].float()).abs().max().item()))
+        gather_check = {"max_abs_diff_vs_nccl_all_gather": err, "layers": wl.L}
     if not args.no_graph:
         # one CUDA graph for the whole step, captured after the warm-up allocated every workspace
         # (and, on several GPUs, after the NCCL communicator ran its first collectives); the 28
@@ -989,7 +1022,7 @@ def main():
                          f"x{args.batch * len(r1s)}"}
 
     # per layer: write (write_frozen_kernel) + read (decode kernel + merge_sk_kernel)
-    launches = wl.L * 3
+    launches = wl.L * (4 if pg is not None else 3)     # + the device wait of the fused gather
     cap = CAPTURED_LAUNCH["layer"]
     traffic, traffic_src = None, "no ncu capture of this kernel build"
     if CAPTURED_LAUNCH["dram_bytes"] and CAPTURED_LAUNCH["src_sha16"] == read_src_sha16() and cap < wl.L \
@@ -1018,7 +1051,13 @@ def main():
                            "storage": ("storage-sharded: coefficient block + this rank's heads' rows"
                                        if world > 1 else "full blobs"),
                            "launch": ("eager" if not graphs else "one CUDA graph per step" if sh is None
-                                      else "one CUDA graph per step, the 28 all-gathers captured in it"),},
+                                      else "one CUDA graph per step, the 28 all-gathers captured in it"
+                                      if pg is None else "one CUDA graph per step, no collective in it"),
+                           "gather": (None if sh is None else "nccl all_gather_into_tensor per layer"
+                                      if pg is None else "fused into the decode's merge: NVLink peer "
+                                      "stores into every rank's output + a device wait on signal words "
+                                      "(CUDA IPC memory, no multicast)"),
+                           "gather_check": gather_check},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                              "kernel": "decode_tc_kernel<3> + merge_sk_kernel (ttkv_decode_paged)",
@@ -1042,6 +1081,8 @@ def main():
         print(json.dumps(line))
     graphs = None
     torch.cuda.synchronize(device)
+    if pg is not None:
+        pg.close()
     if world > 1:
         dist.destroy_process_group()
 

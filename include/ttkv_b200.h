@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define TTKV_ABI_VERSION 4
+#define TTKV_ABI_VERSION 5
 
 /* host-side refusals (return values) */
 #define TTKV_OK 0
@@ -200,6 +200,52 @@ int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cach
                               void* out, int32_t out_dtype, int64_t out_stride,
                               int32_t max_seq_len, int32_t* status, void* stream);
 
+/* ---------------------------------------------------------------- decode, head-sharded, gathered over NVLink
+ * No counterpart in the reference (it has no multi-GPU path): the all-gather of a KV-head-sharded
+ * decode's outputs, fused into the decode's segment merge. Every rank of a group of `world`
+ * processes (one per GPU) reads its KV heads [head_lo, head_hi) and holds the layer's whole output
+ * [n_reqs, HQ, d]; the merge stores each output row into its own `out` AND, at the same byte
+ * offset, into every other rank's (peer stores over NVLink), then counts one arrival per merge
+ * CTA on every rank's signal word. ttkv_peer_wait then waits until the local signal word has
+ * seen every rank's arrivals for this step, after which `out` holds every head. What it replaces:
+ * the copy of a rank's heads into a send buffer, the NCCL all-gather and the copy back.
+ *   - out[p] is rank p's `out` pointer (the same view: base, head offset, stride and dtype on every
+ *     rank) mapped into this process (ttkv_ipc_open), out[rank] == the `out` argument;
+ *   - signal[p] is rank p's signal word for this layer (8 bytes, zeroed once, never reset),
+ *     mapped likewise; epoch is this rank's own counter word for the same layer (local, zeroed
+ *     once): ttkv_peer_wait(step k) waits for signal >= k * arrivals_per_step;
+ *   - arrivals_per_step = world * G * (head_hi - head_lo) * n_reqs (every rank's merge CTAs);
+ *   - served by the tensor-core decode only; other layouts are refused (TTKV_ERR_UNSUPPORTED) and
+ *     the caller gathers another way. world <= TTKV_MAX_PEERS.
+ * The wait is bounded (about 2 s): a rank that never arrives sets TTKV_STATUS_TIMEOUT; the epoch
+ * still advances, and the group is then out of step and must be rebuilt. */
+#define TTKV_MAX_PEERS 8
+typedef struct {
+    int32_t world, rank;
+    void* out[TTKV_MAX_PEERS];
+    unsigned long long* signal[TTKV_MAX_PEERS];
+    unsigned long long* epoch;
+} ttkv_peers_t;
+int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                             const ttkv_batch_t* batch, const ttkv_rope_t* rope,
+                             const void* q, int32_t q_dtype, int64_t q_stride, int32_t HQ,
+                             float scale, int32_t head_lo, int32_t head_hi,
+                             void* out, int32_t out_dtype, int64_t out_stride,
+                             int32_t max_seq_len, void* workspace, size_t workspace_bytes,
+                             const ttkv_peers_t* peers, int32_t* status, void* stream);
+int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals_per_step, int32_t* status, void* stream);
+
+/* Device memory shared between the processes of a group through CUDA IPC handles (plain peer
+ * mappings, no multicast object): ttkv_ipc_alloc allocates `bytes` (zeroed, on the current
+ * device) and writes its handle (ttkv_ipc_handle_bytes bytes) for the other processes, which map
+ * it with ttkv_ipc_open and unmap it with ttkv_ipc_close; the owner frees it with ttkv_ipc_free
+ * after every peer has closed it. */
+size_t ttkv_ipc_handle_bytes(void);
+int ttkv_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int ttkv_ipc_open(const void* handle, void** ptr);
+int ttkv_ipc_close(void* ptr);
+int ttkv_ipc_free(void* ptr);
+
 /* ---------------------------------------------------------------- read: continuation
  * Multi-query read for chunked-prefill / prefix-cache continuations: request r has q_len[r]
  * query tokens at q + (q_start[r] + j)*q_stride, [HQ, d] each, at absolute positions
@@ -207,11 +253,14 @@ int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cach
  * Replaces vllm_ttkv/impl.py:725-778 (_prefill_continuation: krt_multi_from_slots
  * krt_triton.py:269-317, softmax, v_out_multi_from_slots v_out_triton.py:249-294), without
  * materialising the [HQ, Q, n] scores. Outputs at out + (q_start[r] + j)*out_stride.
- * For a layout the tensor-core decode serves, the chunks run on it: a request's (query, query
- * head) rows, query-major, in blocks of 8, each block one decode request with a causal limit per
- * row. ttkv_prefill_workspace_bytes sizes the workspace for that plan with caches of 16 tokens
- * per block (for smaller blocks a workspace below the plan's needs makes the call use the fp32
- * kernel instead). */
+ * With the decoders' operand images (batch->dec_image), 16-bit queries, r1 <= 126 and 16-byte
+ * aligned slot rows, one CTA per (request, KV head, block of 128 (query, head) rows) rebuilds
+ * each stored tile once and runs the scores and the V readout on the tensor cores; it needs no
+ * workspace. Otherwise, for a layout the tensor-core decode serves, the chunks run on it: a
+ * request's (query, query head) rows, query-major, in blocks of 8, each block one decode request
+ * with a causal limit per row. ttkv_prefill_workspace_bytes sizes the workspace for that plan
+ * with caches of 16 tokens per block (for smaller blocks a workspace below the plan's needs makes
+ * the call use the fp32 kernel instead). */
 size_t ttkv_prefill_workspace_bytes(const ttkv_layout_t* lay, int32_t n_reqs, int32_t HQ,
                                     int32_t max_q_len, int32_t max_seq_len,
                                     int32_t head_lo, int32_t head_hi);

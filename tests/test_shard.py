@@ -80,3 +80,75 @@ def _rank_fails_before_gather(rank, world, port):
 def test_a_rank_that_fails_before_the_gather_ends_the_job_with_an_error():
     with pytest.raises(Exception):
         mp.spawn(_rank_fails_before_gather, args=(2, _free_port()), nprocs=2, join=True)
+
+
+class _FakeIpcLib:
+    """Stands in for the library's CUDA IPC calls on a CPU: an allocation is a fresh fake address
+    per rank, its handle names it, and opening a handle maps it at an address of this rank's."""
+
+    def __init__(self, rank):
+        self.rank, self.next, self.log = rank, 0x10000000 * (rank + 1), []
+
+    def ttkv_ipc_handle_bytes(self):
+        return 64
+
+    def ttkv_ipc_alloc(self, nbytes, ptr, handle):
+        ptr._obj.value = self.next
+        tag = f"{self.rank}:{self.next:x}:{nbytes}".encode()
+        handle[:len(tag)] = tag
+        self.log.append(("alloc", self.next, nbytes))
+        self.next += 0x1000000
+        return 0
+
+    def ttkv_ipc_open(self, handle, ptr):
+        rank, addr, _ = bytes(handle).rstrip(b"\0").decode().split(":")
+        ptr._obj.value = 0x900000000 + int(rank) * 0x10000000 + int(addr, 16) % 0x10000000
+        self.log.append(("open", int(rank), int(addr, 16)))
+        return 0
+
+    def ttkv_ipc_close(self, ptr):
+        self.log.append(("close", ptr))
+        return 0
+
+    def ttkv_ipc_free(self, ptr):
+        self.log.append(("free", ptr))
+        return 0
+
+    def ttkv_last_error(self):
+        return b""
+
+
+def _rank_peer_tables(rank, world, port):
+    from vllm_ttkv.shard import PeerGather
+    _init(rank, world, port)
+    try:
+        B, HQ, d, L = 3, 24, 128, 4
+        sh = HeadShard(8, HQ)
+        fake = _FakeIpcLib(rank)
+        g = PeerGather(sh, L, B, d, torch.bfloat16, "cpu", lib=fake)
+        layer = B * HQ * d * 2
+        assert g.arrivals == world * sh.G * (8 // world) * B == sh.G * 8 * B
+        own = [a for op, a, n in fake.log if op == "alloc"]
+        assert [n for op, a, n in fake.log if op == "alloc"] == [L * layer, L * 8]
+        opened = [(r, a) for op, r, a in fake.log if op == "open"]
+        assert sorted({r for r, _ in opened}) == [p for p in range(world) if p != rank]
+        for l in range(L):
+            st = g.peers(l)
+            assert (st.world, st.rank) == (world, rank)
+            assert st.epoch == g.epoch.data_ptr() + 8 * l
+            for p in range(world):
+                base = g.bases[p]
+                assert st.out[p] == base + l * layer + sh.q_lo * d * 2       # this rank's head view
+                assert st.signal[p] == g.signals[p] + 8 * l
+            assert st.out[rank] == own[0] + l * layer + sh.q_lo * d * 2
+        g.close(barrier=dist.barrier)
+        assert [op for op, *_ in fake.log[-3:]] == ["close", "free", "free"] or world == 1
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_gather_maps_every_ranks_output_and_signal_words():
+    """The fused gather's host side on two gloo ranks: one IPC allocation for the outputs of all
+    layers and one for the signal words, the handles exchanged, every other rank's memory mapped,
+    and per layer a ttkv_peers_t whose out[p] is rank p's output at this rank's head offset."""
+    mp.spawn(_rank_peer_tables, args=(2, _free_port()), nprocs=2, join=True)

@@ -92,3 +92,49 @@ extern "C" int ttkv_layout_init(ttkv_layout_t* lay, int32_t H, int32_t d, int32_
     lay->blob_bytes = lay->k_slot_bytes + lay->v_slot_bytes;
     return TTKV_OK;
 }
+
+// ---------------------------------------------------------------- memory shared through CUDA IPC
+extern "C" size_t ttkv_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int ttkv_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return fail(TTKV_ERR_ARG, "ipc alloc: null pointer or zero bytes");
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (*ptr) cudaFree(*ptr);
+        *ptr = nullptr;
+        return fail(TTKV_ERR_CUDA, "ipc alloc of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    return TTKV_OK;
+}
+
+extern "C" int ttkv_ipc_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return fail(TTKV_ERR_ARG, "ipc open: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *ptr = nullptr;
+        return fail(TTKV_ERR_CUDA, "ipc open: %s", cudaGetErrorString(e));
+    }
+    return TTKV_OK;
+}
+
+extern "C" int ttkv_ipc_close(void* ptr) {
+    if (!ptr) return TTKV_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) { cudaGetLastError(); return fail(TTKV_ERR_CUDA, "ipc close: %s", cudaGetErrorString(e)); }
+    return TTKV_OK;
+}
+
+extern "C" int ttkv_ipc_free(void* ptr) {
+    if (!ptr) return TTKV_OK;
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) { cudaGetLastError(); return fail(TTKV_ERR_CUDA, "ipc free: %s", cudaGetErrorString(e)); }
+    return TTKV_OK;
+}

@@ -6,7 +6,7 @@
 // The work is the list of (request, KV head, 128-token tile) units, request-major; CTA c takes the
 // c-th equal share of it, computed on the device from seq_lens, and walks it as segments, one per
 // (request, KV head) it touches, each leaving a partial (o, max, sum) that merge_sk_kernel
-// combines. A segment's tokens must fit the block-table slice a CTA caches (BT_CAP blocks), so when
+// combines. A segment spans at most BT_CAP blocks (the bound the workspace is sized with), so when
 // the shares would be longer than that the device cuts every share into k equal virtual shares
 // (k from the batch's total), and a segment also ends at a virtual boundary. Within a segment, token t of the current tile is TMEM lane t;
 // warpgroup c handles a quarter of that token's 128 head lanes (the RoPE pairs j, j+64 for j in
@@ -253,7 +253,8 @@ struct TcMaps {
 };
 
 constexpr int RP_BOX = 128 * 128;        // one TMA box of RoPE rows: 128 positions x 64 x 16-bit
-constexpr int BT_CAP = 512;              // block-table entries a CTA caches (its token range)
+constexpr int BT_CAP = 512;              // blocks a segment may span; its shared region (2 KB) holds
+                                         // the slot-row offsets of two tiles
 constexpr int KV_PAD = 16;               // code windows may read a few bytes past the last row
 constexpr uint32_t RED_COL = 272;        // TMEM columns of the partial scores: [warpgroup][8 heads]
 
@@ -351,7 +352,9 @@ __device__ __forceinline__ int cta_scan(int v, int* wsum, int& total) {
     return pre + x - v;
 }
 
-template <int G>
+// TBF16: the RoPE table holds bf16 (else fp16) values, fixed at compile time so the conversion of
+// its rows costs no per-element select
+template <int G, bool TBF16>
 __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, const TcGeom T,
                                                              const __grid_constant__ TcMaps maps) {
     extern __shared__ __align__(1024) unsigned char smem_dyn[];
@@ -561,7 +564,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     const float kmag_f = 8388608.f + float(khalf);
     const uint32_t vmag2 = 0x64006400u | (vhalf * 0x10001u);       // fp16 pair 1024 + code
     const __half2 vbias2 = __floats2half2_rn(1024.f + float(vhalf), 1024.f + float(vhalf));
-    const bool tbf16 = P.table_dtype == TTKV_BF16;
+    constexpr bool tbf16 = TBF16;
     const float scale = P.scale;
     const float4* qs4 = reinterpret_cast<const float4*>(qs);
 
@@ -623,29 +626,37 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const uint32_t bsz = uint32_t(P.block_size);
         const uint64_t mul_bs = (0x100000000ull + bsz - 1) / bsz;
         const int blk0 = t_begin / P.block_size;
-        const int32_t* bts = reinterpret_cast<const int32_t*>(base + T.off_bt);
-        auto slot_at = [&](int tok) -> int64_t {
+        static_assert(BT_CAP * 4 >= 2 * TM * 8, "the slot-row table lives in the block-table region");
+        auto slot_at = [&](int tok) -> int64_t {              // tok of this segment (its blocks are checked)
             const uint32_t blk = uint32_t((uint64_t(uint32_t(tok)) * mul_bs) >> 32);
-            return int64_t(bts[int(blk) - blk0]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
+            return int64_t(brow[blk]) * P.block_size + int64_t(uint32_t(tok) - blk * bsz);
         };
         auto ntok = [&](int tile) { return tile < n_tiles ? min(TM, t_end - (t_begin + tile * TM)) : 0; };
+        // byte offsets of the slot rows of a tile's tokens (slot * row_bytes), two tiles' worth by
+        // tile parity, written one barrier before the copies of that tile go out, so that a copy
+        // costs one shared load instead of a block lookup
+        int64_t* trs = reinterpret_cast<int64_t*>(base + T.off_bt);
+        auto fill_rows = [&](int tile, int u) {
+            trs[(tile & 1) * TM + u] = u < ntok(tile) ? slot_at(t_begin + tile * TM + u) * P.row_bytes : 0;
+        };
         auto issue_cf = [&](int tile) {
-            const int t0k = t_begin + tile * TM, n = ntok(tile) * cch;
+            const int n = ntok(tile) * cch;
+            const int64_t* tr = trs + (tile & 1) * TM;
             for (int i = tid; i < n; i += NTHR) {
                 // i / cch as a multiply-high; a one-chunk block (r1 <= 14) has no such multiplier
                 const uint32_t u = cch == 1 ? uint32_t(i) : __umulhi(uint32_t(i), mul_cf),
                                c = uint32_t(i) - u * uint32_t(cch);
-                cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))),
-                           P.cache + slot_at(t0k + int(u)) * P.row_bytes + 16 * c);
+                cp_async16(cfb + u * T.cf_pitch + 16 * (c ^ (u & uint32_t(T.cf_swz))), P.cache + tr[u] + 16 * c);
             }
             cp_async_arrive(&M->mb_cf);
         };
         auto issue_kv = [&](int tile) {
-            const int b = kv_buf(tile), t0k = t_begin + tile * TM, n = ntok(tile) * nkvc;
+            const int b = kv_buf(tile), n = ntok(tile) * nkvc;
+            const int64_t* tr = trs + (tile & 1) * TM;
             unsigned char* dstb = kvb + size_t(b) * TM * T.kvrow;
             for (int i = tid; i < n; i += NTHR) {
                 const uint32_t u = __umulhi(uint32_t(i), mul_kv), c = uint32_t(i) - u * uint32_t(nkvc);
-                const uint8_t* src = P.cache + slot_at(t0k + int(u)) * P.row_bytes;
+                const uint8_t* src = P.cache + tr[u];
                 unsigned char* dst = dstb + u * T.kvrow;
                 if (int(c) < kch) cp_async16(dst + 16 * c, src + (kfield - koff) + 16 * c);
                 else cp_async16(dst + T.kr + 16 * (c - kch), src + (vfield - voff) + 16 * (c - kch));
@@ -657,8 +668,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             tma_load_2d(rpb, &maps.rope, 0, t_begin + tile * TM, &M->mb_rp);
             tma_load_2d(rpb + RP_BOX, &maps.rope, 64, t_begin + tile * TM, &M->mb_rp);
         };
-        // ---- the segment's set-up. Pass 1: its block-table slice (each id checked against the
-        // cache) and its query rows; then the first tile's copies go out at once. Pass 2, under
+        // ---- the segment's set-up. Pass 1: its block ids (each checked against the cache) and
+        // its query rows; then the slot rows of its first two tiles and the first tile's copies. Pass 2, under
         // those copies: the largest |value| of its decoder slice, coalesced rows w + 16 i. After
         // that barrier thread t converts column t of the 8-row chunks wg, wg + NWG, ...
         const float* dec = P.decoders + int64_t(bad ? 0 : di) * P.dec_stride + h * 128 + t;
@@ -666,13 +677,11 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const int nchunk = T.kp16 / 8;
         int local_bad = 0;
         if (!bad) {
-            int32_t* btw = reinterpret_cast<int32_t*>(base + T.off_bt);
             const int nblk = (t_end - 1) / P.block_size - blk0 + 1;        // <= BT_CAP (checked above)
             const int64_t n_blocks = P.n_slots / P.block_size;
             for (int i = tid; i < nblk; i += NTHR) {
                 const int32_t blk = brow[blk0 + i];
                 if (blk < 0 || blk >= n_blocks) local_bad = 1;
-                btw[i] = blk;
             }
             for (int i = tid; i < G * 128; i += NTHR) {
                 const int g = i >> 7, j = i & 127;
@@ -696,7 +705,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             if (P.v_req) lim = tid < P.v_nq[r] ? P.v_pos[r] + (P.v_f0[r] + tid) / P.g_real + 1 : 0;
             M->lim[tid] = lim;
         }
-        if (__syncthreads_or(local_bad)) {                 // block-table slice cached and checked
+        if (__syncthreads_or(local_bad)) {                 // the segment's block ids checked
             if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
             bad = true;
         }
@@ -705,6 +714,8 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             __syncthreads();
             continue;
         }
+        if (tid < 2 * TM && (tid >> 7) < n_tiles) fill_rows(tid >> 7, tid & 127);   // tiles 0 and 1
+        __syncthreads();
         issue_cf(0);
         issue_kv(0);
         if (tid == RP_TID && T.rope_smem) issue_rp(0);
@@ -813,6 +824,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             const uint32_t kv_off = uint32_t(kvrow - base);
             // the next tile's K/V fields, into the other buffer (read by the tile before this one)
             if (T.nkv == 2 && has_next) { issue_kv(it + 1); mark_kv(it + 1); }
+            // the slot rows of tile it + 2 over those of tile it, whose copies went out a barrier
+            // ago; read after this tile's first barrier
+            if (wg == NWG - 1 && it + 2 < n_tiles) fill_rows(it + 2, t);
             const uint32_t rcol = uint32_t(it & 1) * 128u;                 // this tile's reconstruction columns
             const float csp = csp_next;
 
@@ -1213,11 +1227,22 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
     }
     if (!P.v_req) {
         const int head_q = (P.head_lo + hl) * P.G + g;
-        store_elt(P.out, P.out_dtype, int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane, v);
+        const int64_t at = int64_t(r) * P.out_stride + int64_t(head_q) * 128 + lane;
+        store_elt(P.out, P.out_dtype, at, v);
+        // the fused all-gather: the same row at the same offset of every other rank's output
+        for (int p = 0; p < P.n_peers; ++p)
+            if (p != P.peer_rank) store_elt(P.peer_out[p], P.out_dtype, at, v);
     } else if (g < P.v_nq[r]) {                                // row g = (query jq, head gh)
         const int f = P.v_f0[r] + g, jq = f / P.g_real, gh = f - jq * P.g_real;
         store_elt(P.out, P.out_dtype, int64_t(P.v_qrow[r] + jq) * P.out_stride +
                                       int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
+    }
+    if (P.n_peers > 0) {
+        // every thread's stores reach the peers before this CTA's arrival on their signal words
+        __threadfence_system();
+        __syncthreads();
+        if (lane == 0)
+            for (int p = 0; p < P.n_peers; ++p) atomicAdd_system(P.peer_sig[p], 1ull);
     }
 }
 

@@ -83,6 +83,12 @@ struct ReadParams {
     int out_dtype;
     int64_t out_stride;
     int32_t* status;
+    // the merge's fused all-gather (ttkv_decode_paged_gather): n_peers > 0 stores every output row
+    // also at the same offset of peer_out[p] (p != peer_rank) and counts one arrival per merge CTA
+    // on every peer_sig[p]
+    int n_peers, peer_rank;
+    void* peer_out[TTKV_MAX_PEERS];
+    unsigned long long* peer_sig[TTKV_MAX_PEERS];
 };
 
 struct Smem {
@@ -629,7 +635,7 @@ bool tc_maps(tc::TcMaps* M, const tc::TcGeom& T, const ReadParams& P) {
 template <int G>
 int launch_tc_g(const ReadParams& P, const tc::TcGeom& T, const tc::TcMaps& maps, const Plan& pl, int n_reqs,
                 cudaStream_t st) {
-    auto k = tc::decode_tc_kernel<G>;
+    auto k = P.table_dtype == TTKV_BF16 ? tc::decode_tc_kernel<G, true> : tc::decode_tc_kernel<G, false>;
     if (int e = raise_smem_limit(reinterpret_cast<const void*>(k), "decode_tc_kernel")) return e;
     // both launches may start while the kernel before them runs (programmatic dependent launch):
     // the decode waits for the step's write before its first cache read, the merge for the decode
@@ -717,6 +723,28 @@ int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
 }
 
+// The gathered decode's wait (ttkv_peer_wait): this rank's signal word must reach epoch *
+// arrivals_per_step, every rank's merge CTAs of this step having stored their rows here first
+// (each fenced its stores system-wide before its arrival). One thread polls with an acquire load;
+// the wait is bounded, and the epoch advances either way.
+__global__ void peer_wait_kernel(const unsigned long long* sig, unsigned long long* epoch,
+                                 unsigned long long arrivals_per_step, int32_t* status) {
+    if (threadIdx.x != 0) return;
+    const unsigned long long ep = *epoch + 1, target = ep * arrivals_per_step;
+    const long long t0 = clock64();
+    bool ok = true;
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(sig) : "memory");
+        if (v >= target) break;
+        if (clock64() - t0 > kWaitCycles) { ok = false; break; }
+        __nanosleep(128);
+    }
+    *epoch = ep;
+    if (!ok) report(status, TTKV_STATUS_TIMEOUT);
+    __threadfence_system();
+}
+
 }  // namespace
 }  // namespace ttkv
 
@@ -779,7 +807,8 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
                       const int32_t* q_len, const void* q, int32_t q_dtype, int64_t q_stride,
                       int32_t HQ, float scale, int32_t head_lo, int32_t head_hi, void* out,
                       int32_t out_dtype, int64_t out_stride, int32_t max_q_len, int32_t max_seq_len,
-                      void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+                      void* workspace, size_t ws_bytes, int32_t* status, void* stream,
+                      const ttkv_peers_t* peers = nullptr) {
     if (int e = check_read_args(multi, lay, cache, batch, rope, q_start, q_len, q, q_dtype, q_stride, HQ,
                                 head_lo, head_hi, out, out_dtype, out_stride, max_q_len, max_seq_len))
         return e;
@@ -797,6 +826,13 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
     if (use_tc) {
         T = tc::tc_geom(lay, HQ / lay->H);
         use_tc = tc_maps(&maps, T, P);
+    }
+    if (peers) {
+        if (!use_tc)
+            return fail(TTKV_ERR_UNSUPPORTED, "the gathered decode needs the tensor-core decode (r1=%d)", lay->r1);
+        P.n_peers = peers->world;
+        P.peer_rank = peers->rank;
+        for (int i = 0; i < peers->world; ++i) { P.peer_out[i] = peers->out[i]; P.peer_sig[i] = peers->signal[i]; }
     }
     const int Gq = HQ / lay->H;
     // continuation chunks: blocks of up to 128 (query, head) rows with every product on the tensor
@@ -960,4 +996,38 @@ extern "C" int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_ca
     return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ,
                       scale, head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, scratch,
                       size_t(TTKV_NOALLOC_SCRATCH_BYTES), status, stream);
+}
+
+// The head-sharded decode with its outputs gathered over NVLink peer stores in the merge.
+static int check_peers(const ttkv_peers_t* peers) {
+    if (!peers || peers->world < 1 || peers->world > TTKV_MAX_PEERS || peers->rank < 0 ||
+        peers->rank >= peers->world || !peers->epoch)
+        return fail(TTKV_ERR_ARG, "peers: world %d, rank %d", peers ? peers->world : 0, peers ? peers->rank : 0);
+    for (int i = 0; i < peers->world; ++i)
+        if (!peers->out[i] || !peers->signal[i]) return fail(TTKV_ERR_ARG, "peers: rank %d has no out or signal", i);
+    return TTKV_OK;
+}
+
+extern "C" int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
+                                        const ttkv_batch_t* batch, const ttkv_rope_t* rope,
+                                        const void* q, int32_t q_dtype, int64_t q_stride, int32_t HQ,
+                                        float scale, int32_t head_lo, int32_t head_hi, void* out,
+                                        int32_t out_dtype, int64_t out_stride, int32_t max_seq_len,
+                                        void* workspace, size_t workspace_bytes, const ttkv_peers_t* peers,
+                                        int32_t* status, void* stream) {
+    if (int e = check_peers(peers)) return e;
+    if (peers->out[peers->rank] != out) return fail(TTKV_ERR_ARG, "peers: out[rank] is not the call's out");
+    if (batch && batch->n_reqs == 0) return fail(TTKV_ERR_ARG, "a gathered decode of no requests");
+    return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ, scale,
+                      head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, workspace,
+                      workspace_bytes, status, stream, peers);
+}
+
+extern "C" int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals_per_step, int32_t* status,
+                              void* stream) {
+    if (int e = check_peers(peers)) return e;
+    if (arrivals_per_step < 1 || !status) return fail(TTKV_ERR_ARG, "arrivals_per_step %lld", (long long)arrivals_per_step);
+    peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        peers->signal[peers->rank], peers->epoch, (unsigned long long)arrivals_per_step, status);
+    return check_launch("peer_wait_kernel");
 }

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import pathlib
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 LIB_PATH = pathlib.Path(__file__).resolve().parents[1] / "libttkv_sm100.so"
 
 # host-side refusal codes (ttkv_b200.h)
@@ -50,8 +50,19 @@ class Rope(C.Structure):
     _fields_ = [("table", C.c_void_p), ("dtype", C.c_int32), ("rows", C.c_int64)]
 
 
+MAX_PEERS = 8                               # TTKV_MAX_PEERS
+
+
+class Peers(C.Structure):
+    """ttkv_peers_t: the group of a gathered decode (every rank's output and signal word as mapped
+    in this process, and this rank's epoch word)."""
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("out", C.c_void_p * MAX_PEERS),
+                ("signal", C.c_void_p * MAX_PEERS), ("epoch", C.c_void_p)]
+
+
 P, I32, I64, SZ, F = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t, C.c_float
 LP, CP, BP, RP = C.POINTER(Layout), C.POINTER(Cache), C.POINTER(Batch), C.POINTER(Rope)
+PP = C.POINTER(Peers)
 
 # name -> (restype, argtypes); every symbol the header declares
 SIGNATURES = {
@@ -65,6 +76,14 @@ SIGNATURES = {
                                     I32, P, SZ, P, P]),
     "ttkv_decode_paged_noalloc": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P,
                                             I32, I64, I32, P, P]),
+    "ttkv_decode_paged_gather": (C.c_int, [LP, CP, BP, RP, P, I32, I64, I32, F, I32, I32, P, I32,
+                                           I64, I32, P, SZ, PP, P, P]),
+    "ttkv_peer_wait": (C.c_int, [PP, I64, P, P]),
+    "ttkv_ipc_handle_bytes": (SZ, []),
+    "ttkv_ipc_alloc": (C.c_int, [SZ, C.POINTER(C.c_void_p), P]),
+    "ttkv_ipc_open": (C.c_int, [P, C.POINTER(C.c_void_p)]),
+    "ttkv_ipc_close": (C.c_int, [P]),
+    "ttkv_ipc_free": (C.c_int, [P]),
     "ttkv_prefill_workspace_bytes": (SZ, [LP, I32, I32, I32, I32, I32, I32]),
     "ttkv_prefill_cont_paged": (C.c_int, [LP, CP, BP, RP, P, P, P, I32, I64, I32, F, I32, I32,
                                           P, I32, I64, I32, I32, P, SZ, P, P]),
@@ -116,3 +135,9 @@ def lib():
 def check(code: int):
     if code != OK:
         raise TTKVError(code, lib().ttkv_last_error().decode(errors="replace"))
+
+
+def check_with(library, code: int):
+    """`check` against a given library object (the loaded one, or a stand-in in tests)."""
+    if code != OK:
+        raise TTKVError(code, library.ttkv_last_error().decode(errors="replace"))

@@ -207,10 +207,13 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
                  seq_lens: torch.Tensor, decoders: torch.Tensor, dec_index: torch.Tensor,
                  table: torch.Tensor, q: torch.Tensor, scale: float, out: torch.Tensor,
                  max_seq_len: int, head_lo: int = 0, head_hi: int | None = None,
-                 status: torch.Tensor | None = None, images=None) -> torch.Tensor:
+                 status: torch.Tensor | None = None, images=None, peers=None) -> torch.Tensor:
     """Batched decode read: q [B, HQ, d] (row r = request r) -> out [B, HQ, d] (heads of the KV
     heads [head_lo, head_hi) written). `cache` is the [n_slots, row_bytes] uint8 view. `images`:
-    the pool's (image, scales) from `decoder_image`, staged instead of converting the decoders."""
+    the pool's (image, scales) from `decoder_image`, staged instead of converting the decoders.
+    `peers` (a `_lib.Peers` for this layer, see `shard.PeerGather`): the merge also stores the rows
+    into every other rank's `out` and counts its arrivals there (`ttkv_decode_paged_gather`); the
+    caller then waits with `peer_wait` before reading the other ranks' heads."""
     _need_cuda(cache, block_table, seq_lens, decoders, dec_index, table, q, out)
     head_hi = lay.H if head_hi is None else head_hi
     B, HQ, d = q.shape
@@ -225,11 +228,24 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
     c_s = _cache_struct(lay, cache, block_size)
     b_s = _batch_struct(block_table, seq_lens, decoders, dec_index, images)
     r_s = _rope_struct(table)
-    _lib.check(L.ttkv_decode_paged(
-        C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),
-        qs, HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
-        os_, int(max_seq_len), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+    if peers is None:
+        _lib.check(L.ttkv_decode_paged(
+            C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),
+            qs, HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
+            os_, int(max_seq_len), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+    else:
+        _lib.check(L.ttkv_decode_paged_gather(
+            C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q.data_ptr(), dtype_code(q),
+            qs, HQ, float(scale), head_lo, head_hi, out.data_ptr(), dtype_code(out),
+            os_, int(max_seq_len), ws.data_ptr(), ws.numel(), C.byref(peers), st.data_ptr(), _stream()))
     return out
+
+
+def peer_wait(peers, arrivals_per_step: int, status: torch.Tensor | None = None) -> None:
+    """Wait on the device (stream-ordered, bounded) until every rank's merge of this step has
+    stored its rows into this rank's output (`ttkv_peer_wait`)."""
+    st = status if status is not None else status_word()
+    _lib.check(_lib.lib().ttkv_peer_wait(C.byref(peers), int(arrivals_per_step), st.data_ptr(), _stream()))
 
 
 def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,

@@ -7,9 +7,10 @@ coefficient block every head's rows are independent. Rank g of N owns KV heads
   coefficient block and its own heads' rows only, written by `ttkv_write_paged_shard` and read as
   a layout of H/N heads; or
 * holds a replica of the full blobs and reads its heads through `head_lo/head_hi` of the read ABI.
-Either way it writes its query heads [head_lo*G, head_hi*G) of each layer's output, which are
-all-gathered over the process group and reassembled in head order, so every rank ends with the
-whole output.
+Either way it writes its query heads [head_lo*G, head_hi*G) of each layer's output, and every rank
+ends with the whole output: either `PeerGather`, where the decode's merge stores each row into
+every rank's output over NVLink peer memory (no collective per layer), or `HeadShard.read`, an
+all-gather over the process group reassembled in head order.
 
 The write's projection needs every head's K (c = M @ pinv), so every rank projects the step's
 tokens; with the sharded format it packs only its heads. Collectives go through
@@ -17,6 +18,8 @@ tokens; with the sharded format it packs only its heads. Collectives go through
 along dim 0, the form both backends accept.
 """
 from __future__ import annotations
+
+import ctypes as C
 
 import torch
 import torch.distributed as dist
@@ -101,3 +104,126 @@ class HeadShard:
         self.gather(send, recv)
         self.assemble(recv, out)
         return out
+
+
+# ---------------------------------------------------------------------------- fused gather
+def peers_struct(rank: int, outs, signals, epoch: int):
+    """A `_lib.Peers` (ttkv_peers_t) from raw device addresses: every rank's output view and signal
+    word as mapped in this process, and this rank's epoch word."""
+    from vllm_ttkv import _lib
+    world = len(outs)
+    if world != len(signals) or not 1 <= world <= _lib.MAX_PEERS or not 0 <= rank < world:
+        raise ValueError(f"a group of {world} outputs / {len(signals)} signals, rank {rank}")
+    st = _lib.Peers()
+    st.world, st.rank, st.epoch = world, rank, int(epoch)
+    for i, (o, g) in enumerate(zip(outs, signals)):
+        st.out[i], st.signal[i] = int(o), int(g)
+    return st
+
+
+class _DeviceArray:
+    """Library-owned device memory as an int16 array, for a zero-copy `torch.as_tensor`."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2", "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGather:
+    """The all-gather of a KV-head-sharded decode fused into its merge, over NVLink peer memory
+    (`ttkv_decode_paged_gather` + `ttkv_peer_wait`): no NCCL call per layer.
+
+    Every rank allocates, through CUDA IPC (plain peer mappings, no multicast object), one output
+    buffer for all layers [L, B, HQ, d] and one 8-byte signal word per layer, and keeps one epoch
+    word per layer of its own. The handles are exchanged over the process group once and every rank
+    maps the others'. Per layer and step, `ops.decode_paged(..., out=g.local_out(l),
+    peers=g.peers(l))` stores this rank's query heads into every rank's buffer and counts its merge
+    CTAs on every rank's signal word; `g.wait(l)` then waits (on the device, bounded) until this
+    rank's buffer holds every head of the step: `g.out(l)` [B, HQ, d].
+
+    Every rank must run the same layers in the same order each step (the signal counts are
+    cumulative). `lib` and `gather_object` stand in for the library and the collective in tests."""
+
+    def __init__(self, shard: HeadShard, n_layers: int, B: int, d: int, dtype, device,
+                 group=None, lib=None, gather_object=None):
+        from vllm_ttkv import _lib
+        self.shard, self.L, self.B, self.d = shard, int(n_layers), int(B), int(d)
+        self.world, self.rank = shard.world, shard.rank
+        self.device = torch.device(device)
+        self._lib = lib if lib is not None else _lib.lib()
+        self.esz = torch.tensor([], dtype=dtype).element_size()
+        self.layer_bytes = self.B * shard.HQ * self.d * self.esz
+        # every rank's merge CTAs (G x its KV heads x requests) arrive once per step
+        self.arrivals = self.world * shard.G * (shard.head_hi - shard.head_lo) * self.B
+        self._own, self._opened = [], []
+        hb = int(self._lib.ttkv_ipc_handle_bytes())
+
+        def alloc(nbytes):
+            ptr, h = C.c_void_p(), (C.c_char * hb)()
+            _lib.check_with(self._lib, self._lib.ttkv_ipc_alloc(nbytes, C.byref(ptr), h))
+            self._own.append(ptr.value)
+            return ptr.value, bytes(h)
+
+        base, h_out = alloc(self.L * self.layer_bytes)
+        sig, h_sig = alloc(self.L * 8)
+        handles = [None] * self.world
+        if gather_object is None:
+            dist.all_gather_object(handles, (h_out, h_sig), group=group)
+        else:
+            gather_object(handles, (h_out, h_sig))
+        self.bases, self.signals = [], []
+        for p, (ho, hs) in enumerate(handles):
+            if p == self.rank:
+                self.bases.append(base)
+                self.signals.append(sig)
+                continue
+            pair = []
+            for h in (ho, hs):
+                ptr = C.c_void_p()
+                _lib.check_with(self._lib, self._lib.ttkv_ipc_open(h, C.byref(ptr)))
+                self._opened.append(ptr.value)
+                pair.append(ptr.value)
+            self.bases.append(pair[0])
+            self.signals.append(pair[1])
+        self.epoch = torch.zeros(self.L, dtype=torch.int64, device=self.device)
+        self.all_out = None
+        if self.device.type == "cuda":
+            raw = torch.as_tensor(_DeviceArray(base, (self.L, self.B, shard.HQ, self.d)), device=self.device)
+            self.all_out = raw.view(dtype)
+        q_off = shard.q_lo * self.d * self.esz
+        self._peers = [peers_struct(self.rank, [b + l * self.layer_bytes + q_off for b in self.bases],
+                                    [g + 8 * l for g in self.signals], self.epoch.data_ptr() + 8 * l)
+                       for l in range(self.L)]
+
+    def out(self, l: int) -> torch.Tensor:
+        """Layer l's whole output [B, HQ, d] on this rank (every head after `wait(l)`)."""
+        return self.all_out[l]
+
+    def local_out(self, l: int) -> torch.Tensor:
+        """This rank's query heads of layer l's output: the `out` its decode writes."""
+        return self.all_out[l][:, self.shard.q_lo:self.shard.q_hi]
+
+    def peers(self, l: int):
+        return self._peers[l]
+
+    def wait(self, l: int, status=None) -> None:
+        from vllm_ttkv import ops
+        ops.peer_wait(self._peers[l], self.arrivals, status)
+
+    def close(self, group=None, barrier=None) -> None:
+        """Unmap the peers' memory and free this rank's, once every rank is done with it (a group
+        barrier first, or `barrier()` in tests)."""
+        from vllm_ttkv import _lib
+        if not self._own and not self._opened:
+            return
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        (barrier or (lambda: dist.barrier(group)))()
+        for ptr in self._opened:
+            _lib.check_with(self._lib, self._lib.ttkv_ipc_close(ptr))
+        self._opened = []
+        (barrier or (lambda: dist.barrier(group)))()
+        self.all_out = None
+        for ptr in self._own:
+            _lib.check_with(self._lib, self._lib.ttkv_ipc_free(ptr))
+        self._own = []
