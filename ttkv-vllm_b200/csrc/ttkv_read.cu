@@ -1017,7 +1017,9 @@ extern "C" int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cac
                                         int32_t* status, void* stream) {
     if (int e = check_peers(peers)) return e;
     if (peers->out[peers->rank] != out) return fail(TTKV_ERR_ARG, "peers: out[rank] is not the call's out");
-    if (batch && batch->n_reqs == 0) return fail(TTKV_ERR_ARG, "a gathered decode of no requests");
+    // every rank's merge must arrive: a call that would launch nothing is refused instead
+    if ((batch && batch->n_reqs == 0) || max_seq_len == 0)
+        return fail(TTKV_ERR_ARG, "a gathered decode of no requests or rows");
     return read_entry(false, lay, cache, batch, rope, nullptr, nullptr, q, q_dtype, q_stride, HQ, scale,
                       head_lo, head_hi, out, out_dtype, out_stride, 1, max_seq_len, workspace,
                       workspace_bytes, status, stream, peers);
