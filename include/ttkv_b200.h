@@ -212,13 +212,15 @@ int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cach
  *   - out[p] is rank p's `out` pointer (the same view: base, head offset, stride and dtype on every
  *     rank) mapped into this process (ttkv_ipc_open), out[rank] == the `out` argument;
  *   - signal[p] is rank p's signal word for this layer (8 bytes, zeroed once, never reset),
- *     mapped likewise; epoch is this rank's own counter word for the same layer (local, zeroed
- *     once): ttkv_peer_wait(step k) waits for signal >= k * arrivals_per_step;
- *   - arrivals_per_step = world * G * (head_hi - head_lo) * n_reqs (every rank's merge CTAs);
+ *     mapped likewise; epoch is this rank's own word for the same layer (local, zeroed once): the
+ *     arrivals its waits have taken so far. ttkv_peer_wait adds the step's arrivals to it and
+ *     waits until the signal word reaches the sum (so batch sizes may change from step to step);
+ *   - a step's arrivals = world * G * (head_hi - head_lo) * n_reqs (every rank's merge CTAs; every
+ *     rank runs the same requests);
  *   - served by the tensor-core decode only; other layouts are refused (TTKV_ERR_UNSUPPORTED) and
  *     the caller gathers another way. world <= TTKV_MAX_PEERS.
- * The wait is bounded (about 2 s): a rank that never arrives sets TTKV_STATUS_TIMEOUT; the epoch
- * still advances, and the group is then out of step and must be rebuilt. */
+ * The wait is bounded (about 2 s): a rank that never arrives sets TTKV_STATUS_TIMEOUT; the count
+ * waited for still advances, and the group is then out of step and must be rebuilt. */
 #define TTKV_MAX_PEERS 8
 typedef struct {
     int32_t world, rank;
@@ -233,7 +235,7 @@ int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cache_t* cache
                              void* out, int32_t out_dtype, int64_t out_stride,
                              int32_t max_seq_len, void* workspace, size_t workspace_bytes,
                              const ttkv_peers_t* peers, int32_t* status, void* stream);
-int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals_per_step, int32_t* status, void* stream);
+int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals, int32_t* status, void* stream);
 
 /* Device memory shared between the processes of a group through CUDA IPC handles (plain peer
  * mappings, no multicast object): ttkv_ipc_alloc allocates `bytes` (zeroed, on the current

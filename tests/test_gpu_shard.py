@@ -96,7 +96,7 @@ def test_the_gathered_decode_leaves_every_head_on_every_rank():
         ops.check_status()
         for r in range(world):
             assert int(sigs[r][0].item()) == (step + 1) * arrivals
-            assert int(epochs[r][0].item()) == step + 1
+            assert int(epochs[r][0].item()) == (step + 1) * arrivals
             for l in range(L):
                 np.testing.assert_allclose(outs[r][l].float().cpu().numpy(), full.out[l].float().cpu().numpy(),
                                            rtol=1e-2, atol=1e-3, err_msg=f"rank {r} layer {l} step {step}")
@@ -104,7 +104,8 @@ def test_the_gathered_decode_leaves_every_head_on_every_rank():
 
 def test_a_peer_wait_with_no_arrivals_runs_out_and_reports():
     """A signal word nobody counts on: the bounded wait gives up after about two seconds, sets
-    TTKV_STATUS_TIMEOUT and advances its epoch; the device stays usable."""
+    TTKV_STATUS_TIMEOUT and still counts the step's arrivals as waited for; the device stays
+    usable."""
     import time
 
     from vllm_ttkv import _lib, ops
@@ -119,12 +120,12 @@ def test_a_peer_wait_with_no_arrivals_runs_out_and_reports():
     torch.cuda.synchronize()
     assert 0.5 < time.perf_counter() - t0 < 30
     assert int(ops.status_word().item()) == 6          # TTKV_STATUS_TIMEOUT
-    assert int(ep.item()) == 1
+    assert int(ep.item()) == 3
     ops.reset_status()
-    sig.fill_(6)                                       # two steps' arrivals: the next wait passes
-    ops.peer_wait(st, 3)
+    sig.fill_(3 + 5)                                   # the next step of 5 arrivals: the wait passes
+    ops.peer_wait(st, 5)
     torch.cuda.synchronize()
     ops.check_status()
-    assert int(ep.item()) == 2
+    assert int(ep.item()) == 8
     with pytest.raises(_lib.TTKVError):
         ops.peer_wait(peers_struct(0, [out.data_ptr()], [sig.data_ptr()], 0), 3)   # no epoch word

@@ -723,14 +723,14 @@ int launch(const ReadParams& P, const Plan& pl, int n_reqs, cudaStream_t st) {
     return fail(TTKV_ERR_UNSUPPORTED, "GQA group %d", P.G);
 }
 
-// The gathered decode's wait (ttkv_peer_wait): this rank's signal word must reach epoch *
-// arrivals_per_step, every rank's merge CTAs of this step having stored their rows here first
-// (each fenced its stores system-wide before its arrival). One thread polls with an acquire load;
-// the wait is bounded, and the epoch advances either way.
-__global__ void peer_wait_kernel(const unsigned long long* sig, unsigned long long* epoch,
-                                 unsigned long long arrivals_per_step, int32_t* status) {
+// The gathered decode's wait (ttkv_peer_wait): this rank's signal word must reach the arrivals
+// waited for so far plus this step's, every rank's merge CTAs of this step having stored their rows
+// here first (each fenced its stores system-wide before its arrival). One thread polls with an
+// acquire load; the wait is bounded, and the count waited for advances either way.
+__global__ void peer_wait_kernel(const unsigned long long* sig, unsigned long long* waited,
+                                 unsigned long long arrivals, int32_t* status) {
     if (threadIdx.x != 0) return;
-    const unsigned long long ep = *epoch + 1, target = ep * arrivals_per_step;
+    const unsigned long long target = *waited + arrivals;
     const long long t0 = clock64();
     bool ok = true;
     for (;;) {
@@ -740,7 +740,7 @@ __global__ void peer_wait_kernel(const unsigned long long* sig, unsigned long lo
         if (clock64() - t0 > kWaitCycles) { ok = false; break; }
         __nanosleep(128);
     }
-    *epoch = ep;
+    *waited = target;
     if (!ok) report(status, TTKV_STATUS_TIMEOUT);
     __threadfence_system();
 }
@@ -1025,11 +1025,10 @@ extern "C" int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cac
                       workspace_bytes, status, stream, peers);
 }
 
-extern "C" int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals_per_step, int32_t* status,
-                              void* stream) {
+extern "C" int ttkv_peer_wait(const ttkv_peers_t* peers, int64_t arrivals, int32_t* status, void* stream) {
     if (int e = check_peers(peers)) return e;
-    if (arrivals_per_step < 1 || !status) return fail(TTKV_ERR_ARG, "arrivals_per_step %lld", (long long)arrivals_per_step);
+    if (arrivals < 1 || !status) return fail(TTKV_ERR_ARG, "arrivals %lld", (long long)arrivals);
     peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        peers->signal[peers->rank], peers->epoch, (unsigned long long)arrivals_per_step, status);
+        peers->signal[peers->rank], peers->epoch, (unsigned long long)arrivals, status);
     return check_launch("peer_wait_kernel");
 }

@@ -241,11 +241,12 @@ def decode_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int, block_tab
     return out
 
 
-def peer_wait(peers, arrivals_per_step: int, status: torch.Tensor | None = None) -> None:
+def peer_wait(peers, arrivals: int, status: torch.Tensor | None = None) -> None:
     """Wait on the device (stream-ordered, bounded) until every rank's merge of this step has
-    stored its rows into this rank's output (`ttkv_peer_wait`)."""
+    stored its rows into this rank's output (`ttkv_peer_wait`); `arrivals` = world * G * KV heads
+    per rank * requests of the step."""
     st = status if status is not None else status_word()
-    _lib.check(_lib.lib().ttkv_peer_wait(C.byref(peers), int(arrivals_per_step), st.data_ptr(), _stream()))
+    _lib.check(_lib.lib().ttkv_peer_wait(C.byref(peers), int(arrivals), st.data_ptr(), _stream()))
 
 
 def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,

@@ -139,10 +139,12 @@ class PeerGather:
     maps the others'. Per layer and step, `ops.decode_paged(..., out=g.local_out(l),
     peers=g.peers(l))` stores this rank's query heads into every rank's buffer and counts its merge
     CTAs on every rank's signal word; `g.wait(l)` then waits (on the device, bounded) until this
-    rank's buffer holds every head of the step: `g.out(l)` [B, HQ, d].
+    rank's buffer holds every head of the step: `g.out(l)` [B, HQ, d] (the step's requests in its
+    first rows).
 
-    Every rank must run the same layers in the same order each step (the signal counts are
-    cumulative). `lib` and `gather_object` stand in for the library and the collective in tests."""
+    Every rank must run the same layers and requests in the same order each step (the signal
+    counts are cumulative; each rank's epoch word counts the arrivals its waits have taken).
+    `lib` and `gather_object` stand in for the library and the collective in tests."""
 
     def __init__(self, shard: HeadShard, n_layers: int, B: int, d: int, dtype, device,
                  group=None, lib=None, gather_object=None):
@@ -154,7 +156,8 @@ class PeerGather:
         self.esz = torch.tensor([], dtype=dtype).element_size()
         self.layer_bytes = self.B * shard.HQ * self.d * self.esz
         # every rank's merge CTAs (G x its KV heads x requests) arrive once per step
-        self.arrivals = self.world * shard.G * (shard.head_hi - shard.head_lo) * self.B
+        self.per_request = self.world * shard.G * (shard.head_hi - shard.head_lo)
+        self.arrivals = self.per_request * self.B
         self._own, self._opened = [], []
         hb = int(self._lib.ttkv_ipc_handle_bytes())
 
@@ -206,9 +209,12 @@ class PeerGather:
     def peers(self, l: int):
         return self._peers[l]
 
-    def wait(self, l: int, status=None) -> None:
+    def wait(self, l: int, n_reqs: int | None = None, status=None) -> None:
+        """Wait on the device for every rank's rows of layer l; `n_reqs`: the step's request count
+        (every rank's), default the batch the buffers were sized for."""
         from vllm_ttkv import ops
-        ops.peer_wait(self._peers[l], self.arrivals, status)
+        n = self.B if n_reqs is None else int(n_reqs)
+        ops.peer_wait(self._peers[l], self.per_request * n, status)
 
     def close(self, group=None, barrier=None) -> None:
         """Unmap the peers' memory and free this rank's, once every rank is done with it (a group
