@@ -533,6 +533,101 @@ def run_prefill(args):
     print(json.dumps(line))
 
 
+def run_ttft(args):
+    """A first chunk through the plugin: one request of `--prompt-len` tokens over `--layers`
+    calibrated layers (`safe`, block 16, bf16), each layer one `TTKVAttentionImpl.forward` of the
+    whole prompt: the TT-SVD fit and the fitted write of its keys and values, and the attention over
+    its own post-RoPE q/k/v (SDPA, a library call as in the reference), which goes out first on a
+    side stream and runs under the fit. Inputs are copied in from pinned host memory and the outputs
+    back every step. The dense line is the same attention alone (what a dense-cache backend does at
+    prefill besides its cache copy)."""
+    import torch
+
+    from vllm_ttkv import metadata, patch, rope_store
+    from vllm_ttkv import synthetic as S
+    from vllm_ttkv.impl import TTKVAttentionImpl
+    from vllm_ttkv.decode import attend_prefill
+    from vllm_ttkv.layout import layout_for_config
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    P, L, H, HQ, d, bs = args.prompt_len, args.layers, 8, 24, 128, 16
+    r1s = (S.LLAMA32_3B_R1 * ((L + 27) // 28))[:L]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    n_blocks = (P + bs - 1) // bs
+    slots = torch.arange(P, device=device, dtype=torch.int64)
+    bt = torch.arange(n_blocks, device=device, dtype=torch.int32).view(1, -1)
+    table = torch.from_numpy(S.cos_sin_cache(P + 16, dtype="float32")).to(device).to(torch.bfloat16)
+    impl = TTKVAttentionImpl(HQ, d, d ** -0.5, H)
+    layers = []
+    for l in range(L):
+        lay = layout_for_config("safe", r1s[l], H=H)
+        layer = types_ns(layer_name=f"model.layers.{l}.self_attn.attn", ttkv_layout=lay,
+                         rotary_emb=types_ns(cos_sin_cache=table))
+        page = torch.zeros(n_blocks, 1, bs, lay.compressed_bytes_per_token(), dtype=torch.uint8, device=device)
+        layers.append((layer, page))
+    # one set of q, raw K, post-RoPE K and V (every layer fits and stores the same keys: the work
+    # per layer does not depend on the values), copied in every step; the last layer's output
+    # copied back
+    per = P * (HQ + 3 * H) * d
+    K, V = synth_kv_device(gen, H, P, dtype=torch.bfloat16)
+    q = torch.randn(P, HQ, d, generator=gen, device=device).to(torch.bfloat16)
+    kpost = torch.randn(P, H, d, generator=gen, device=device).to(torch.bfloat16)
+    pin_in = torch.cat([q.reshape(-1), K.permute(1, 0, 2).reshape(-1), kpost.reshape(-1),
+                        V.permute(1, 0, 2).reshape(-1)]).cpu().pin_memory()
+    del K, V, q, kpost
+    dev_in = torch.empty_like(pin_in, device=device)
+    out = torch.empty(P, HQ, d, dtype=torch.bfloat16, device=device)
+    pin_o = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def views(l):
+        b = dev_in
+        q = b[:P * HQ * d].view(P, HQ, d)
+        k = b[P * HQ * d:P * (HQ + H) * d].view(P, H, d)
+        kp = b[P * (HQ + H) * d:P * (HQ + 2 * H) * d].view(P, H, d)
+        v = b[P * (HQ + 2 * H) * d:].view(P, H, d)
+        return q, k, kp, v
+
+    qsl_cpu = torch.tensor([0, P], dtype=torch.int32)
+
+    def step():
+        dev_in.copy_(pin_in, non_blocking=True)
+        md = metadata.TTKVAttentionMetadata(
+            seq_lens=torch.tensor([P], dtype=torch.int32, device=device), slot_mapping=slots,
+            block_table=bt, query_start_loc=qsl_cpu.to(device), query_start_loc_cpu=qsl_cpu,
+            num_actual_tokens=P, max_query_len=P, max_seq_len=P, ttkv_serial=metadata.next_serial())
+        for l, (layer, page) in enumerate(layers):
+            q, k, kp, v = views(l)
+            patch.stash_raw_k(layer.layer_name, k, None, table)
+            impl.forward(layer, q, kp, v, page, md, out)
+        pin_o.copy_(out, non_blocking=True)
+
+    def dense_step():
+        for l in range(L):
+            q, k, kp, v = views(l)
+            out.copy_(attend_prefill(q.float(), kp.float(), v.float(), d ** -0.5))
+
+    ms = _event_ms(step, args.steps, args.warmup)
+    dense_ms = _event_ms(dense_step, args.steps, args.warmup)
+    rope_store.clear_decoders()
+    h2d = pin_in.numel() * 2
+    line = {"metric": "first-chunk (prefill) attention + TT-KV fit and write, ms to first token",
+            "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": False, "workload": "ttft",
+            "dtype": "bf16 model tensors, fp32 fit and attention, u8 slots", "data": "synthetic",
+            "config": {"workload": f"1 request x {P} tokens, {L} calibrated layers, safe, block 16, "
+                                   f"through TTKVAttentionImpl.forward (fit + write + SDPA per layer)"},
+            "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": pin_o.numel() * 2},
+            "dense_prefill_attention_ms": dense_ms}
+    print(json.dumps(line))
+
+
+def types_ns(**kw):
+    from types import SimpleNamespace
+    return SimpleNamespace(**kw)
+
+
 def run_encode(args):
     """Config 4, the write path at prefill: requests of `--prompt-len` tokens (16384 for config 4),
     `--layers` layers at the `tight` allocation with r1 = 110: per layer the TT-SVD fit (library
@@ -796,9 +891,10 @@ def main():
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every layer eagerly instead of replaying a CUDA graph per step")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "encode", "sweep", "dense"],
+                    choices=["decode", "prefill", "encode", "sweep", "dense", "ttft"],
                     help="decode: config 1 (the default line); sweep: config 2; prefill: config 3; "
-                         "encode: config 4; dense: the bf16-KV comparator of configs 1 and 2")
+                         "encode: config 4; dense: the bf16-KV comparator of configs 1 and 2; "
+                         "ttft: a first chunk through the plugin (fit + write + attention)")
     ap.add_argument("--sweep-ctx", default="1082,4322,8642,14402", help="sweep: cached tokens")
     ap.add_argument("--sweep-batch", default="1,8,32,64", help="sweep: batch sizes")
     ap.add_argument("--prompt-len", type=int, default=None,
@@ -824,7 +920,7 @@ def main():
             args.prompt_len = 7379 if args.workload == "prefill" else 16384
         if args.steps == 200:                      # the decode default; these steps take seconds
             args.steps = 3
-        (run_prefill if args.workload == "prefill" else run_encode)(args)
+        {"prefill": run_prefill, "encode": run_encode, "ttft": run_ttft}[args.workload](args)
         return
     if args.impl == "reference":
         run_reference(args)

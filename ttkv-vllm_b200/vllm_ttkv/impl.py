@@ -275,14 +275,47 @@ class TTKVAttentionImpl(_ImplBase):
         if N == 0:
             return output
         name = getattr(layer, "layer_name", None)
+        # first chunks attend over their own q/k/v, which the write does not change: their SDPA
+        # goes out first, on a side stream, and runs under the fits (whose rank choice reads back
+        # to the host) and the writes; the step's stream waits for it before returning
+        side = self._first_chunks_aside(plan, query, key, value, output)
         table = self._write(layer, name, lay, cache, value, plan, attn_metadata, query.device)
         if plan.n_dec:
             self._decode(name, lay, cache, plan, attn_metadata, table, query, output)
         if plan.prefills:
-            self._prefill(name, lay, cache, plan, attn_metadata, table, query, key, value, output)
+            self._prefill(name, lay, cache, plan, attn_metadata, table, query, key, value, output,
+                          skip_first=side is not None)
+        if side is not None:
+            torch.cuda.current_stream(query.device).wait_stream(side)
         if _CHECK:
             ops.check_status(query.device)
         return output
+
+    def _first_chunks_aside(self, plan, query, key, value, output):
+        """Launch the first chunks' attention on a side stream (CUDA only); None when there are
+        none, or off CUDA, or under a capture (the side stream is not part of it)."""
+        if not query.is_cuda or ops.capturing():
+            return None
+        firsts = [r for r in plan.prefills if plan.seq_lens[r] == plan.qsl[r + 1] - plan.qsl[r]]
+        if not firsts:
+            return None
+        cur = torch.cuda.current_stream(query.device)
+        side = torch.cuda.Stream(device=query.device)
+        side.wait_stream(cur)                       # q/k/v are the step stream's
+        with torch.cuda.stream(side):
+            self._attend_first_chunks(firsts, plan, query, key, value, output)
+        for t in (query, key, value, output):       # used on the side stream
+            if t is not None:
+                t.record_stream(side)
+        return side
+
+    def _attend_first_chunks(self, firsts, plan, query, key, value, output):
+        for r in firsts:
+            s, e = plan.qsl[r], plan.qsl[r + 1]
+            k = encode.as_kv_heads(key, self.num_kv_heads, self.head_size, "key")[s:e].float()
+            v = encode.as_kv_heads(value, self.num_kv_heads, self.head_size, "value")[s:e].float()
+            out = dc.attend_prefill(query[s:e].float(), k, v, self.scale)
+            output[s:e] = out.to(output.dtype)
 
     # ------------------------------------------------------------------ a device-planned decode step
     def _decode_step(self, layer, lay, cache, plan, md, query, value, output, capturing):
@@ -376,7 +409,7 @@ class TTKVAttentionImpl(_ImplBase):
                          pool.decoders, plan.dec_rows(query.device), self._device_table(table, query),
                          query[:n], self.scale, output[:n], max(plan.seq_lens[:n]), images=pool.images)
 
-    def _prefill(self, name, lay, cache, plan, md, table, query, key, value, output):
+    def _prefill(self, name, lay, cache, plan, md, table, query, key, value, output, skip_first=False):
         cont = []
         for r in plan.prefills:
             s, e = plan.qsl[r], plan.qsl[r + 1]
@@ -385,10 +418,8 @@ class TTKVAttentionImpl(_ImplBase):
                     f"request {r} has seq_len={plan.seq_lens[r]} but {e - s} query tokens: the slot "
                     f"mapping and the sequence length disagree")
             if plan.seq_lens[r] == e - s:          # first chunk: its own post-RoPE q/k/v
-                k = encode.as_kv_heads(key, self.num_kv_heads, self.head_size, "key")[s:e].float()
-                v = encode.as_kv_heads(value, self.num_kv_heads, self.head_size, "value")[s:e].float()
-                out = dc.attend_prefill(query[s:e].float(), k, v, self.scale)
-                output[s:e] = out.to(output.dtype)
+                if not skip_first:                 # (else already attended on the side stream)
+                    self._attend_first_chunks([r], plan, query, key, value, output)
             else:
                 cont.append(r)
         if not cont:
