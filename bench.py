@@ -1056,6 +1056,8 @@ def main():
             a.record()
             wl.read(l)
             b.record()
+            if pg is not None:
+                pg.wait(l)                 # (after the event) keeps the arrival counts in step
     torch.cuda.synchronize(device)
     dec_ms = [a.elapsed_time(b) for a, b in evs]
     dec_total_ms = sum(dec_ms) / reps                          # all layers' decode launches, per step

@@ -1238,11 +1238,13 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
                                       int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
     }
     if (P.n_peers > 0) {
-        // every thread's stores reach the peers before this CTA's arrival on their signal words
-        __threadfence_system();
+        // one arrival per CTA on every rank's signal word, after the barrier: a system-scope
+        // release reduction, which orders the CTA's row stores (seen through the barrier) before
+        // it; no reply is awaited
         __syncthreads();
         if (lane == 0)
-            for (int p = 0; p < P.n_peers; ++p) atomicAdd_system(P.peer_sig[p], 1ull);
+            for (int p = 0; p < P.n_peers; ++p)
+                asm volatile("red.release.sys.global.add.u64 [%0], %1;" :: "l"(P.peer_sig[p]), "l"(1ull) : "memory");
     }
 }
 
