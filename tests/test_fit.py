@@ -14,7 +14,8 @@ def _recon(G1, G2, G3):
     return G1 @ torch.einsum("rdq,qh->rdh", G2, G3).reshape(r, -1)
 
 
-@pytest.mark.parametrize("n,cap", [(3000, 110), (5000, 143), (2100, 14)])
+@pytest.mark.parametrize("n,cap", [(3000, 110), (5000, 143), (2100, 14), (1082, 110), (600, 110),
+                                   (256, 67)])
 def test_gram_fit_matches_the_svd_fit(n, cap):
     K = torch.from_numpy(S.synth_kv(7, n)[0])
     H, _, d = K.shape
@@ -48,7 +49,8 @@ def test_gram_fit_of_low_rank_and_zero_keys():
 
 def test_fit_method_selection(monkeypatch):
     monkeypatch.delenv(encode.FIT_ENV, raising=False)
-    assert encode.fit_method(4096, 1024) == "gram" and encode.fit_method(1000, 1024) == "svd"
+    assert encode.fit_method(4096, 1024) == "gram" and encode.fit_method(1082, 1024) == "gram"
+    assert encode.fit_method(encode.GRAM_MIN_TOKENS - 1, 1024) == "svd"
     monkeypatch.setenv(encode.FIT_ENV, "svd")
     assert encode.fit_method(16384, 1024) == "svd"
     monkeypatch.setenv(encode.FIT_ENV, "bogus")
