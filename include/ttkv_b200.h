@@ -205,8 +205,9 @@ int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_cache_t* cach
  * decode's outputs, fused into the decode's segment merge. Every rank of a group of `world`
  * processes (one per GPU) reads its KV heads [head_lo, head_hi) and holds the layer's whole output
  * [n_reqs, HQ, d]; the merge stores each output row into its own `out` AND, at the same byte
- * offset, into every other rank's (peer stores over NVLink), then counts one arrival per merge
- * CTA on every rank's signal word. ttkv_peer_wait then waits until the local signal word has
+ * offset, into every other rank's (peer stores over NVLink); each merge CTA then counts itself on
+ * a local ticket word (a GPU-scope release), and the launch's last CTA posts one arrival per merge
+ * CTA of the launch to every rank's signal word (system-scope releases, one per rank). ttkv_peer_wait then waits until the local signal word has
  * seen every rank's arrivals for this step, after which `out` holds every head. What it replaces:
  * the copy of a rank's heads into a send buffer, the NCCL all-gather and the copy back.
  *   - out[p] is rank p's `out` pointer (the same view: base, head offset, stride and dtype on every
@@ -227,6 +228,10 @@ typedef struct {
     void* out[TTKV_MAX_PEERS];
     unsigned long long* signal[TTKV_MAX_PEERS];
     unsigned long long* epoch;
+    unsigned long long* ticket;   /* this rank's own word for the layer (local, zeroed once): its
+                                     merge CTAs count themselves here, and the last of each launch
+                                     posts the launch's arrivals to every rank's signal word and
+                                     sets it back to zero */
 } ttkv_peers_t;
 int ttkv_decode_paged_gather(const ttkv_layout_t* lay, const ttkv_cache_t* cache,
                              const ttkv_batch_t* batch, const ttkv_rope_t* rope,

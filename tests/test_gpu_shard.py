@@ -74,6 +74,7 @@ def test_the_gathered_decode_leaves_every_head_on_every_rank():
     outs = [torch.full((L, B, HQ, d), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
     sigs = [torch.zeros(L, dtype=torch.int64, device="cuda") for _ in range(world)]
     epochs = [torch.zeros(L, dtype=torch.int64, device="cuda") for _ in range(world)]
+    tickets = [torch.zeros(L, dtype=torch.int64, device="cuda") for _ in range(world)]
     arrivals = world * G * (full.H // world) * B
     ops.reset_status()
     for step in range(2):
@@ -83,7 +84,8 @@ def test_the_gathered_decode_leaves_every_head_on_every_rank():
             for r, wl in enumerate(ranks):
                 lo, hi = head_range(r, world, wl.H)
                 st = peers_struct(r, [o[l].data_ptr() + lo * G * d * 2 for o in outs],
-                                  [g.data_ptr() + 8 * l for g in sigs], epochs[r].data_ptr() + 8 * l)
+                                  [g.data_ptr() + 8 * l for g in sigs], epochs[r].data_ptr() + 8 * l,
+                                  tickets[r].data_ptr() + 8 * l)
                 structs.append(st)
                 wl.write(l)
                 ops.decode_paged(wl.read_layouts[l], wl.caches[l], wl.bs, wl.block_table, wl.seq_lens,
@@ -97,6 +99,7 @@ def test_the_gathered_decode_leaves_every_head_on_every_rank():
         for r in range(world):
             assert int(sigs[r][0].item()) == (step + 1) * arrivals
             assert int(epochs[r][0].item()) == (step + 1) * arrivals
+            assert int(tickets[r].abs().sum().item()) == 0              # every launch's last CTA reset it
             for l in range(L):
                 np.testing.assert_allclose(outs[r][l].float().cpu().numpy(), full.out[l].float().cpu().numpy(),
                                            rtol=1e-2, atol=1e-3, err_msg=f"rank {r} layer {l} step {step}")
@@ -113,7 +116,8 @@ def test_a_peer_wait_with_no_arrivals_runs_out_and_reports():
     out = torch.zeros(1, 8, 128, dtype=torch.bfloat16, device="cuda")
     sig = torch.zeros(1, dtype=torch.int64, device="cuda")
     ep = torch.zeros(1, dtype=torch.int64, device="cuda")
-    st = peers_struct(0, [out.data_ptr()], [sig.data_ptr()], ep.data_ptr())
+    tk = torch.zeros(1, dtype=torch.int64, device="cuda")
+    st = peers_struct(0, [out.data_ptr()], [sig.data_ptr()], ep.data_ptr(), tk.data_ptr())
     ops.reset_status()
     t0 = time.perf_counter()
     ops.peer_wait(st, 3)
@@ -128,4 +132,4 @@ def test_a_peer_wait_with_no_arrivals_runs_out_and_reports():
     ops.check_status()
     assert int(ep.item()) == 8
     with pytest.raises(_lib.TTKVError):
-        ops.peer_wait(peers_struct(0, [out.data_ptr()], [sig.data_ptr()], 0), 3)   # no epoch word
+        ops.peer_wait(peers_struct(0, [out.data_ptr()], [sig.data_ptr()], 0, tk.data_ptr()), 3)   # no epoch word

@@ -136,6 +136,7 @@ def _rank_peer_tables(rank, world, port):
             st = g.peers(l)
             assert (st.world, st.rank) == (world, rank)
             assert st.epoch == g.epoch.data_ptr() + 8 * l
+            assert st.ticket == g.ticket.data_ptr() + 8 * l
             for p in range(world):
                 base = g.bases[p]
                 assert st.out[p] == base + l * layer + sh.q_lo * d * 2       # this rank's head view

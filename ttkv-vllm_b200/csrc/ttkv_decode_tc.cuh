@@ -1238,13 +1238,21 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
                                       int64_t((P.head_lo + hl) * P.g_real + gh) * 128 + lane, v);
     }
     if (P.n_peers > 0) {
-        // one arrival per CTA on every rank's signal word, after the barrier: a system-scope
-        // release reduction, which orders the CTA's row stores (seen through the barrier) before
-        // it; no reply is awaited
+        // the CTA counts itself on the local ticket (a GPU-scope acquire-release add, ordered after
+        // the CTA's row stores, which the barrier makes this thread's); the launch's last CTA, which
+        // has acquired every other CTA's count and with it their stores, posts the launch's arrivals
+        // to every rank's signal word with one system-scope release reduction per rank
         __syncthreads();
-        if (lane == 0)
-            for (int p = 0; p < P.n_peers; ++p)
-                asm volatile("red.release.sys.global.add.u64 [%0], %1;" :: "l"(P.peer_sig[p]), "l"(1ull) : "memory");
+        if (lane == 0) {
+            const unsigned long long n = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+            unsigned long long t;
+            asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(t) : "l"(P.peer_ticket), "l"(1ull) : "memory");
+            if (t + 1 == n) {                                  // the last: reset for the next launch
+                for (int p = 0; p < P.n_peers; ++p)
+                    asm volatile("red.release.sys.global.add.u64 [%0], %1;" :: "l"(P.peer_sig[p]), "l"(n) : "memory");
+                asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(P.peer_ticket), "l"(0ull) : "memory");
+            }
+        }
     }
 }
 

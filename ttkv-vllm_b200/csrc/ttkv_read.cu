@@ -89,6 +89,8 @@ struct ReadParams {
     int n_peers, peer_rank;
     void* peer_out[TTKV_MAX_PEERS];
     unsigned long long* peer_sig[TTKV_MAX_PEERS];
+    unsigned long long* peer_ticket;  // this rank's ticket word: the merge CTAs of a launch count
+                                      // here; the last posts the launch's arrivals to every rank
 };
 
 struct Smem {
@@ -832,6 +834,7 @@ static int read_entry(bool multi, const ttkv_layout_t* lay, const ttkv_cache_t* 
             return fail(TTKV_ERR_UNSUPPORTED, "the gathered decode needs the tensor-core decode (r1=%d)", lay->r1);
         P.n_peers = peers->world;
         P.peer_rank = peers->rank;
+        P.peer_ticket = peers->ticket;
         for (int i = 0; i < peers->world; ++i) { P.peer_out[i] = peers->out[i]; P.peer_sig[i] = peers->signal[i]; }
     }
     const int Gq = HQ / lay->H;
@@ -1001,7 +1004,7 @@ extern "C" int ttkv_decode_paged_noalloc(const ttkv_layout_t* lay, const ttkv_ca
 // The head-sharded decode with its outputs gathered over NVLink peer stores in the merge.
 static int check_peers(const ttkv_peers_t* peers) {
     if (!peers || peers->world < 1 || peers->world > TTKV_MAX_PEERS || peers->rank < 0 ||
-        peers->rank >= peers->world || !peers->epoch)
+        peers->rank >= peers->world || !peers->epoch || !peers->ticket)
         return fail(TTKV_ERR_ARG, "peers: world %d, rank %d", peers ? peers->world : 0, peers ? peers->rank : 0);
     for (int i = 0; i < peers->world; ++i)
         if (!peers->out[i] || !peers->signal[i]) return fail(TTKV_ERR_ARG, "peers: rank %d has no out or signal", i);

@@ -57,7 +57,7 @@ class Peers(C.Structure):
     """ttkv_peers_t: the group of a gathered decode (every rank's output and signal word as mapped
     in this process, and this rank's epoch word)."""
     _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("out", C.c_void_p * MAX_PEERS),
-                ("signal", C.c_void_p * MAX_PEERS), ("epoch", C.c_void_p)]
+                ("signal", C.c_void_p * MAX_PEERS), ("epoch", C.c_void_p), ("ticket", C.c_void_p)]
 
 
 P, I32, I64, SZ, F = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t, C.c_float

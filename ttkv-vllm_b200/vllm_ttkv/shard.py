@@ -107,15 +107,15 @@ class HeadShard:
 
 
 # ---------------------------------------------------------------------------- fused gather
-def peers_struct(rank: int, outs, signals, epoch: int):
+def peers_struct(rank: int, outs, signals, epoch: int, ticket: int):
     """A `_lib.Peers` (ttkv_peers_t) from raw device addresses: every rank's output view and signal
-    word as mapped in this process, and this rank's epoch word."""
+    word as mapped in this process, and this rank's epoch and ticket words."""
     from vllm_ttkv import _lib
     world = len(outs)
     if world != len(signals) or not 1 <= world <= _lib.MAX_PEERS or not 0 <= rank < world:
         raise ValueError(f"a group of {world} outputs / {len(signals)} signals, rank {rank}")
     st = _lib.Peers()
-    st.world, st.rank, st.epoch = world, rank, int(epoch)
+    st.world, st.rank, st.epoch, st.ticket = world, rank, int(epoch), int(ticket)
     for i, (o, g) in enumerate(zip(outs, signals)):
         st.out[i], st.signal[i] = int(o), int(g)
     return st
@@ -188,14 +188,17 @@ class PeerGather:
                 pair.append(ptr.value)
             self.bases.append(pair[0])
             self.signals.append(pair[1])
+        # per layer: the arrivals this rank's waits have taken, and its merge CTAs' ticket
         self.epoch = torch.zeros(self.L, dtype=torch.int64, device=self.device)
+        self.ticket = torch.zeros(self.L, dtype=torch.int64, device=self.device)
         self.all_out = None
         if self.device.type == "cuda":
             raw = torch.as_tensor(_DeviceArray(base, (self.L, self.B, shard.HQ, self.d)), device=self.device)
             self.all_out = raw.view(dtype)
         q_off = shard.q_lo * self.d * self.esz
         self._peers = [peers_struct(self.rank, [b + l * self.layer_bytes + q_off for b in self.bases],
-                                    [g + 8 * l for g in self.signals], self.epoch.data_ptr() + 8 * l)
+                                    [g + 8 * l for g in self.signals], self.epoch.data_ptr() + 8 * l,
+                                    self.ticket.data_ptr() + 8 * l)
                        for l in range(self.L)]
 
     def out(self, l: int) -> torch.Tensor:
