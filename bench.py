@@ -1051,6 +1051,10 @@ def main():
            for _ in range(wl.L * reps)]
     torch.cuda.synchronize(device)
     for rep in range(reps):
+        # a few ms of device sleep first, so that the host has queued every launch of the rep
+        # before the device reaches them: the events then time the device, not the host's
+        # launch overhead (which exceeds a short read's device time at 4 and 8 GPUs)
+        torch.cuda._sleep(int(2e7))
         for l in range(wl.L):
             a, b = evs[rep * wl.L + l]
             a.record()
