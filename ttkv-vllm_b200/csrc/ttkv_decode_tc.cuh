@@ -1206,21 +1206,31 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
         const long long U = before * nh + (long long)hl * nt;
         const long long c0 = ((U + 1) * n - 1) / T, c1 = ((U + nt) * n - 1) / T;
         const long long p = (long long)r * nh + hl;
-        // a CTA whose share is empty (fewer units than CTAs) wrote nothing
+        // a CTA whose share is empty (fewer units than CTAs) wrote nothing; with at least as many
+        // units as shares no share is empty, and the two 64-bit divisions per share are skipped
+        const bool some_empty = T < n;
         auto empty = [&](long long c) { return c * T / n == (c + 1) * T / n; };
-        float M = -INFINITY;
-        for (long long c = c0; c <= c1; ++c)
-            if (!empty(c)) M = fmaxf(M, P.part_ml[((c + p) * P.G + g) * 2]);
-        float acc = 0.f, den = 0.f;
-        if (M != -INFINITY) {
-            for (long long c = c0; c <= c1; ++c) {
-                if (empty(c)) continue;
-                const long long row = (c + p) * P.G + g;
-                const float ms = P.part_ml[row * 2];
-                if (ms == -INFINITY) continue;
-                const float w = expf(ms - M);
-                acc = fmaf(w, P.part_o[row * 128 + lane], acc);
-                den = fmaf(w, P.part_ml[row * 2 + 1], den);
+        // one pass, four shares' loads in flight at a time, the running max rescaling the sums
+        float M = -INFINITY, acc = 0.f, den = 0.f;
+        for (long long c = c0; c <= c1; c += 4) {
+            float ms[4], ls[4], os[4];
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const long long cc = c + k;
+                const bool ok = cc <= c1 && !(some_empty && empty(cc));
+                const long long row = (min(cc, c1) + p) * P.G + g;
+                ms[k] = ok ? P.part_ml[row * 2] : -INFINITY;
+                ls[k] = ok ? P.part_ml[row * 2 + 1] : 0.f;
+                os[k] = ok ? P.part_o[row * 128 + lane] : 0.f;
+            }
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (ms[k] == -INFINITY) continue;
+                const float Mn = fmaxf(M, ms[k]);
+                const float a = expf(M - Mn), b = expf(ms[k] - Mn);   // a = 0 while M is -inf
+                acc = fmaf(acc, a, b * os[k]);
+                den = fmaf(den, a, b * ls[k]);
+                M = Mn;
             }
         }
         v = den > 0.f ? acc / den : 0.f;
