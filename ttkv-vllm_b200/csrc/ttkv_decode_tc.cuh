@@ -1210,12 +1210,13 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
         // units as shares no share is empty, and the two 64-bit divisions per share are skipped
         const bool some_empty = T < n;
         auto empty = [&](long long c) { return c * T / n == (c + 1) * T / n; };
-        // one pass, four shares' loads in flight at a time, the running max rescaling the sums
+        // one pass, eight shares' loads in flight at a time, the running max rescaling the sums
+        constexpr int NF = 8;
         float M = -INFINITY, acc = 0.f, den = 0.f;
-        for (long long c = c0; c <= c1; c += 4) {
-            float ms[4], ls[4], os[4];
+        for (long long c = c0; c <= c1; c += NF) {
+            float ms[NF], ls[NF], os[NF];
             #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < NF; ++k) {
                 const long long cc = c + k;
                 const bool ok = cc <= c1 && !(some_empty && empty(cc));
                 const long long row = (min(cc, c1) + p) * P.G + g;
@@ -1224,7 +1225,7 @@ __global__ void __launch_bounds__(128) merge_sk_kernel(const ReadParams P) {
                 os[k] = ok ? P.part_o[row * 128 + lane] : 0.f;
             }
             #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < NF; ++k) {
                 if (ms[k] == -INFINITY) continue;
                 const float Mn = fmaxf(M, ms[k]);
                 const float a = expf(M - Mn), b = expf(ms[k] - Mn);   // a = 0 while M is -inf
