@@ -59,6 +59,7 @@ except Exception:                      # pragma: no cover
 
 _CHECK = os.environ.get("VLLM_TTKV_CHECK", "") not in ("", "0")
 _DEVICE_PLAN = os.environ.get("VLLM_TTKV_DEVICE_PLAN", "") not in ("", "0")
+_SIDE_STREAMS: dict = {}        # device -> the stream first chunks' attention runs on
 _PLAN_ATTR = "_ttkv_plan"
 
 
@@ -300,7 +301,9 @@ class TTKVAttentionImpl(_ImplBase):
         if not firsts:
             return None
         cur = torch.cuda.current_stream(query.device)
-        side = torch.cuda.Stream(device=query.device)
+        side = _SIDE_STREAMS.get(query.device)
+        if side is None:                            # one per device, made once
+            side = _SIDE_STREAMS[query.device] = torch.cuda.Stream(device=query.device)
         side.wait_stream(cur)                       # q/k/v are the step stream's
         with torch.cuda.stream(side):
             self._attend_first_chunks(firsts, plan, query, key, value, output)
