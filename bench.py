@@ -961,14 +961,32 @@ def main():
     setup_s = time.perf_counter() - t0
 
     pg = None
+    gather_note = None
     if sh is not None and args.gather == "p2p":
         # the layer outputs live in memory every rank maps (CUDA IPC); the decode's merge stores
-        # each row into every rank's copy and the step waits on the device for the others' rows
+        # each row into every rank's copy and the step waits on the device for the others' rows.
+        # Every rank must agree that its mappings worked; if any failed, all take the NCCL path
         from vllm_ttkv.shard import PeerGather
-        pg = PeerGather(sh, wl.L, wl.B, 128, wl.dtype, device)
-        wl.outbuf = pg.all_out.reshape(-1)
-        wl.out = [pg.out(l) for l in range(wl.L)]
-        wl.peers = [pg.peers(l) for l in range(wl.L)]
+        err = None
+        try:
+            pg = PeerGather(sh, wl.L, wl.B, 128, wl.dtype, device)
+        except Exception as e:                              # noqa: BLE001 (reported in the line)
+            err = f"{type(e).__name__}: {e}"
+        ok = torch.tensor([0 if err else 1], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 1:
+            wl.outbuf = pg.all_out.reshape(-1)
+            wl.out = [pg.out(l) for l in range(wl.L)]
+            wl.peers = [pg.peers(l) for l in range(wl.L)]
+        else:
+            if pg is not None:
+                pg.close()                                  # two group barriers inside
+                pg = None
+            else:
+                dist.barrier()                              # the same two as the others' close()
+                dist.barrier()
+            gather_note = "p2p set-up failed on a rank (%s); gathered by NCCL" % (err or "another rank")
+            print(f"rank {rank}: {gather_note}", file=sys.stderr)
     bufs = [sh.buffers(wl.B, 128, wl.dtype, device) for _ in range(wl.L)] if sh else None
 
     def layer_work(l):
@@ -1155,9 +1173,9 @@ def main():
                            "launch": ("eager" if not graphs else "one CUDA graph per step" if sh is None
                                       else "one CUDA graph per step, the 28 all-gathers captured in it"
                                       if pg is None else "one CUDA graph per step, no collective in it"),
-                           "gather": (None if sh is None else "nccl all_gather_into_tensor per layer"
-                                      if pg is None else "fused into the decode's merge: NVLink peer "
-                                      "stores into every rank's output + a device wait on signal words "
+                           "gather": (None if sh is None else (gather_note or "nccl all_gather_into_tensor "
+                                      "per layer") if pg is None else "fused into the decode's merge: NVLink "
+                                      "peer stores into every rank's output + a device wait on signal words "
                                       "(CUDA IPC memory, no multicast)"),
                            "gather_check": gather_check},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
