@@ -153,3 +153,18 @@ def test_peer_gather_maps_every_ranks_output_and_signal_words():
     layers and one for the signal words, the handles exchanged, every other rank's memory mapped,
     and per layer a ttkv_peers_t whose out[p] is rank p's output at this rank's head offset."""
     mp.spawn(_rank_peer_tables, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def test_peers_struct_refuses_mismatched_or_oversized_groups():
+    from vllm_ttkv import _lib
+    from vllm_ttkv.shard import peers_struct
+    st = peers_struct(1, [0x1000, 0x2000], [0x3000, 0x4000], 0x5000, 0x6000)
+    assert (st.world, st.rank, st.epoch, st.ticket) == (2, 1, 0x5000, 0x6000)
+    assert list(st.out)[:2] == [0x1000, 0x2000] and list(st.signal)[:2] == [0x3000, 0x4000]
+    with pytest.raises(ValueError):
+        peers_struct(0, [1, 2], [3], 4, 5)                          # one signal for two outputs
+    with pytest.raises(ValueError):
+        peers_struct(2, [1, 2], [3, 4], 5, 6)                       # rank outside the group
+    n = _lib.MAX_PEERS + 1
+    with pytest.raises(ValueError):
+        peers_struct(0, list(range(1, n + 1)), list(range(1, n + 1)), 1, 1)
