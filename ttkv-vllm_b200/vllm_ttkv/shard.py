@@ -134,8 +134,8 @@ class PeerGather:
     (`ttkv_decode_paged_gather` + `ttkv_peer_wait`): no NCCL call per layer.
 
     Every rank allocates, through CUDA IPC (plain peer mappings, no multicast object), one output
-    buffer for all layers [L, B, HQ, d] and one 8-byte signal word per layer, and keeps one epoch
-    word per layer of its own. The handles are exchanged over the process group once and every rank
+    buffer for all layers [L, B, HQ, d] (a 16- or 32-bit dtype) and one 8-byte signal word per
+    layer, and keeps an epoch word and a ticket word per layer of its own. The handles are exchanged over the process group once and every rank
     maps the others'. Per layer and step, `ops.decode_paged(..., out=g.local_out(l),
     peers=g.peers(l))` stores this rank's query heads into every rank's buffer and counts its merge
     CTAs on every rank's signal word; `g.wait(l)` then waits (on the device, bounded) until this
@@ -193,8 +193,9 @@ class PeerGather:
         self.ticket = torch.zeros(self.L, dtype=torch.int64, device=self.device)
         self.all_out = None
         if self.device.type == "cuda":
-            raw = torch.as_tensor(_DeviceArray(base, (self.L, self.B, shard.HQ, self.d)), device=self.device)
-            self.all_out = raw.view(dtype)
+            raw = torch.as_tensor(_DeviceArray(base, (self.L, self.B, shard.HQ, self.d * self.esz // 2)),
+                                  device=self.device)
+            self.all_out = raw.view(dtype)                    # [L, B, HQ, d] of `dtype`
         q_off = shard.q_lo * self.d * self.esz
         self._peers = [peers_struct(self.rank, [b + l * self.layer_bytes + q_off for b in self.bases],
                                     [g + 8 * l for g in self.signals], self.epoch.data_ptr() + 8 * l,
