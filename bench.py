@@ -45,7 +45,7 @@ METRIC = "decode step ms & tok/s (3B shape, bs1-64, 1k-16k ctx) + HBM GB/s vs pe
 # capture. The per-launch `traffic` of the roofline scales it by algorithmic bytes (the kernel reads
 # each slot byte once, so traffic grows in proportion to the rows and widths a launch reads); when
 # the sources no longer hash the same, the capture describes another kernel and `traffic` is null.
-CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 37326592, "src_sha16": "ad9c423d57b2557f",
+CAPTURED_LAUNCH = {"layer": 9, "dram_bytes": 37336320, "src_sha16": "9a6dec30c44e4a5e",
                    "kernel": "decode_tc_kernel<3, bf16 table>"}
 READ_SOURCES = ("ttkv-vllm_b200/csrc/ttkv_read.cu", "ttkv-vllm_b200/csrc/ttkv_decode_tc.cuh")
 

@@ -574,7 +574,11 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
     while (unit < M->sched_hi && !timed_out) {
         // ---- the next segment: the run of this CTA's units that belongs to one (request, KV head)
         if (r >= P.n_reqs) break;                                   // unreachable: hi <= T
+        // the segment's two scalar loads go out together (a continuation launch's request r is a
+        // block of queries of stored request rq)
         const int seq = P.seq_lens[r];
+        const int rq = P.v_req ? P.v_req[r] : r;
+        const int di = P.dec_index[rq];
         const int nt = req_tiles(seq);
         const int64_t rs = before * nh, re = rs + int64_t(nt) * nh;
         if (unit >= re) { before += nt; ++r; continue; }        // past this request (or it has no rows)
@@ -591,9 +595,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const int h = P.head_lo + hl;
 
         // ---- the cheap refusals (uniform); the block ids are checked as the set-up loads them
-        // a continuation launch's request r is a block of queries of stored request rq
-        const int rq = P.v_req ? P.v_req[r] : r;
-        const int di = P.dec_index[rq];
         bool bad = false;
         if (seq > P.max_seq) { if (tid == 0) report(P.status, TTKV_STATUS_SEQ_BOUND); bad = true; }
         if (!bad && (di < 0 || di >= P.n_decoders)) { if (tid == 0) report(P.status, TTKV_STATUS_DECODER); bad = true; }
@@ -677,25 +678,43 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
         const int nchunk = T.kp16 / 8;
         int local_bad = 0;
         if (!bad) {
+            // one pass with every load issued before any is used: this thread's block id of the
+            // segment (nblk <= BT_CAP = NTHR), the block of its token of the first two tiles (for
+            // their slot-row tables), and its query values (G * 128 <= 2 NTHR)
+            static_assert(BT_CAP <= NTHR && kMaxG * 128 <= 2 * NTHR, "one pass of the set-up");
             const int nblk = (t_end - 1) / P.block_size - blk0 + 1;        // <= BT_CAP (checked above)
             const int64_t n_blocks = P.n_slots / P.block_size;
-            for (int i = tid; i < nblk; i += NTHR) {
-                const int32_t blk = brow[blk0 + i];
-                if (blk < 0 || blk >= n_blocks) local_bad = 1;
-            }
-            for (int i = tid; i < G * 128; i += NTHR) {
+            const int32_t blk = tid < nblk ? brow[blk0 + tid] : 0;
+            const int ft = tid >> 7, fu = tid & 127;
+            const bool frow = tid < 2 * TM && fu < ntok(ft);            // ntok is 0 past the last tile
+            const int ftok = t_begin + ft * TM + fu;
+            const uint32_t fb = frow ? uint32_t((uint64_t(uint32_t(ftok)) * mul_bs) >> 32) : 0u;
+            const int32_t fblk = frow ? brow[fb] : 0;
+            float qv[2];
+            int qi[2];
+            #pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int i = tid + k * NTHR;
                 const int g = i >> 7, j = i & 127;
-                const int qi = (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1);
-                float qv = 0.f;
-                if (!P.v_req) {
-                    qv = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
-                } else if (g < P.v_nq[r]) {              // row g = (query jq, head gh) of the block
-                    const int f = P.v_f0[r] + g, jq = f / P.g_real, gh = f - jq * P.g_real;
-                    qv = load_elt(P.q, P.q_dtype, int64_t(P.v_qrow[r] + jq) * P.q_stride +
-                                                  int64_t(h * P.g_real + gh) * 128 + j);
+                qi[k] = i < G * 128 ? (g * 32 + ((j & 63) >> 1)) * 4 + (j >= 64 ? 2 : 0) + (j & 1) : -1;
+                qv[k] = 0.f;
+                if (i < G * 128) {
+                    if (!P.v_req) {
+                        qv[k] = load_elt(P.q, P.q_dtype, int64_t(r) * P.q_stride + int64_t(h * G + g) * 128 + j);
+                    } else if (g < P.v_nq[r]) {          // row g = (query jq, head gh) of the block
+                        const int f = P.v_f0[r] + g, jq = f / P.g_real, gh = f - jq * P.g_real;
+                        qv[k] = load_elt(P.q, P.q_dtype, int64_t(P.v_qrow[r] + jq) * P.q_stride +
+                                                         int64_t(h * P.g_real + gh) * 128 + j);
+                    }
                 }
-                qs[qi] = qv;
             }
+            if (tid < nblk && (blk < 0 || blk >= n_blocks)) local_bad = 1;
+            // the first two tiles' slot rows (a bad block id makes the segment skipped: unused)
+            if (tid < 2 * TM)
+                trs[(ft & 1) * TM + fu] = frow ? (int64_t(fblk) * P.block_size + int64_t(uint32_t(ftok) - fb * bsz)) * P.row_bytes : 0;
+            #pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if (qi[k] >= 0) qs[qi[k]] = qv[k];
         }
         if (tid < kMaxG) {
             M->m[tid] = -INFINITY;
@@ -705,7 +724,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             if (P.v_req) lim = tid < P.v_nq[r] ? P.v_pos[r] + (P.v_f0[r] + tid) / P.g_real + 1 : 0;
             M->lim[tid] = lim;
         }
-        if (__syncthreads_or(local_bad)) {                 // the segment's block ids checked
+        if (__syncthreads_or(local_bad)) {                 // block ids checked, slot rows and queries in
             if (tid == 0) report(P.status, TTKV_STATUS_BLOCK_RANGE);
             bad = true;
         }
@@ -714,8 +733,6 @@ __global__ void __launch_bounds__(NTHR, 1) decode_tc_kernel(const ReadParams P, 
             __syncthreads();
             continue;
         }
-        if (tid < 2 * TM && (tid >> 7) < n_tiles) fill_rows(tid >> 7, tid & 127);   // tiles 0 and 1
-        __syncthreads();
         issue_cf(0);
         issue_kv(0);
         if (tid == RP_TID && T.rope_smem) issue_rp(0);
