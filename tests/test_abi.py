@@ -67,3 +67,31 @@ def test_workspace_sizes_are_host_computable():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(ImportError, match="no CPU or Triton fallback"):
         _lib.load(tmp_path / "libttkv_sm100.so")
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """Every struct the ctypes binding declares has the C header's size and field offsets (a C
+    program built from include/ttkv_b200.h prints them)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"ttkv_layout_t": _lib.Layout, "ttkv_cache_t": _lib.Cache, "ttkv_batch_t": _lib.Batch,
+               "ttkv_rope_t": _lib.Rope, "ttkv_peers_t": _lib.Peers}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ttkv_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c99", f"-I{HEADER.parent}", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l.strip()}
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
