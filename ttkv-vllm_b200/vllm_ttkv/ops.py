@@ -268,17 +268,27 @@ def prefill_cont_paged(lay: TTKLayout, cache: torch.Tensor, block_size: int,
     L = _lib.lib()
     la = lay.abi()
     B = block_table.shape[0]
-    ws_n = L.ttkv_prefill_workspace_bytes(C.byref(la), B, HQ, max_q_len, max_seq_len, head_lo, head_hi)
-    ws = workspace(ws_n, q.device)
     st = status if status is not None else status_word(q.device)
     c_s = _cache_struct(lay, cache, block_size)
     b_s = _batch_struct(block_table, seq_lens, decoders, dec_index, images)
     r_s = _rope_struct(table)
-    _lib.check(L.ttkv_prefill_cont_paged(
-        C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q_start.data_ptr(), q_len.data_ptr(),
-        q.data_ptr(), dtype_code(q), qs, HQ, float(scale), head_lo, head_hi,
-        out.data_ptr(), dtype_code(out), os_, int(max_q_len), int(max_seq_len),
-        ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()))
+
+    def call(ws_ptr, ws_n):
+        return L.ttkv_prefill_cont_paged(
+            C.byref(la), C.byref(c_s), C.byref(b_s), C.byref(r_s), q_start.data_ptr(), q_len.data_ptr(),
+            q.data_ptr(), dtype_code(q), qs, HQ, float(scale), head_lo, head_hi,
+            out.data_ptr(), dtype_code(out), os_, int(max_q_len), int(max_seq_len),
+            ws_ptr, ws_n, st.data_ptr(), _stream())
+
+    # the tensor-core continuation (decoder images given) needs no workspace: call without one
+    # first; a path that needs one answers TTKV_ERR_WORKSPACE before it launches anything, and
+    # only then is the workspace sized (hundreds of MB at 256-query chunks) and the call repeated
+    code = call(None, 0) if images is not None else _lib.ERR_WORKSPACE
+    if code == _lib.ERR_WORKSPACE:
+        ws_n = L.ttkv_prefill_workspace_bytes(C.byref(la), B, HQ, max_q_len, max_seq_len, head_lo, head_hi)
+        ws = workspace(ws_n, q.device)
+        code = call(ws.data_ptr(), ws.numel())
+    _lib.check(code)
     return out
 
 
