@@ -34,3 +34,22 @@ def test_tokens_that_fit_sets_the_rest_aside():
     per = memory.cache_bytes_per_token(lays)
     assert n == (free - taken) // per and n > 3_000_000
     assert memory.tokens_that_fit(lays, 1000, 64, 256, 16384, 24) == 0
+
+
+def test_the_tensor_core_continuation_takes_no_scratch():
+    lays = _layers()
+    bound = memory.step_scratch_bytes(lays, 8, 256, 16384, 24)
+    tc = memory.step_scratch_bytes(lays, 8, 256, 16384, 24, tc_continuation=True)
+    decode_only = memory.step_scratch_bytes(lays, 8, 1, 16384, 24, max_tokens=8 * 256)
+    # the calibrated layers above the continuation kernel's largest rank (130..143) still count
+    # the 8-row plan's workspace, and they set the maximum
+    assert any(l.r1 > memory.TC_CONTINUATION_MAX_R1 for l in lays)
+    assert decode_only < tc <= bound
+    small = [layout_for_config("safe", r) for r in (14, 67, 110, 126)]
+    small_tc = memory.step_scratch_bytes(small, 8, 256, 16384, 24, tc_continuation=True)
+    assert small_tc == memory.step_scratch_bytes(small, 8, 1, 16384, 24, max_tokens=8 * 256)
+    assert small_tc < memory.step_scratch_bytes(small, 8, 256, 16384, 24)
+    assert all(memory.tc_continuation_serves(l, 24) for l in small)
+    assert not memory.tc_continuation_serves(layout_for_config("safe", 130), 24)
+    assert not memory.tc_continuation_serves(layout_for_config("safe", 110), 80)     # G = 10
+    assert not memory.tc_continuation_serves(layout_for_config("safe", 110), 20)     # HQ % H != 0
